@@ -1,0 +1,482 @@
+"""Benchmark of the myelin_b200 hot path (one JSON line on stdout, rank 0).
+
+Workload (default ``alif_bf16``, BASELINE config 3, the shape the north-star
+metric is quoted on): ALIF forward + atan-surrogate backward, T=256, B=128,
+N=4096, bf16 currents ~ N(0.2, 0.6), tau_mem=10 (decay 0.9), tau_adaptation=50
+(rho 0.98), beta=1.8, threshold 1, subtractive reset, checkpoint_size="memory",
+upstream spike gradient ~ N(0, 1). A step is one forward + backward pass through
+the public API (``surrogate_alif_forward`` + autograd) over one batch.
+Other workloads: ``lif_fp32`` (same shape, LIF, fp32, hard reset) and
+``pack_count`` (config 4 shard: Bernoulli(0.05) bool [128, 1024/N, 8192] ->
+packed words + per-neuron int32 counts).
+
+Multi-GPU (torchrun, one process per GPU): every rank runs its own batch shard
+of the same size (weak scaling, no collective on the data path); the value is
+all ranks' neuron-steps divided by the max-over-ranks device time.
+
+``--impl reference`` times the reference algorithm's CPU restatement (the
+oracle, all host threads) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+FALLBACK_HBM_GBS = 6650.0
+
+# ---------------------------------------------------------------------------
+# workload definitions
+# ---------------------------------------------------------------------------
+T_STEPS, BATCH, NEURONS = 256, 128, 4096
+
+# algorithmic bytes per neuron-step (from the API's I/O; DESIGN.md derives them)
+#   forward : read x, write dense spikes, write fp32 checkpoints (s states / 16 steps)
+#   backward: read x, read grad_spikes, write grad_x, read checkpoints
+ALGO_BYTES = {
+    "alif_bf16": {"fwd": 2 + 2 + 4 * 2 / 16, "bwd": 2 + 2 + 2 + 4 * 2 / 16},
+    "lif_fp32": {"fwd": 4 + 4 + 4 * 1 / 16, "bwd": 4 + 4 + 4 + 4 * 1 / 16},
+}
+
+
+def load_peak_hbm() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic(name: str) -> float | None:
+    """DRAM bytes per launch from a committed ncu summary, if one exists."""
+
+    path = ROOT / "profiles" / f"{name}.json"
+    if not path.exists():
+        return None
+    try:
+        return float(json.loads(path.read_text())["dram_bytes_per_launch"])
+    except (KeyError, ValueError):
+        return None
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region (NVML reads only)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {
+        "hw_slowdown": 0x0000000000000008,
+        "sw_thermal_slowdown": 0x0000000000000020,
+        "hw_thermal_slowdown": 0x0000000000000040,
+        "sw_power_cap": 0x0000000000000004,
+        "hw_power_brake_slowdown": 0x0000000000000080,
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.005) -> None:
+        self.samples: list[tuple[float, int, int]] = []
+        self.period = period_s
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._handle = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+        except Exception:  # NVML missing: report no clocks rather than fail the bench
+            self._nvml = None
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def _run(self) -> None:
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+                self.samples.append((time.perf_counter(), mhz, reasons))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __exit__(self, *exc) -> None:
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=2)
+
+    def summary(self) -> dict | None:
+        if self._nvml is None or not self.samples:
+            return None
+        mhz = [s[1] for s in self.samples]
+        reasons = set()
+        for _, _, r in self.samples:
+            for name, bit in self.REASONS.items():
+                if r & bit:
+                    reasons.add(name)
+        return {"sm_mhz": float(statistics.median(mhz)), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(mhz)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def scan_workload(name: str, rank: int):
+    import myelin_b200 as mb
+
+    gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    shape = (T_STEPS, BATCH, NEURONS)
+    if name == "alif_bf16":
+        dtype = torch.bfloat16
+        x = (torch.randn(shape, generator=gen, device="cuda") * 0.6 + 0.2).to(dtype)
+        gs = torch.randn(shape, generator=gen, device="cuda").to(dtype)
+        params = mb.ALIFParams(tau_mem=10.0, tau_adaptation=50.0, threshold=1.0, reset=0.0,
+                               beta=1.8)
+        zeros = torch.zeros((BATCH, NEURONS), dtype=dtype, device="cuda")
+
+        def forward(xin):
+            state, spikes = mb.surrogate_alif_forward(
+                xin, mb.ALIFState(zeros, zeros), params, surrogate="atan",
+                checkpoint_size="memory", reset_mode="subtract")
+            return spikes
+    else:
+        dtype = torch.float32
+        x = torch.randn(shape, generator=gen, device="cuda") * 0.5 + 0.3
+        gs = torch.randn(shape, generator=gen, device="cuda")
+        params = mb.LIFParams(tau_mem=10.0, threshold=1.0, reset=0.0)
+        zeros = torch.zeros((BATCH, NEURONS), dtype=dtype, device="cuda")
+
+        def forward(xin):
+            state, spikes = mb.surrogate_lif_forward(xin, mb.LIFState(zeros), params,
+                                                     surrogate="atan", checkpoint_size="memory")
+            return spikes
+    return x, gs, forward
+
+
+def run_gpu(args) -> None:
+    world, rank, local = dist_setup(args.gpus)
+    from myelin_b200 import _native as nat
+
+    name = args.workload
+    if name == "pack_count":
+        return run_pack_count(args, world, rank, local)
+    x, gs, forward = scan_workload(name, rank)
+    x.requires_grad_(True)
+    stream = torch.cuda.current_stream()
+    units = T_STEPS * BATCH * NEURONS  # neuron-steps per rank per step
+
+    def step(xin, g):
+        spikes = forward(xin)
+        (gx,) = torch.autograd.grad(spikes, xin, g)
+        return gx
+
+    for _ in range(args.warmup):
+        step(x, gs)
+    torch.cuda.synchronize()
+
+    # device-resident throughput, with per-kernel events on the launching stream
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
+        start.record(stream)
+        for k in range(args.steps):
+            e0, e1, e2 = ev[k]
+            e0.record(stream)
+            spikes = forward(x)
+            e1.record(stream)
+            torch.autograd.grad(spikes, x, gs)
+            e2.record(stream)
+        stop.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+    total_ms = max_over_ranks(start.elapsed_time(stop), world)
+    fwd_ms = statistics.mean(a.elapsed_time(b) for a, b, _ in ev)
+    bwd_ms = statistics.mean(b.elapsed_time(c) for _, b, c in ev)
+    ms_per_step = total_ms / args.steps
+    value = units * world / (ms_per_step / 1e3)
+    status = nat.device_status(clear=True)
+
+    # end to end through the public API with host buffers
+    pinned_x = x.detach().cpu().pin_memory()
+    pinned_g = gs.cpu().pin_memory()
+    out_host = torch.empty(x.shape, dtype=x.dtype).pin_memory()
+    e2e_steps = max(1, min(args.steps, 20))
+    for _ in range(2):
+        xd = pinned_x.to("cuda", non_blocking=True).requires_grad_(True)
+        out_host.copy_(step(xd, pinned_g.to("cuda", non_blocking=True)), non_blocking=True)
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    s2, t2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record(stream)
+    for _ in range(e2e_steps):
+        xd = pinned_x.to("cuda", non_blocking=True).requires_grad_(True)
+        gd = pinned_g.to("cuda", non_blocking=True)
+        out_host.copy_(step(xd, gd), non_blocking=True)
+    t2.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(s2.elapsed_time(t2), world) / e2e_steps
+    elt = x.element_size()
+
+    peak, peak_kind = load_peak_hbm()
+    bytes_fwd = ALGO_BYTES[name]["fwd"] * units
+    bytes_bwd = ALGO_BYTES[name]["bwd"] * units
+
+    def roof(bytes_per_launch: float, ms: float, profile: str) -> dict:
+        achieved = bytes_per_launch / (ms / 1e3) / 1e9
+        return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                "traffic": profile_traffic(profile),
+                "algorithmic_bytes": int(bytes_per_launch), "avg_launch_ms": round(ms, 4)}
+
+    result = {
+        "metric": "LIF/ALIF fwd+bwd neuron-timesteps/s",
+        "value": value,
+        "unit": "neuron-steps/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_per_step,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16" if name == "alif_bf16" else "f32",
+        "data": "synthetic (seeded on device; shapes/distributions of BASELINE config 3)",
+        "config": {
+            "workload": name + (" (BASELINE config 3: ALIF fwd + atan bwd, checkpoint_size=memory,"
+                                " subtractive reset)" if name == "alif_bf16" else
+                                " (LIF fwd + atan bwd at the config-3 shape)"),
+            "T": T_STEPS, "B_per_gpu": BATCH, "N": NEURONS, "global_batch": BATCH * world,
+            "parallelism": f"dp{world} (batch-sharded, no data-path collective)",
+            "l2": "inputs larger than L2 (x and grad_spikes are T*B*N*elt = "
+                  f"{units * elt / 1e6:.0f} MB each), no flush",
+        },
+        "roofline": roof(bytes_bwd, bwd_ms, f"scan_bwd_{name}"),
+        "roofline_fwd": roof(bytes_fwd, fwd_ms, f"scan_fwd_{name}"),
+        "e2e": {"value": units * world / (e2e_ms / 1e3), "unit": "neuron-steps/s",
+                "h2d_bytes_per_step": 2 * units * elt, "d2h_bytes_per_step": units * elt,
+                "ms_per_step": e2e_ms},
+        "gpu_launches": 2 * args.steps,
+        "device_status": status,
+    }
+    clk = clocks.summary()
+    if clk is not None:
+        result["clocks"] = clk
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(name, seconds=args.cpu_seconds)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def run_pack_count(args, world, rank, local) -> None:
+    """BASELINE config 4 shard: pack [128, 1024/world, 8192] bool spikes + int32 column counts."""
+
+    import myelin_b200 as mb
+    from myelin_b200 import _native as nat
+
+    T, B, N = 128, 1024 // world, 8192
+    gen = torch.Generator(device="cuda").manual_seed(77 + rank)
+    spikes = torch.rand((T, B, N), generator=gen, device="cuda") < 0.05
+    stream = torch.cuda.current_stream()
+
+    def step():
+        packed = mb.pack_spikes(spikes)
+        mb.packed_spike_counts_over_leading_dims(packed, dtype=torch.int32)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    start.record(stream)
+    for _ in range(args.steps):
+        step()
+    stop.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(start.elapsed_time(stop), world) / args.steps
+    units = T * B * N
+    peak, peak_kind = load_peak_hbm()
+    algo = units * (1 + 0.125) + units * 0.125  # read bool, write words, re-read words
+    achieved = algo / (ms / 1e3) / 1e9
+    result = {
+        "metric": "packed spikes/s (pack + per-neuron count)", "value": units * world / (ms / 1e3),
+        "unit": "spikes/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "u8", "data": "synthetic Bernoulli(0.05)",
+        "config": {"workload": "pack_count (BASELINE config 4 shard)", "T": T, "B_per_gpu": B, "N": N},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None},
+        "gpu_launches": 3 * args.steps, "device_status": nat.device_status(clear=True),
+    }
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# CPU arms (oracle = CPU restatement of the reference algorithm)
+# ---------------------------------------------------------------------------
+def _oracle_sample(name: str, rows: int):
+    from oracle import oracle
+
+    rng = np.random.default_rng(99)
+    shape = (T_STEPS, rows, NEURONS)
+    if name == "alif_bf16":
+        x = torch.from_numpy(rng.normal(0.2, 0.6, shape).astype(np.float32)).to(torch.bfloat16)
+        x = x.float().numpy()
+        gs = torch.from_numpy(rng.normal(0, 1, shape).astype(np.float32)).to(torch.bfloat16)
+        gs = gs.float().numpy()
+        kw = dict(neuron=oracle.ALIF, reset_mode=oracle.SUBTRACT, decay=np.float32(0.9),
+                  threshold=np.float32(1.0), reset=np.float32(0.0),
+                  adapt_decay=np.float32(1 - 1 / 50), beta=np.float32(1.8))
+    else:
+        x = rng.normal(0.3, 0.5, shape).astype(np.float32)
+        gs = rng.normal(0, 1, shape).astype(np.float32)
+        kw = dict(neuron=oracle.LIF, decay=np.float32(0.9), threshold=np.float32(1.0),
+                  reset=np.float32(0.0))
+    z = np.zeros((rows, NEURONS), np.float32)
+
+    def step():
+        oracle.scan_forward(x, z, z, **kw)
+        oracle.scan_backward(x, z, z, grad_spikes=gs, surrogate="atan", slope=10.0, **kw)
+
+    return step, T_STEPS * rows * NEURONS, oracle.num_threads()
+
+
+def cpu_baseline(name: str, seconds: float = 10.0) -> dict:
+    rows = 4
+    step, units, threads = _oracle_sample(name, rows)
+    step()  # warm
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        step()
+        n += 1
+    elapsed = time.perf_counter() - t0
+    return {"value": units * n / elapsed, "unit": "neuron-steps/s", "cores": threads,
+            "kind": "port",
+            "sample": f"{name}: T={T_STEPS}, B={rows} of {BATCH}, N={NEURONS}; {n} fwd+bwd passes "
+                      f"in {elapsed:.1f} s (C restatement, OpenMP, {threads} threads)"}
+
+
+def run_reference(args) -> None:
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    name = args.workload if args.workload != "pack_count" else "alif_bf16"
+    rows = 4
+    step, units, threads = _oracle_sample(name, rows)
+    for _ in range(args.warmup):
+        step()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    ms = 1e3 * sum(times) / len(times)
+    value = units / (ms / 1e3)
+    result = {
+        "impl": "reference",
+        "metric": "LIF/ALIF fwd+bwd neuron-timesteps/s", "value": value, "unit": "neuron-steps/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16" if name == "alif_bf16" else "f32", "data": "synthetic",
+        "config": {"workload": name, "T": T_STEPS, "B_per_gpu": BATCH, "N": NEURONS,
+                   "sample_rows": rows},
+        "cpu_baseline": {"value": value, "unit": "neuron-steps/s", "cores": threads,
+                         "kind": "port",
+                         "sample": f"each step: T={T_STEPS}, B={rows} of {BATCH}, N={NEURONS}, "
+                                   "fwd+bwd of the C restatement (OpenMP, all host threads)"},
+        "e2e": {"value": value, "unit": "neuron-steps/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(result), flush=True)
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__,
+                                     formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=50)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", choices=("mine", "reference"), default="mine")
+    parser.add_argument("--workload", choices=("alif_bf16", "lif_fp32", "pack_count"),
+                        default="alif_bf16")
+    parser.add_argument("--cpu-seconds", type=float, default=10.0)
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    sys.path.insert(0, str(ROOT))
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

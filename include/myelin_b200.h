@@ -1,0 +1,180 @@
+/*
+ * myelin_b200 C ABI — hand-written sm_100a kernels for the spiking-neuron hot
+ * path of djsaunde/myelin: the fused-time LIF/ALIF membrane scan with its
+ * reverse-time surrogate backward, and bit-packed spike pack/unpack/count.
+ *
+ * Conventions (every entry point):
+ *   - Plain C: device pointers, sizes, scalars, and a cudaStream_t passed as
+ *     `void*` (NULL = legacy default stream). No torch types.
+ *   - Tensors are dense, C-contiguous, time-major [T, B, N] (state [B, N]),
+ *     exactly the layout of the reference's Python API.
+ *   - Return 0 on success; non-zero on error, with a message available from
+ *     mb_last_error() (thread-local). Launch is asynchronous on `stream`.
+ *   - Stateless and reentrant from any host thread; no allocation.
+ *
+ * The reference has no FFI: its boundary is a set of Python functions that
+ * launch Triton kernels. Each entry point below cites the reference function
+ * (path inside the reference project, file:line) whose work it replaces.
+ */
+#ifndef MYELIN_B200_H
+#define MYELIN_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types of I/O tensors. */
+enum mb_dtype {
+  MB_F32 = 0,
+  MB_BF16 = 1,
+  MB_F16 = 2,
+  MB_F64 = 3,
+  MB_U8 = 4,  /* bool / uint8 / int8: nonzero byte = spike */
+  MB_I16 = 5,
+  MB_I32 = 6,
+  MB_I64 = 7
+};
+
+/* Neuron models on the scan path. */
+enum mb_neuron { MB_LIF = 0, MB_ALIF = 1 };
+
+/* Reset rule after a spike: HARD sets the membrane to `reset`
+ * (src/myelin/neurons.py:113, functional.py:143); SUBTRACT removes the
+ * (adaptive) threshold, m <- p - theta (extension, not in the reference). */
+enum mb_reset { MB_RESET_HARD = 0, MB_RESET_SUBTRACT = 1 };
+
+/* Surrogate derivative ids, numbered as src/myelin/triton/lif.py:356-370.
+ * MB_SURR_NONE gives the exact gradient of the hard (non-surrogate) forward,
+ * used by the plain lif_forward/alif_forward backward. */
+enum mb_surrogate {
+  MB_SURR_SIGMOID = 0,
+  MB_SURR_FAST_SIGMOID = 1,
+  MB_SURR_ATAN = 2,
+  MB_SURR_TRIANGULAR = 3,
+  MB_SURR_SUPERSPIKE = 4,
+  MB_SURR_MULTI_GAUSSIAN = 5,
+  MB_SURR_NONE = 6
+};
+
+/* Replay chunk (time steps) the backward uses: the forward writes one fp32
+ * checkpoint of the state every MB_SCAN_CHUNK steps, the backward replays a
+ * chunk in registers from it and walks it in reverse. */
+#define MB_SCAN_CHUNK 16
+
+/* Last error message of the calling host thread ("" if none). */
+const char* mb_last_error(void);
+
+/* Library version string. */
+const char* mb_version(void);
+
+/* Device status of the scan kernels on the current device: 0 = ok, 1 = a
+ * bounded wait for an asynchronous copy ran out (the kernel stopped early and
+ * its outputs are incomplete). Synchronises the device. `clear` != 0 resets
+ * the status to 0 after reading it. Returns -1 if the status can't be read.
+ * No reference counterpart (the reference's Triton kernels never wait). */
+int mb_device_status(int clear);
+
+/* Number of chunk checkpoints for T steps: ceil(T / MB_SCAN_CHUNK). */
+int64_t mb_scan_num_checkpoints(int64_t T);
+
+/*
+ * Fused-time forward scan over x[T,B,N] for LIF or ALIF neurons.
+ *   p_t = m_{t-1} * decay + x_t            (two roundings, no FMA)
+ *   theta_t = threshold [+ beta * a_{t-1}]  (ALIF)
+ *   s_t = p_t >= theta_t
+ *   m_t = s_t ? reset : p_t   (HARD)   |  s_t ? p_t - theta_t : p_t  (SUBTRACT)
+ *   a_t = a_{t-1} * adapt_decay + s_t       (ALIF)
+ * The membrane/adaptation are carried in fp32 whatever `dtype` is.
+ * Inputs : x [T,B,N] (dtype), v0 [B,N] (dtype), a0 [B,N] (dtype, ALIF only).
+ * Outputs (each may be NULL):
+ *   vT, aT        final state [B,N] (dtype)
+ *   spikes        dense 0/1 [T,B,N] (dtype)
+ *   packed        int32 words [T,B,ceil(N/32)], bit j of word w = neuron 32w+j
+ *   rates         spike count / T [B,N] (dtype)
+ *   ckpt_v/ckpt_a fp32 state at the start of every MB_SCAN_CHUNK-step chunk,
+ *                 [mb_scan_num_checkpoints(T), B, N], consumed by the backward.
+ * Replaces: kernels.lif_forward (src/myelin/kernels.py:52) -> triton/lif.py:16-95;
+ *   kernels.lif_forward_packed_spikes (kernels.py:96) -> triton/lif.py:98-192;
+ *   kernels.alif_forward (kernels.py:159) -> triton/generated.py:1159-1189;
+ *   surrogate forward of kernels.surrogate_lif_forward (kernels.py:249)
+ *   -> triton/lif.py:195-222,373-405; rate forward (triton/lif.py:823-889).
+ */
+int mb_scan_forward(int neuron, int dtype, const void* x, const void* v0, const void* a0,
+                    void* vT, void* aT, void* spikes, int32_t* packed, void* rates,
+                    float* ckpt_v, float* ckpt_a, int64_t T, int64_t B, int64_t N,
+                    float decay, float threshold, float reset, float adapt_decay,
+                    float beta, int reset_mode, void* stream);
+
+/*
+ * Reverse-time surrogate backward of mb_scan_forward. Replays each chunk from
+ * its checkpoint in registers (bit-identical to the forward), then walks it in
+ * reverse:
+ *   d   = slope * surrogate'(slope * (p - theta))
+ *   HARD:     Gs = gs + gm*(reset - p) [+ ga];  gp = gm*(1 - s) + Gs*d
+ *   SUBTRACT: Gs = gs - gm*theta       [+ ga];  gp = gm + Gs*d
+ *   ALIF: ga <- ga*adapt_decay - beta*(Gs*d [+ gm*s for SUBTRACT])
+ *   grad_x_t = gp;  gm <- gp * decay
+ * gs = grad_spikes[t] (if given) + grad_rates / T (if given).
+ * Inputs : x, ckpt_v, ckpt_a (ALIF) from the forward; grad_spikes [T,B,N],
+ *          grad_rates [B,N], grad_vT [B,N], grad_aT [B,N] (dtype; each may be NULL).
+ * Outputs: grad_x [T,B,N] (dtype, required), grad_v0 / grad_a0 [B,N] (nullable).
+ * Replaces: triton/lif.py:252-336,408-551 (surrogate LIF backward) and the
+ *   torch autograd through functional.surrogate_alif_unroll (functional.py:149-189).
+ */
+int mb_scan_backward(int neuron, int dtype, const void* x, const float* ckpt_v,
+                     const float* ckpt_a, const void* grad_spikes, const void* grad_rates,
+                     const void* grad_vT, const void* grad_aT, void* grad_x, void* grad_v0,
+                     void* grad_a0, int64_t T, int64_t B, int64_t N, float decay,
+                     float threshold, float reset, float adapt_decay, float beta,
+                     int reset_mode, int surrogate, float slope, void* stream);
+
+/*
+ * Pack spikes[rows, n] (any dtype; nonzero = spike, -0.0 counts as zero) into
+ * int32 words[rows, ceil(n/32)], LSB-first, zero padding bits.
+ * Replaces: packing.pack_spikes (src/myelin/packing.py:45-71) and
+ *   triton/packing.py:20-41,100-131.
+ */
+int mb_pack_spikes(int dtype, const void* spikes, int32_t* words, int64_t rows, int64_t n,
+                   void* stream);
+
+/*
+ * Unpack words[rows, ceil(n/32)] into out[rows, n] of `dtype` (0/1 values).
+ * Replaces: packing.unpack_spikes (packing.py:74-81), triton/packing.py:44-66,134-175.
+ */
+int mb_unpack_spikes(const int32_t* words, int dtype, void* out, int64_t rows, int64_t n,
+                     void* stream);
+
+/*
+ * Per-row spike counts (reduction over the last dimension, padding bits
+ * ignored): counts[rows] int64.
+ * Replaces: packing._packed_spike_row_counts (packing.py:165-206),
+ *   triton/packing.py:69-91,178-225.
+ */
+int mb_count_rows(const int32_t* words, int64_t rows, int64_t n, int64_t* counts,
+                  void* stream);
+
+/*
+ * Workspace (bytes, device memory) that mb_count_columns needs for
+ * words[rows, ceil(n/32)]: one int32 partial count per (row slice, neuron).
+ */
+int64_t mb_count_columns_workspace_bytes(int64_t rows, int64_t n);
+
+/*
+ * Per-neuron spike counts summed over all leading rows (the dim=(0..nd-2)
+ * reduction): counts[n]. Writes int64 to counts64 and/or int32 to counts32
+ * (either may be NULL). Deterministic (integer arithmetic, fixed slice order).
+ * `workspace` must hold mb_count_columns_workspace_bytes(rows, n) bytes,
+ * 4-byte aligned; it is overwritten.
+ * Replaces: packing._packed_spike_counts_over_leading_dims (packing.py:209-216).
+ */
+int mb_count_columns(const int32_t* words, int64_t rows, int64_t n, int64_t* counts64,
+                     int32_t* counts32, void* workspace, int64_t workspace_bytes,
+                     void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MYELIN_B200_H */

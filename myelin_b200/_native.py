@@ -1,0 +1,242 @@
+"""ctypes binding of the myelin_b200 C ABI (``include/myelin_b200.h``).
+
+This module is the only place that talks to ``libmyelin_b200.so``. It loads
+the in-tree library (built by ``python -m myelin_b200.build``), declares the
+C signatures, and offers thin helpers that pass torch tensors as raw device
+pointers on the current CUDA stream. There is no fallback: if the library is
+missing, or a tensor is not on a CUDA device, the call raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libmyelin_b200.so"
+
+# enum mb_dtype
+MB_F32, MB_BF16, MB_F16, MB_F64, MB_U8, MB_I16, MB_I32, MB_I64 = range(8)
+# enum mb_neuron / mb_reset
+MB_LIF, MB_ALIF = 0, 1
+MB_RESET_HARD, MB_RESET_SUBTRACT = 0, 1
+MB_SURR_NONE = 6
+SCAN_CHUNK = 16  # MB_SCAN_CHUNK
+
+_DTYPE_CODES: dict[torch.dtype, int] = {
+    torch.float32: MB_F32,
+    torch.bfloat16: MB_BF16,
+    torch.float16: MB_F16,
+    torch.float64: MB_F64,
+    torch.bool: MB_U8,
+    torch.uint8: MB_U8,
+    torch.int8: MB_U8,
+    torch.int16: MB_I16,
+    torch.int32: MB_I32,
+    torch.int64: MB_I64,
+}
+SCAN_DTYPES = (torch.float32, torch.bfloat16, torch.float16)
+
+_lib: ctypes.CDLL | None = None
+_lock = threading.Lock()
+
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_int = ctypes.c_int
+_f = ctypes.c_float
+
+_SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "mb_last_error": (ctypes.c_char_p, []),
+    "mb_version": (ctypes.c_char_p, []),
+    "mb_device_status": (_int, [_int]),
+    "mb_scan_num_checkpoints": (_i64, [_i64]),
+    "mb_scan_forward": (
+        _int,
+        [_int, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+         _i64, _i64, _i64, _f, _f, _f, _f, _f, _int, _vp],
+    ),
+    "mb_scan_backward": (
+        _int,
+        [_int, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+         _i64, _i64, _i64, _f, _f, _f, _f, _f, _int, _int, _f, _vp],
+    ),
+    "mb_pack_spikes": (_int, [_int, _vp, _vp, _i64, _i64, _vp]),
+    "mb_unpack_spikes": (_int, [_vp, _int, _vp, _i64, _i64, _vp]),
+    "mb_count_rows": (_int, [_vp, _i64, _i64, _vp, _vp]),
+    "mb_count_columns_workspace_bytes": (_i64, [_i64, _i64]),
+    "mb_count_columns": (_int, [_vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp]),
+}
+
+EXPORTED_SYMBOLS = tuple(_SIGNATURES)
+
+
+def lib() -> ctypes.CDLL:
+    """Load (once) and return the native library; raise if it is not built."""
+
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise RuntimeError(
+                    f"myelin_b200 native library not found at {LIB_PATH}; build it with "
+                    "`python -m myelin_b200.build` (nvcc, sm_100a)"
+                )
+            handle = ctypes.CDLL(str(LIB_PATH))
+            for name, (restype, argtypes) in _SIGNATURES.items():
+                fn = getattr(handle, name)
+                fn.restype = restype
+                fn.argtypes = argtypes
+            _lib = handle
+    return _lib
+
+
+def version() -> str:
+    return lib().mb_version().decode()
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODES[dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype for myelin_b200 kernels: {dtype}") from None
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        message = lib().mb_last_error().decode() or "unknown error"
+        raise RuntimeError(f"{what} failed: {message}")
+
+
+def require_cuda(tensor: torch.Tensor, what: str = "inputs") -> None:
+    if not tensor.is_cuda:
+        raise ValueError(
+            f"myelin_b200 runs on CUDA devices only; {what} is on {tensor.device}. "
+            "Move the tensors to a CUDA device (there is no CPU fallback)."
+        )
+
+
+def device_status(clear: bool = True) -> int:
+    """Return (and by default clear) the scan kernels' device status word."""
+
+    return int(lib().mb_device_status(1 if clear else 0))
+
+
+def scan_forward(
+    *,
+    neuron: int,
+    x: torch.Tensor,
+    v0: torch.Tensor,
+    a0: torch.Tensor | None,
+    vT: torch.Tensor | None,
+    aT: torch.Tensor | None,
+    spikes: torch.Tensor | None,
+    packed: torch.Tensor | None,
+    rates: torch.Tensor | None,
+    ckpt_v: torch.Tensor | None,
+    ckpt_a: torch.Tensor | None,
+    decay: float,
+    threshold: float,
+    reset: float,
+    adapt_decay: float,
+    beta: float,
+    reset_mode: int,
+) -> None:
+    T, B, N = x.shape
+    with torch.cuda.device(x.device):
+        status = lib().mb_scan_forward(
+            neuron, dtype_code(x.dtype), ptr(x), ptr(v0), ptr(a0), ptr(vT), ptr(aT),
+            ptr(spikes), ptr(packed), ptr(rates), ptr(ckpt_v), ptr(ckpt_a),
+            T, B, N, decay, threshold, reset, adapt_decay, beta, reset_mode,
+            stream_handle(x.device),
+        )
+    check(status, "mb_scan_forward")
+
+
+def scan_backward(
+    *,
+    neuron: int,
+    x: torch.Tensor,
+    ckpt_v: torch.Tensor,
+    ckpt_a: torch.Tensor | None,
+    grad_spikes: torch.Tensor | None,
+    grad_rates: torch.Tensor | None,
+    grad_vT: torch.Tensor | None,
+    grad_aT: torch.Tensor | None,
+    grad_x: torch.Tensor,
+    grad_v0: torch.Tensor | None,
+    grad_a0: torch.Tensor | None,
+    decay: float,
+    threshold: float,
+    reset: float,
+    adapt_decay: float,
+    beta: float,
+    reset_mode: int,
+    surrogate: int,
+    slope: float,
+) -> None:
+    T, B, N = x.shape
+    with torch.cuda.device(x.device):
+        status = lib().mb_scan_backward(
+            neuron, dtype_code(x.dtype), ptr(x), ptr(ckpt_v), ptr(ckpt_a),
+            ptr(grad_spikes), ptr(grad_rates), ptr(grad_vT), ptr(grad_aT),
+            ptr(grad_x), ptr(grad_v0), ptr(grad_a0),
+            T, B, N, decay, threshold, reset, adapt_decay, beta, reset_mode,
+            surrogate, slope, stream_handle(x.device),
+        )
+    check(status, "mb_scan_backward")
+
+
+def num_checkpoints(T: int) -> int:
+    return int(lib().mb_scan_num_checkpoints(T))
+
+
+def pack(spikes: torch.Tensor, words: torch.Tensor, rows: int, n: int) -> None:
+    with torch.cuda.device(spikes.device):
+        status = lib().mb_pack_spikes(
+            dtype_code(spikes.dtype), ptr(spikes), ptr(words), rows, n,
+            stream_handle(spikes.device),
+        )
+    check(status, "mb_pack_spikes")
+
+
+def unpack(words: torch.Tensor, out: torch.Tensor, rows: int, n: int) -> None:
+    with torch.cuda.device(words.device):
+        status = lib().mb_unpack_spikes(
+            ptr(words), dtype_code(out.dtype), ptr(out), rows, n, stream_handle(words.device)
+        )
+    check(status, "mb_unpack_spikes")
+
+
+def count_rows(words: torch.Tensor, counts: torch.Tensor, rows: int, n: int) -> None:
+    with torch.cuda.device(words.device):
+        status = lib().mb_count_rows(ptr(words), rows, n, ptr(counts), stream_handle(words.device))
+    check(status, "mb_count_rows")
+
+
+def count_columns(
+    words: torch.Tensor,
+    rows: int,
+    n: int,
+    counts64: torch.Tensor | None,
+    counts32: torch.Tensor | None,
+) -> None:
+    need = int(lib().mb_count_columns_workspace_bytes(rows, n))
+    workspace = torch.empty(max(need, 4), dtype=torch.uint8, device=words.device)
+    with torch.cuda.device(words.device):
+        status = lib().mb_count_columns(
+            ptr(words), rows, n, ptr(counts64), ptr(counts32), ptr(workspace), need,
+            stream_handle(words.device),
+        )
+    check(status, "mb_count_columns")

@@ -1,0 +1,100 @@
+// Bulk asynchronous global->shared copies (the TMA engine's 1-D form) tracked
+// by shared-memory mbarriers, for sm_100a. Every wait is bounded: a wait that
+// runs out records an error code in a device status word that the host reads
+// with mb_device_status(), and returns false instead of spinning forever.
+#pragma once
+
+#include "common.cuh"
+
+namespace mb {
+
+// Device status word of this translation unit: 0 = ok. Set (first error
+// wins) by kernels whose bounded waits ran out; read and cleared by the host
+// through mb_device_status().
+static __device__ int g_device_status = 0;
+
+enum DeviceStatus : int {
+  kStatusOk = 0,
+  kStatusWaitTimeout = 1,
+};
+
+__device__ __forceinline__ void record_status(int code) { atomicCAS(&g_device_status, 0, code); }
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+
+// Make initialised barriers visible to the async proxy (the copy engine).
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Order this thread's earlier generic-proxy shared-memory accesses before
+// later async-proxy accesses (a buffer that was read is about to be refilled).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// One contiguous copy of `bytes` (multiple of 16, both addresses 16-byte
+// aligned) from global memory into this CTA's shared memory; completion is
+// signalled on `bar` as transaction bytes.
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes,
+                                              uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n"
+      "  .reg .pred p;\n"
+      "  mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "  selp.u32 %0, 1, 0, p;\n"
+      "}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Upper bound on try_wait polls (each poll may itself suspend the thread for a
+// bounded, hardware-defined time). Far above any legitimate wait here: a chunk
+// copy is tens of kilobytes.
+constexpr uint32_t kMaxWaitPolls = 1u << 22;
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kMaxWaitPolls; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+  }
+  record_status(kStatusWaitTimeout);
+  return false;
+}
+
+// Host side: read (and optionally clear) this translation unit's status word.
+// Synchronises with the device.
+static inline int read_device_status(bool clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v != 0) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return v;
+}
+
+}  // namespace mb

@@ -1,0 +1,396 @@
+// Bit-packed spike words: pack, unpack, per-row and per-neuron counts.
+//
+// Word format (src/myelin/packing.py:45-71): spikes[..., n] -> int32 words
+// [..., ceil(n / 32)], bit j of word w holds neuron 32*w + j (LSB first),
+// padding bits are zero, bit 31 makes the word negative.
+//
+// All kernels are HBM-streaming integer work. When the last dimension is a
+// multiple of 32 and the base pointer is 16-byte aligned, every thread moves
+// exactly 16 bytes per access (fully coalesced); other shapes take a scalar
+// path with the same results.
+#include "common.cuh"
+
+namespace mb {
+
+// ---------------------------------------------------------------------------
+// Nonzero test on the raw bits of one element ("spikes != 0" in torch: -0.0
+// is zero, NaN is nonzero).
+// ---------------------------------------------------------------------------
+template <int DT>
+struct Raw;
+template <> struct Raw<MB_U8>   { using U = uint8_t;  static __device__ __forceinline__ bool nz(U v) { return v != 0; } };
+template <> struct Raw<MB_I16>  { using U = uint16_t; static __device__ __forceinline__ bool nz(U v) { return v != 0; } };
+template <> struct Raw<MB_F16>  { using U = uint16_t; static __device__ __forceinline__ bool nz(U v) { return (v & 0x7fffu) != 0; } };
+template <> struct Raw<MB_BF16> { using U = uint16_t; static __device__ __forceinline__ bool nz(U v) { return (v & 0x7fffu) != 0; } };
+template <> struct Raw<MB_I32>  { using U = uint32_t; static __device__ __forceinline__ bool nz(U v) { return v != 0; } };
+template <> struct Raw<MB_F32>  { using U = uint32_t; static __device__ __forceinline__ bool nz(U v) { return (v & 0x7fffffffu) != 0; } };
+template <> struct Raw<MB_I64>  { using U = uint64_t; static __device__ __forceinline__ bool nz(U v) { return v != 0; } };
+template <> struct Raw<MB_F64>  { using U = uint64_t; static __device__ __forceinline__ bool nz(U v) { return (v & 0x7fffffffffffffffull) != 0; } };
+
+// The value 1 in each element type, as raw bits.
+template <int DT> __device__ __forceinline__ typename Raw<DT>::U raw_one();
+template <> __device__ __forceinline__ uint8_t raw_one<MB_U8>() { return 1; }
+template <> __device__ __forceinline__ uint16_t raw_one<MB_I16>() { return 1; }
+template <> __device__ __forceinline__ uint16_t raw_one<MB_F16>() { return 0x3c00u; }
+template <> __device__ __forceinline__ uint16_t raw_one<MB_BF16>() { return 0x3f80u; }
+template <> __device__ __forceinline__ uint32_t raw_one<MB_I32>() { return 1u; }
+template <> __device__ __forceinline__ uint32_t raw_one<MB_F32>() { return 0x3f800000u; }
+template <> __device__ __forceinline__ uint64_t raw_one<MB_I64>() { return 1ull; }
+template <> __device__ __forceinline__ uint64_t raw_one<MB_F64>() { return 0x3ff0000000000000ull; }
+
+// ---------------------------------------------------------------------------
+// Pack, vector path: n % 32 == 0, 16-byte aligned. Each thread loads 16 bytes
+// (kEPT elements) and contributes kEPT bits; the kLPW lanes that share one
+// word OR their bits together with shuffles, and the first lane stores it.
+// ---------------------------------------------------------------------------
+template <int DT>
+__global__ void __launch_bounds__(256) pack_vec_kernel(const uint4* __restrict__ in,
+                                                       int32_t* __restrict__ words,
+                                                       int64_t n_vec) {
+  using U = typename Raw<DT>::U;
+  constexpr int kEPT = 16 / sizeof(U);
+  constexpr int kLPW = 32 / kEPT;  // lanes per word
+  const int lane = threadIdx.x & 31;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  // The grid-stride loop keeps whole warps together (n_vec is a multiple of
+  // kLPW and every warp starts on a word boundary), so the shuffles below are
+  // executed by full warps only when all lanes are in range.
+  for (int64_t i0 = int64_t(blockIdx.x) * blockDim.x; i0 < n_vec; i0 += stride) {
+    const int64_t i = i0 + threadIdx.x;
+    uint32_t bits = 0;
+    if (i < n_vec) {
+      const uint4 v = in[i];
+      U el[kEPT];
+      *reinterpret_cast<uint4*>(el) = v;
+      if (DT == MB_U8) {
+        // four bytes at a time: high bit of each byte set iff the byte != 0
+        const uint32_t* w4 = reinterpret_cast<const uint32_t*>(&v);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t h = (((w4[q] & 0x7f7f7f7fu) + 0x7f7f7f7fu) | w4[q]) & 0x80808080u;
+          h >>= 7;
+          h = (h | (h >> 7) | (h >> 14) | (h >> 21)) & 0xfu;
+          bits |= h << (4 * q);
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < kEPT; ++k) bits |= uint32_t(Raw<DT>::nz(el[k])) << k;
+      }
+    }
+    uint32_t word = bits << ((lane % kLPW) * kEPT);
+#pragma unroll
+    for (int off = 1; off < kLPW; off <<= 1) word |= __shfl_xor_sync(0xffffffffu, word, off);
+    if (i < n_vec && (lane % kLPW) == 0) words[i / kLPW] = static_cast<int32_t>(word);
+  }
+}
+
+// Pack, scalar path: one thread per output word.
+template <int DT>
+__global__ void __launch_bounds__(256) pack_scalar_kernel(const typename Raw<DT>::U* __restrict__ in,
+                                                          int32_t* __restrict__ words, int64_t rows,
+                                                          int64_t n, int64_t W) {
+  const int64_t total = rows * W;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t wi = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; wi < total; wi += stride) {
+    const int64_t r = wi / W;
+    const int64_t w = wi - r * W;
+    const int64_t n0 = w * 32;
+    const int cnt = static_cast<int>(imin64(32, n - n0));
+    const typename Raw<DT>::U* src = in + r * n + n0;
+    uint32_t word = 0;
+    for (int k = 0; k < cnt; ++k) word |= uint32_t(Raw<DT>::nz(src[k])) << k;
+    words[wi] = static_cast<int32_t>(word);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Unpack.
+// ---------------------------------------------------------------------------
+template <int DT>
+__global__ void __launch_bounds__(256) unpack_vec_kernel(const uint32_t* __restrict__ words,
+                                                         uint4* __restrict__ out, int64_t n_vec) {
+  using U = typename Raw<DT>::U;
+  constexpr int kEPT = 16 / sizeof(U);
+  constexpr int kLPW = 32 / kEPT;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n_vec; i += stride) {
+    const uint32_t word = words[i / kLPW] >> ((i % kLPW) * kEPT);
+    U el[kEPT];
+#pragma unroll
+    for (int k = 0; k < kEPT; ++k) el[k] = ((word >> k) & 1u) ? raw_one<DT>() : U(0);
+    out[i] = *reinterpret_cast<const uint4*>(el);
+  }
+}
+
+template <int DT>
+__global__ void __launch_bounds__(256) unpack_scalar_kernel(const uint32_t* __restrict__ words,
+                                                            typename Raw<DT>::U* __restrict__ out,
+                                                            int64_t rows, int64_t n, int64_t W) {
+  using U = typename Raw<DT>::U;
+  const int64_t total = rows * n;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t r = i / n;
+    const int64_t c = i - r * n;
+    const uint32_t word = words[r * W + (c >> 5)];
+    out[i] = ((word >> (c & 31)) & 1u) ? raw_one<DT>() : U(0);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Per-row counts: one warp per row, popcount over the row's words with the
+// padding bits of the last word masked off.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) count_rows_kernel(const uint32_t* __restrict__ words,
+                                                         int64_t* __restrict__ counts,
+                                                         int64_t rows, int64_t W,
+                                                         uint32_t last_mask) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t r = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
+    const uint32_t* src = words + r * W;
+    int64_t c = 0;
+    for (int64_t w = lane; w < W; w += 32) {
+      uint32_t v = src[w];
+      if (w == W - 1) v &= last_mask;
+      c += __popc(v);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) c += __shfl_xor_sync(0xffffffffu, c, off);
+    if (lane == 0) counts[r] = c;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Per-neuron counts over all rows (column popcount). Each lane owns one word
+// column; its 32 bit positions are counted in 8 SWAR registers holding four
+// 8-bit counters each (bit k, k+8, k+16, k+24), flushed into 32 int32
+// counters before any 8-bit counter can overflow. The 8 warps of a block take
+// interleaved rows of the same 32 word columns and are reduced through shared
+// memory; every (row slice, neuron) partial is written to the workspace and a
+// second kernel sums the slices.
+// ---------------------------------------------------------------------------
+constexpr int kColWarps = 8;
+
+__global__ void __launch_bounds__(256) count_columns_partial_kernel(
+    const uint32_t* __restrict__ words, int32_t* __restrict__ partial, int64_t rows, int64_t W,
+    int64_t n, int64_t rows_per_slice) {
+  __shared__ int32_t red[kColWarps][32 * 33];
+  const int lane = threadIdx.x & 31;
+  const int wid = threadIdx.x >> 5;
+  const int64_t w = int64_t(blockIdx.x) * 32 + lane;
+  const int64_t r_begin = int64_t(blockIdx.y) * rows_per_slice;
+  const int64_t r_end = imin64(rows, r_begin + rows_per_slice);
+
+  int32_t acc[32];
+#pragma unroll
+  for (int k = 0; k < 32; ++k) acc[k] = 0;
+  uint32_t swar[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) swar[k] = 0;
+  int pending = 0;
+
+  if (w < W) {
+    for (int64_t r = r_begin + wid; r < r_end; r += kColWarps) {
+      const uint32_t v = words[r * W + w];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) swar[k] += (v >> k) & 0x01010101u;
+      if (++pending == 255) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) acc[k + 8 * q] += (swar[k] >> (8 * q)) & 0xffu;
+          swar[k] = 0;
+        }
+        pending = 0;
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acc[k + 8 * q] += (swar[k] >> (8 * q)) & 0xffu;
+  }
+  // padding stride 33 keeps the transposed reads below conflict-free
+#pragma unroll
+  for (int k = 0; k < 32; ++k) red[wid][lane * 33 + k] = acc[k];
+  __syncthreads();
+  // thread t sums neuron (t) of this block's 32*32 = 1024 neurons, 4 per thread
+  for (int j = threadIdx.x; j < 1024; j += blockDim.x) {
+    const int wl = j >> 5;  // word column within block
+    const int bit = j & 31;
+    int32_t s = 0;
+#pragma unroll
+    for (int q = 0; q < kColWarps; ++q) s += red[q][wl * 33 + bit];
+    const int64_t neuron = int64_t(blockIdx.x) * 1024 + j;
+    if (neuron < n) partial[int64_t(blockIdx.y) * n + neuron] = s;
+  }
+}
+
+__global__ void __launch_bounds__(256) count_columns_final_kernel(const int32_t* __restrict__ partial,
+                                                                  int64_t slices, int64_t n,
+                                                                  int64_t* __restrict__ out64,
+                                                                  int32_t* __restrict__ out32) {
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t j = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; j < n; j += stride) {
+    int64_t s = 0;
+    for (int64_t q = 0; q < slices; ++q) s += partial[q * n + j];
+    if (out64) out64[j] = s;
+    if (out32) out32[j] = static_cast<int32_t>(s);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side.
+// ---------------------------------------------------------------------------
+static int grid_for(int64_t work_items, int block = 256) {
+  const int64_t cap = 148 * 32;  // grid-stride loops beyond ~32 blocks per SM
+  int64_t g = ceil_div(work_items, block);
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return static_cast<int>(g);
+}
+
+template <int DT>
+static void launch_pack(const void* spikes, int32_t* words, int64_t rows, int64_t n,
+                        cudaStream_t s) {
+  using U = typename Raw<DT>::U;
+  const int64_t W = ceil_div(n, 32);
+  if (n % 32 == 0 && aligned_to(spikes, 16)) {
+    const int64_t n_vec = rows * n * int64_t(sizeof(U)) / 16;
+    pack_vec_kernel<DT><<<grid_for(n_vec), 256, 0, s>>>(static_cast<const uint4*>(spikes), words,
+                                                        n_vec);
+  } else {
+    pack_scalar_kernel<DT><<<grid_for(rows * W), 256, 0, s>>>(static_cast<const U*>(spikes),
+                                                             words, rows, n, W);
+  }
+}
+
+template <int DT>
+static void launch_unpack(const int32_t* words, void* out, int64_t rows, int64_t n,
+                          cudaStream_t s) {
+  using U = typename Raw<DT>::U;
+  const int64_t W = ceil_div(n, 32);
+  const uint32_t* uw = reinterpret_cast<const uint32_t*>(words);
+  if (n % 32 == 0 && aligned_to(out, 16)) {
+    const int64_t n_vec = rows * n * int64_t(sizeof(U)) / 16;
+    unpack_vec_kernel<DT><<<grid_for(n_vec), 256, 0, s>>>(uw, static_cast<uint4*>(out), n_vec);
+  } else {
+    unpack_scalar_kernel<DT><<<grid_for(rows * n), 256, 0, s>>>(uw, static_cast<U*>(out), rows, n,
+                                                               W);
+  }
+}
+
+#define MB_DISPATCH_DTYPE(dtype, FN, ...)              \
+  switch (dtype) {                                     \
+    case MB_F32: FN<MB_F32>(__VA_ARGS__); break;       \
+    case MB_BF16: FN<MB_BF16>(__VA_ARGS__); break;     \
+    case MB_F16: FN<MB_F16>(__VA_ARGS__); break;       \
+    case MB_F64: FN<MB_F64>(__VA_ARGS__); break;       \
+    case MB_U8: FN<MB_U8>(__VA_ARGS__); break;         \
+    case MB_I16: FN<MB_I16>(__VA_ARGS__); break;       \
+    case MB_I32: FN<MB_I32>(__VA_ARGS__); break;       \
+    default: FN<MB_I64>(__VA_ARGS__); break;           \
+  }
+
+// Row slices for the column count: enough blocks for ~4 per SM, at least
+// 64 rows per slice.
+static int64_t column_slices(int64_t rows, int64_t n) {
+  const int64_t col_blocks = ceil_div(ceil_div(n, 32), 32);
+  int64_t slices = ceil_div(148 * 4, col_blocks);
+  const int64_t max_by_rows = ceil_div(rows, 64);
+  if (slices > max_by_rows) slices = max_by_rows;
+  if (slices < 1) slices = 1;
+  return slices;
+}
+
+int launch_count_columns(const int32_t* words, int64_t rows, int64_t n, int64_t* counts64,
+                         int32_t* counts32, int32_t* workspace, cudaStream_t s) {
+  const int64_t W = ceil_div(n, 32);
+  const int64_t slices = column_slices(rows, n);
+  const int64_t rows_per_slice = ceil_div(rows, slices);
+  dim3 grid(static_cast<unsigned>(ceil_div(W, 32)), static_cast<unsigned>(slices));
+  count_columns_partial_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const uint32_t*>(words),
+                                                    workspace, rows, W, n, rows_per_slice);
+  count_columns_final_kernel<<<grid_for(n), 256, 0, s>>>(workspace, slices, n, counts64, counts32);
+  return 0;
+}
+
+int64_t count_columns_workspace_bytes(int64_t rows, int64_t n) {
+  if (rows <= 0 || n <= 0) return 0;
+  return column_slices(rows, n) * n * int64_t(sizeof(int32_t));
+}
+
+}  // namespace mb
+
+using namespace mb;
+
+static bool valid_io_dtype(int dtype) { return dtype >= MB_F32 && dtype <= MB_I64; }
+
+extern "C" int mb_pack_spikes(int dtype, const void* spikes, int32_t* words, int64_t rows,
+                              int64_t n, void* stream) {
+  clear_error();
+  MB_CHECK_ARG(valid_io_dtype(dtype), "mb_pack_spikes: unknown dtype %d", dtype);
+  MB_CHECK_ARG(rows >= 0 && n > 0, "mb_pack_spikes: cannot pack an empty last dimension");
+  if (rows == 0) return 0;
+  MB_CHECK_ARG(spikes != nullptr && words != nullptr, "mb_pack_spikes: null pointer");
+  cudaStream_t s = as_stream(stream);
+  MB_DISPATCH_DTYPE(dtype, launch_pack, spikes, words, rows, n, s);
+  MB_CHECK_LAUNCH("mb_pack_spikes");
+  return 0;
+}
+
+extern "C" int mb_unpack_spikes(const int32_t* words, int dtype, void* out, int64_t rows,
+                                int64_t n, void* stream) {
+  clear_error();
+  MB_CHECK_ARG(valid_io_dtype(dtype), "mb_unpack_spikes: unknown dtype %d", dtype);
+  MB_CHECK_ARG(rows >= 0 && n > 0, "mb_unpack_spikes: packed.original_shape must have non-empty last dimension");
+  if (rows == 0) return 0;
+  MB_CHECK_ARG(words != nullptr && out != nullptr, "mb_unpack_spikes: null pointer");
+  cudaStream_t s = as_stream(stream);
+  MB_DISPATCH_DTYPE(dtype, launch_unpack, words, out, rows, n, s);
+  MB_CHECK_LAUNCH("mb_unpack_spikes");
+  return 0;
+}
+
+extern "C" int mb_count_rows(const int32_t* words, int64_t rows, int64_t n, int64_t* counts,
+                             void* stream) {
+  clear_error();
+  MB_CHECK_ARG(rows >= 0 && n > 0, "mb_count_rows: packed.original_shape must have non-empty last dimension");
+  if (rows == 0) return 0;
+  MB_CHECK_ARG(words != nullptr && counts != nullptr, "mb_count_rows: null pointer");
+  const int64_t W = ceil_div(n, 32);
+  const uint32_t last_mask = (n % 32 == 0) ? 0xffffffffu : ((1u << (n % 32)) - 1u);
+  count_rows_kernel<<<grid_for(rows * 32), 256, 0, as_stream(stream)>>>(
+      reinterpret_cast<const uint32_t*>(words), counts, rows, W, last_mask);
+  MB_CHECK_LAUNCH("mb_count_rows");
+  return 0;
+}
+
+extern "C" int64_t mb_count_columns_workspace_bytes(int64_t rows, int64_t n) {
+  return count_columns_workspace_bytes(rows, n);
+}
+
+extern "C" int mb_count_columns(const int32_t* words, int64_t rows, int64_t n, int64_t* counts64,
+                                int32_t* counts32, void* workspace, int64_t workspace_bytes,
+                                void* stream) {
+  clear_error();
+  MB_CHECK_ARG(rows >= 0 && n > 0, "mb_count_columns: packed.original_shape must have non-empty last dimension");
+  MB_CHECK_ARG(counts64 != nullptr || counts32 != nullptr, "mb_count_columns: no output");
+  cudaStream_t s = as_stream(stream);
+  if (rows == 0) {
+    if (counts64) cudaMemsetAsync(counts64, 0, n * sizeof(int64_t), s);
+    if (counts32) cudaMemsetAsync(counts32, 0, n * sizeof(int32_t), s);
+    MB_CHECK_LAUNCH("mb_count_columns");
+    return 0;
+  }
+  MB_CHECK_ARG(words != nullptr, "mb_count_columns: null words");
+  const int64_t need = count_columns_workspace_bytes(rows, n);
+  MB_CHECK_ARG(workspace != nullptr && workspace_bytes >= need,
+               "mb_count_columns: workspace of %lld bytes required, got %lld", (long long)need,
+               (long long)workspace_bytes);
+  MB_CHECK_ARG(aligned_to(workspace, 4), "mb_count_columns: workspace misaligned");
+  launch_count_columns(words, rows, n, counts64, counts32, static_cast<int32_t*>(workspace), s);
+  MB_CHECK_LAUNCH("mb_count_columns");
+  return 0;
+}

@@ -1,0 +1,420 @@
+"""Public fused-kernel entry points, signature-compatible with ``myelin.kernels``.
+
+Every function keeps the reference's positional/keyword names and defaults
+(src/myelin/kernels.py:52-865). ``backend`` and the Triton tile arguments
+(``block_size``, ``block_b``, ``block_n``, ``block_f``) are accepted for
+drop-in compatibility; every backend name the reference defines selects the
+same hand-written sm_100a kernels. Tensors must be on a CUDA device: there is
+no CPU fallback.
+
+Extensions over the reference: ``reset_mode="subtract"`` (membrane minus the
+(adaptive) threshold after a spike instead of a hard reset) on the LIF/ALIF
+scans, ``checkpoint_size`` on ``surrogate_alif_forward``, and a backward for
+``surrogate_alif_forward`` / ``alif_forward`` on the GPU.
+"""
+
+from __future__ import annotations
+
+from typing import Literal
+
+import torch
+
+from myelin_b200 import _native as nat
+from myelin_b200.autograd import ALIFScanFunction, LIFScanFunction, LinearScanFunction
+from myelin_b200.checkpointing import CheckpointSize, resolve_checkpoint_size
+from myelin_b200.neurons import ALIFParams, ALIFState, LIFParams, LIFState
+from myelin_b200.packing import PackedSpikes
+from myelin_b200.surrogates import SurrogateName, surrogate_id
+
+Backend = Literal["auto", "torch", "triton", "triton_generated", "triton_compile", "cuda"]
+_BACKENDS = frozenset(("auto", "torch", "triton", "triton_generated", "triton_compile", "cuda"))
+ResetMode = Literal["hard", "subtract"]
+
+
+def _check_backend(backend: str) -> None:
+    if backend not in _BACKENDS:
+        raise ValueError(f"unsupported backend: {backend}")
+
+
+def _reset_code(reset_mode: str) -> int:
+    if reset_mode == "hard":
+        return nat.MB_RESET_HARD
+    if reset_mode == "subtract":
+        return nat.MB_RESET_SUBTRACT
+    raise ValueError("reset_mode must be 'hard' or 'subtract'")
+
+
+def _validate_scan(inputs: torch.Tensor, states: list[tuple[str, torch.Tensor]]) -> None:
+    """Validation order and messages of src/myelin/triton/lif.py:340-353."""
+
+    if inputs.ndim != 3:
+        raise ValueError(f"inputs must be shaped [T, B, N]; got {tuple(inputs.shape)}")
+    for name, tensor in states:
+        if tensor.shape != inputs.shape[1:]:
+            raise ValueError(
+                f"initial_state.{name} must match inputs.shape[1:]; "
+                f"got {tuple(tensor.shape)} and {tuple(inputs.shape[1:])}"
+            )
+    nat.require_cuda(inputs)
+    for name, tensor in states:
+        if tensor.device != inputs.device:
+            raise ValueError(f"initial_state.{name} must be on the same device as inputs")
+        if tensor.dtype != inputs.dtype:
+            raise ValueError(f"initial_state.{name} must have the same dtype as inputs")
+    if inputs.dtype not in nat.SCAN_DTYPES:
+        raise ValueError(
+            f"inputs must be float32, bfloat16 or float16 for the CUDA scan; got {inputs.dtype}"
+        )
+
+
+def _hard_forward_only(hard_forward: bool, what: str) -> None:
+    if not hard_forward:
+        raise ValueError(f"{what} currently supports only hard_forward=True")
+
+
+def lif_forward(
+    inputs: torch.Tensor,
+    initial_state: LIFState,
+    params: LIFParams,
+    *,
+    backend: Backend = "auto",
+    block_size: int = 256,
+    reset_mode: ResetMode = "hard",
+) -> tuple[LIFState, torch.Tensor]:
+    """Fused-time LIF forward over ``[T, B, N]`` (src/myelin/kernels.py:52-93).
+
+    Spikes are bit-exact with the reference's ``lif_unroll``. The backward
+    supports gradients of the final membrane only, like the reference's fused
+    path (src/myelin/autograd.py:44-101).
+    """
+
+    _check_backend(backend)
+    rc = _reset_code(reset_mode)
+    _validate_scan(inputs, [("membrane", initial_state.membrane)])
+    vT, spikes = LIFScanFunction.apply(
+        inputs.contiguous(),
+        initial_state.membrane.contiguous(),
+        params.decay,
+        float(params.threshold),
+        float(params.reset),
+        rc,
+        nat.MB_SURR_NONE,
+        0.0,
+        True,
+    )
+    return LIFState(membrane=vT), spikes
+
+
+def fused_lif_unroll(
+    inputs: torch.Tensor,
+    initial_state: LIFState,
+    params: LIFParams,
+    *,
+    backend: Backend = "auto",
+    block_size: int = 256,
+) -> tuple[LIFState, torch.Tensor]:
+    """Compatibility alias for ``lif_forward`` (src/myelin/kernels.py:849-865)."""
+
+    return lif_forward(inputs, initial_state, params, backend=backend, block_size=block_size)
+
+
+def lif_forward_packed_spikes(
+    inputs: torch.Tensor,
+    initial_state: LIFState,
+    params: LIFParams,
+    *,
+    backend: Backend = "auto",
+    block_b: int = 8,
+    reset_mode: ResetMode = "hard",
+) -> tuple[LIFState, PackedSpikes]:
+    """LIF forward writing int32 spike words directly (src/myelin/kernels.py:96-156).
+
+    Forward-only, like the reference's fused packed path.
+    """
+
+    _check_backend(backend)
+    rc = _reset_code(reset_mode)
+    _validate_scan(inputs, [("membrane", initial_state.membrane)])
+    x = inputs.contiguous()
+    v0 = initial_state.membrane.contiguous()
+    T, B, N = x.shape
+    words = torch.empty((T, B, (N + 31) // 32), dtype=torch.int32, device=x.device)
+    vT = torch.empty_like(v0)
+    nat.scan_forward(
+        neuron=nat.MB_LIF, x=x, v0=v0, a0=None, vT=vT, aT=None, spikes=None, packed=words,
+        rates=None, ckpt_v=None, ckpt_a=None, decay=params.decay,
+        threshold=float(params.threshold), reset=float(params.reset), adapt_decay=0.0, beta=0.0,
+        reset_mode=rc,
+    )
+    return LIFState(membrane=vT), PackedSpikes(data=words, original_shape=tuple(x.shape))
+
+
+def alif_forward(
+    inputs: torch.Tensor,
+    initial_state: ALIFState,
+    params: ALIFParams,
+    *,
+    backend: Backend = "auto",
+    block_size: int = 256,
+    reset_mode: ResetMode = "hard",
+) -> tuple[ALIFState, torch.Tensor]:
+    """Fused-time ALIF forward (src/myelin/kernels.py:159-199).
+
+    Spikes are bit-exact with ``alif_unroll``. Like the reference's torch
+    path, spikes carry no gradient; final-state gradients flow through the
+    membrane and adaptation recurrences.
+    """
+
+    _check_backend(backend)
+    rc = _reset_code(reset_mode)
+    _validate_scan(
+        inputs,
+        [("membrane", initial_state.membrane), ("adaptation", initial_state.adaptation)],
+    )
+    vT, aT, spikes = ALIFScanFunction.apply(
+        inputs.contiguous(),
+        initial_state.membrane.contiguous(),
+        initial_state.adaptation.contiguous(),
+        params.decay,
+        float(params.threshold),
+        float(params.reset),
+        params.adaptation_decay,
+        float(params.beta),
+        rc,
+        nat.MB_SURR_NONE,
+        0.0,
+    )
+    return ALIFState(membrane=vT, adaptation=aT), spikes.detach()
+
+
+def surrogate_lif_forward(
+    inputs: torch.Tensor,
+    initial_state: LIFState,
+    params: LIFParams,
+    *,
+    surrogate: SurrogateName = "atan",
+    surrogate_slope: float = 10.0,
+    hard_forward: bool = True,
+    backend: Backend = "auto",
+    block_size: int = 256,
+    checkpoint_size: CheckpointSize | None = None,
+    reset_mode: ResetMode = "hard",
+) -> tuple[LIFState, torch.Tensor]:
+    """Hard-forward LIF with a surrogate-gradient backward (src/myelin/kernels.py:249-337)."""
+
+    sid = surrogate_id(surrogate)
+    _check_backend(backend)
+    _hard_forward_only(hard_forward, "CUDA surrogate LIF")
+    rc = _reset_code(reset_mode)
+    _validate_scan(inputs, [("membrane", initial_state.membrane)])
+    if checkpoint_size is not None:
+        resolve_checkpoint_size(int(inputs.shape[0]) or 1, checkpoint_size)
+    vT, spikes = LIFScanFunction.apply(
+        inputs.contiguous(),
+        initial_state.membrane.contiguous(),
+        params.decay,
+        float(params.threshold),
+        float(params.reset),
+        rc,
+        sid,
+        float(surrogate_slope),
+        False,
+    )
+    return LIFState(membrane=vT), spikes
+
+
+def surrogate_alif_forward(
+    inputs: torch.Tensor,
+    initial_state: ALIFState,
+    params: ALIFParams,
+    *,
+    surrogate: SurrogateName = "atan",
+    surrogate_slope: float = 10.0,
+    hard_forward: bool = True,
+    backend: Backend = "auto",
+    checkpoint_size: CheckpointSize | None = None,
+    reset_mode: ResetMode = "hard",
+) -> tuple[ALIFState, torch.Tensor]:
+    """Hard-forward ALIF with a surrogate-gradient backward on the GPU.
+
+    The reference runs this only through torch autograd of
+    ``surrogate_alif_unroll`` (src/myelin/kernels.py:340-392,
+    src/myelin/functional.py:149-189); its adjoint is computed here in closed
+    form with chunked replay.
+    """
+
+    sid = surrogate_id(surrogate)
+    _check_backend(backend)
+    _hard_forward_only(hard_forward, "CUDA surrogate ALIF")
+    rc = _reset_code(reset_mode)
+    _validate_scan(
+        inputs,
+        [("membrane", initial_state.membrane), ("adaptation", initial_state.adaptation)],
+    )
+    if checkpoint_size is not None:
+        resolve_checkpoint_size(int(inputs.shape[0]) or 1, checkpoint_size)
+    vT, aT, spikes = ALIFScanFunction.apply(
+        inputs.contiguous(),
+        initial_state.membrane.contiguous(),
+        initial_state.adaptation.contiguous(),
+        params.decay,
+        float(params.threshold),
+        float(params.reset),
+        params.adaptation_decay,
+        float(params.beta),
+        rc,
+        sid,
+        float(surrogate_slope),
+    )
+    return ALIFState(membrane=vT, adaptation=aT), spikes
+
+
+def _validate_linear(
+    inputs: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None
+) -> None:
+    if inputs.ndim != 3:
+        raise ValueError(f"inputs must be shaped [T, B, F]; got {tuple(inputs.shape)}")
+    if weight.ndim != 2:
+        raise ValueError(f"weight must be shaped [F, N]; got {tuple(weight.shape)}")
+    if inputs.shape[2] != weight.shape[0]:
+        raise ValueError("inputs.shape[2] must match weight.shape[0]")
+    nat.require_cuda(inputs)
+    if weight.device != inputs.device or weight.dtype != inputs.dtype:
+        raise ValueError("weight must have the same device and dtype as inputs")
+    if bias is not None:
+        if bias.shape != (weight.shape[1],):
+            raise ValueError("bias must be shaped [N]")
+        if bias.device != inputs.device or bias.dtype != inputs.dtype:
+            raise ValueError("bias must have the same device and dtype as inputs")
+    if inputs.dtype not in nat.SCAN_DTYPES:
+        raise ValueError(
+            f"inputs must be float32, bfloat16 or float16 for the CUDA scan; got {inputs.dtype}"
+        )
+
+
+def linear_surrogate_lif_forward(
+    inputs: torch.Tensor,
+    weight: torch.Tensor,
+    bias: torch.Tensor | None,
+    params: LIFParams,
+    *,
+    surrogate: SurrogateName = "atan",
+    surrogate_slope: float = 10.0,
+    hard_forward: bool = True,
+    backend: Backend = "auto",
+    checkpoint_size: CheckpointSize | None = None,
+    block_b: int = 16,
+    block_n: int = 32,
+    block_f: int = 32,
+) -> tuple[LIFState, torch.Tensor]:
+    """Dense projection + surrogate LIF (src/myelin/kernels.py:395-562).
+
+    The membrane starts at zero (src/myelin/autograd.py:469-473). Gradients
+    flow to inputs, weight and bias.
+    """
+
+    sid = surrogate_id(surrogate)
+    _check_backend(backend)
+    _hard_forward_only(hard_forward, "streamed LinearSurrogateLIF")
+    if checkpoint_size is not None:
+        resolve_checkpoint_size(int(inputs.shape[0]), checkpoint_size)
+    _validate_linear(inputs, weight, bias)
+    vT, spikes = LinearScanFunction.apply(
+        inputs.contiguous(),
+        weight.contiguous(),
+        None if bias is None else bias.contiguous(),
+        params.decay,
+        float(params.threshold),
+        float(params.reset),
+        sid,
+        float(surrogate_slope),
+        False,
+    )
+    return LIFState(membrane=vT), spikes
+
+
+def linear_surrogate_lif_rate_forward(
+    inputs: torch.Tensor,
+    weight: torch.Tensor,
+    bias: torch.Tensor | None,
+    params: LIFParams,
+    *,
+    surrogate: SurrogateName = "atan",
+    surrogate_slope: float = 10.0,
+    hard_forward: bool = True,
+    backend: Backend = "auto",
+    checkpoint_size: CheckpointSize = 25,
+    block_b: int = 16,
+    block_n: int = 32,
+    block_f: int = 32,
+    reduction: Literal["mean", "none"] = "mean",
+) -> tuple[LIFState, torch.Tensor]:
+    """Dense projection + surrogate LIF returning spike rates ``count / T``.
+
+    Never materialises dense spikes (src/myelin/kernels.py:565-702).
+    """
+
+    sid = surrogate_id(surrogate)
+    _check_backend(backend)
+    resolve_checkpoint_size(int(inputs.shape[0]), checkpoint_size)
+    _hard_forward_only(hard_forward, "checkpointed spike-rate LIF")
+    if reduction not in {"mean", "none"}:
+        raise ValueError("reduction must be 'mean' or 'none'")
+    _validate_linear(inputs, weight, bias)
+    vT, rates = LinearScanFunction.apply(
+        inputs.contiguous(),
+        weight.contiguous(),
+        None if bias is None else bias.contiguous(),
+        params.decay,
+        float(params.threshold),
+        float(params.reset),
+        sid,
+        float(surrogate_slope),
+        True,
+    )
+    if reduction == "mean":
+        return LIFState(membrane=vT), rates.mean()
+    return LIFState(membrane=vT), rates
+
+
+def linear_surrogate_lif_packed_forward(
+    inputs: torch.Tensor,
+    weight: torch.Tensor,
+    bias: torch.Tensor | None,
+    params: LIFParams,
+    *,
+    surrogate: SurrogateName = "atan",
+    surrogate_slope: float = 10.0,
+    hard_forward: bool = True,
+    backend: Backend = "auto",
+    checkpoint_size: CheckpointSize = 25,
+    block_b: int = 16,
+    block_f: int = 32,
+) -> tuple[LIFState, PackedSpikes]:
+    """Forward-only dense projection + LIF with packed int32 spike output.
+
+    src/myelin/kernels.py:705-776. Not differentiable.
+    """
+
+    surrogate_id(surrogate)
+    _check_backend(backend)
+    resolve_checkpoint_size(int(inputs.shape[0]), checkpoint_size)
+    _hard_forward_only(hard_forward, "packed surrogate LIF")
+    _validate_linear(inputs, weight, bias)
+    with torch.no_grad():
+        T, B, F = inputs.shape
+        N = weight.shape[1]
+        x2 = inputs.contiguous().reshape(T * B, F)
+        w = weight.contiguous()
+        currents = torch.addmm(bias, x2, w) if bias is not None else torch.mm(x2, w)
+        currents = currents.view(T, B, N)
+        v0 = torch.zeros((B, N), dtype=inputs.dtype, device=inputs.device)
+        vT = torch.empty_like(v0)
+        words = torch.empty((T, B, (N + 31) // 32), dtype=torch.int32, device=inputs.device)
+        nat.scan_forward(
+            neuron=nat.MB_LIF, x=currents, v0=v0, a0=None, vT=vT, aT=None, spikes=None,
+            packed=words, rates=None, ckpt_v=None, ckpt_a=None, decay=params.decay,
+            threshold=float(params.threshold), reset=float(params.reset), adapt_decay=0.0,
+            beta=0.0, reset_mode=nat.MB_RESET_HARD,
+        )
+    return LIFState(membrane=vT), PackedSpikes(data=words, original_shape=(T, B, N))

@@ -1,0 +1,184 @@
+"""Host logic of the packed-spike collectives, on CPU.
+
+A fake ``torch.distributed`` (as in the reference's tests/test_distributed.py:86-124)
+checks the call pattern; a real 2-rank gloo process group (spawned processes,
+file:// rendezvous, bounded joins) checks the all-gather layout, the int32
+wire format and the int64 results. Counting on CPU uses the numpy oracle in
+place of the CUDA count kernels (which the GPU tests cover).
+"""
+
+from __future__ import annotations
+
+import multiprocessing
+from pathlib import Path
+from typing import Any
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as torch_dist
+
+import myelin_b200.distributed as mbd
+from myelin_b200.packing import PackedSpikes, _normalize_count_dims
+
+
+def oracle_packed(spikes: np.ndarray) -> PackedSpikes:
+    from oracle import oracle
+
+    return PackedSpikes(data=torch.from_numpy(oracle.pack(spikes)), original_shape=spikes.shape)
+
+
+def oracle_count(packed: PackedSpikes, dim=None) -> torch.Tensor:
+    """Dense-like counts from the oracle's unpack (CPU stand-in for the CUDA counts)."""
+
+    from oracle import oracle
+
+    bits = torch.from_numpy(oracle.unpack(packed.data.numpy(), packed.original_shape[-1])).to(torch.int64)
+    if dim is None:
+        return bits.sum()
+    return bits.sum(dim=_normalize_count_dims(dim, ndim=bits.ndim))
+
+
+def oracle_leading(packed: PackedSpikes, *, dtype=torch.int64) -> torch.Tensor:
+    return oracle_count(packed, tuple(range(len(packed.original_shape) - 1))).to(dtype)
+
+
+class FakeDist:
+    class ReduceOp:
+        SUM = "sum"
+
+    def __init__(self, world_size: int = 2, initialized: bool = True) -> None:
+        self.world_size = world_size
+        self.initialized = initialized
+        self.reduced_dtype: torch.dtype | None = None
+
+    def is_available(self) -> bool:
+        return True
+
+    def is_initialized(self) -> bool:
+        return self.initialized
+
+    def get_world_size(self, group: Any | None = None) -> int:
+        return self.world_size
+
+    def all_gather_into_tensor(self, out: torch.Tensor, local: torch.Tensor, group=None) -> None:
+        assert out.shape[0] == self.world_size * local.shape[0]  # concatenated form
+        blocks = out.view(self.world_size, *local.shape)
+        for rank in range(self.world_size):
+            blocks[rank].copy_(local + rank)
+
+    def all_reduce(self, tensor: torch.Tensor, op=None, group=None) -> None:
+        assert op == self.ReduceOp.SUM
+        self.reduced_dtype = tensor.dtype
+        tensor.mul_(self.world_size)
+
+
+@pytest.fixture
+def fake(monkeypatch):
+    fd = FakeDist(world_size=3)
+    monkeypatch.setattr(mbd, "dist", fd)
+    monkeypatch.setattr(mbd, "packed_spike_count", oracle_count)
+    monkeypatch.setattr(mbd, "packed_spike_counts_over_leading_dims", oracle_leading)
+    return fd
+
+
+def test_all_gather_keeps_metadata_and_rank_order(fake):
+    spikes = np.zeros((2, 3, 35), np.float32)
+    spikes[..., 0] = 1.0
+    packed = oracle_packed(spikes)
+    gathered = mbd.packed_spike_all_gather(packed)
+    assert len(gathered) == 3
+    for rank, item in enumerate(gathered):
+        assert item.original_shape == packed.original_shape
+        assert torch.equal(item.data, packed.data + rank)
+    buf = mbd.packed_spike_all_gather_into_tensor(packed)
+    assert buf.shape == (3, *packed.data.shape)
+
+
+def test_count_all_reduce_uses_int32_wire_and_returns_int64(fake):
+    spikes = np.zeros((2, 3, 35), np.float32)
+    spikes[0, :, 0] = 1.0
+    spikes[1, :, 1] = 1.0
+    packed = oracle_packed(spikes)
+    counts = mbd.packed_spike_count_all_reduce(packed, dim=-1)
+    assert fake.reduced_dtype == torch.int32
+    assert counts.dtype == torch.int64
+    assert torch.equal(counts, torch.from_numpy(spikes.sum(-1).astype(np.int64)) * 3)
+    per_neuron = mbd.packed_spike_count_all_reduce(packed, dim=(0, 1))
+    assert torch.equal(per_neuron, torch.from_numpy(spikes.sum((0, 1)).astype(np.int64)) * 3)
+    rates = mbd.packed_spike_rate_all_reduce(packed, dim=-1)
+    assert torch.allclose(rates, torch.from_numpy(spikes.mean(-1)))
+
+
+def test_count_all_reduce_falls_back_to_int64_when_int32_could_overflow(fake, monkeypatch):
+    monkeypatch.setattr(mbd, "_INT32_MAX", 10)
+    packed = oracle_packed(np.ones((2, 3, 35), np.float32))
+    counts = mbd.packed_spike_count_all_reduce(packed)
+    assert fake.reduced_dtype == torch.int64
+    assert counts.item() == 2 * 3 * 35 * 3
+
+
+def test_collectives_require_initialized_process_group(monkeypatch):
+    monkeypatch.setattr(mbd, "dist", FakeDist(initialized=False))
+    packed = PackedSpikes(data=torch.zeros((1, 1), dtype=torch.int32), original_shape=(1, 32))
+    with pytest.raises(RuntimeError, match="not initialized"):
+        mbd.packed_spike_all_gather(packed)
+    with pytest.raises(RuntimeError, match="not initialized"):
+        mbd.packed_spike_count_all_reduce(packed)
+    assert not mbd.distributed_available_and_initialized() or torch_dist.is_initialized()
+
+
+def _rank_spikes(rank: int) -> np.ndarray:
+    spikes = np.zeros((4, 3, 70), np.float32)
+    spikes[..., rank] = 1.0
+    spikes[rank, 1, 40 + rank] = 1.0
+    return spikes
+
+
+def _gloo_worker(rank: int, world: int, init: str, queue) -> None:
+    torch_dist.init_process_group("gloo", init_method=init, rank=rank, world_size=world)
+    try:
+        mbd.packed_spike_count = oracle_count
+        mbd.packed_spike_counts_over_leading_dims = oracle_leading
+        packed = oracle_packed(_rank_spikes(rank))
+        gathered = mbd.packed_spike_all_gather(packed)
+        ok = all(torch.equal(g.data, oracle_packed(_rank_spikes(r)).data) for r, g in enumerate(gathered))
+        total = sum(_rank_spikes(r) for r in range(world))
+        cols = mbd.packed_spike_count_all_reduce(packed, dim=(0, 1))
+        ok = ok and torch.equal(cols, torch.from_numpy(total.sum((0, 1)).astype(np.int64)))
+        rows = mbd.packed_spike_count_all_reduce(packed, dim=-1)
+        ok = ok and torch.equal(rows, torch.from_numpy(total.sum(-1).astype(np.int64)))
+        rate = mbd.packed_spike_rate_all_reduce(packed)
+        ok = ok and torch.allclose(rate, torch.tensor(float(total.sum()) / (total.size * world)))
+        queue.put((rank, bool(ok), ""))
+    except Exception as exc:  # the parent reports child failures
+        queue.put((rank, False, f"{type(exc).__name__}: {exc}"))
+    finally:
+        torch_dist.destroy_process_group()
+
+
+def test_collectives_on_two_gloo_ranks(tmp_path: Path):
+    if not torch_dist.is_available() or not torch_dist.is_gloo_available():
+        pytest.skip("gloo unavailable")
+    world = 2
+    ctx = multiprocessing.get_context("spawn")
+    queue = ctx.Queue()
+    init = f"file://{tmp_path / 'rendezvous'}"
+    procs = [ctx.Process(target=_gloo_worker, args=(r, world, init, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    failures = []
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.terminate()
+            failures.append(f"rank process {p.pid} timed out")
+        elif p.exitcode != 0:
+            failures.append(f"rank process {p.pid} exited with {p.exitcode}")
+    results = []
+    while not queue.empty():
+        results.append(queue.get(timeout=1))
+    failures += [msg for _, ok, msg in results if not ok]
+    if len(results) != world:
+        failures.append(f"expected {world} results, got {len(results)}")
+    assert not failures, failures
