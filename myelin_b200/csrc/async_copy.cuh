@@ -46,6 +46,11 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// Plain arrival (count 1) on a barrier, e.g. "this warp is done with a stage".
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
 // One contiguous copy of `bytes` (multiple of 16, both addresses 16-byte
 // aligned) from global memory into this CTA's shared memory; completion is
 // signalled on `bar` as transaction bytes.

@@ -15,101 +15,9 @@
 
 #include "async_copy.cuh"
 #include "common.cuh"
+#include "scan_common.cuh"
 
 namespace mb {
-
-constexpr int kChunk = MB_SCAN_CHUNK;
-constexpr int kBlock = 256;
-
-struct ScanFwdArgs {
-  const void* x;
-  const void* v0;
-  const void* a0;
-  void* vT;
-  void* aT;
-  void* spikes;
-  int32_t* packed;
-  void* rates;
-  float* ckpt_v;
-  float* ckpt_a;
-  int64_t T, B, N, BN;
-  int64_t words_per_row;   // ceil(N / 32)
-  int64_t groups_per_row;  // ceil(N / (32 * NPT))
-  float decay, threshold, reset, adapt_decay, beta;
-};
-
-struct ScanBwdArgs {
-  const void* x;
-  const float* ckpt_v;
-  const float* ckpt_a;
-  const void* grad_spikes;
-  const void* grad_rates;
-  const void* grad_vT;
-  const void* grad_aT;
-  void* grad_x;
-  void* grad_v0;
-  void* grad_a0;
-  int64_t T, B, N, BN;
-  int64_t groups_per_row;  // ceil(N / 32)
-  float decay, threshold, reset, adapt_decay, beta, slope;
-};
-
-// One step of the neuron recurrence, shared by the forward and the backward
-// replay so that both produce bit-identical membranes and spike decisions.
-template <int KIND, int RESET>
-struct Step {
-  float p;      // pre-reset membrane
-  float theta;  // (adaptive) threshold used for this step
-  bool s;       // spike
-  __device__ __forceinline__ void run(float& m, float& a, float x, const float decay,
-                                      const float thr, const float reset_v,
-                                      const float adapt_decay, const float beta) {
-    p = __fadd_rn(__fmul_rn(m, decay), x);
-    theta = (KIND == MB_ALIF) ? __fadd_rn(thr, __fmul_rn(beta, a)) : thr;
-    s = p >= theta;
-    if (RESET == MB_RESET_HARD) {
-      m = s ? reset_v : p;
-    } else {
-      m = s ? __fsub_rn(p, theta) : p;
-    }
-    if (KIND == MB_ALIF) {
-      a = __fadd_rn(__fmul_rn(a, adapt_decay), s ? 1.0f : 0.0f);
-    }
-  }
-};
-
-// Closed-form surrogate derivatives, as src/myelin/surrogates.py:78-102 and
-// src/myelin/triton/lif.py:225-249 (ids 0..5). MB_SURR_NONE returns 0: the
-// gradient of the hard threshold itself.
-template <int SURR>
-__device__ __forceinline__ float surrogate_grad(float c) {
-  if constexpr (SURR == MB_SURR_SIGMOID) {
-    const float v = __fdividef(1.0f, 1.0f + __expf(-c));
-    return v * (1.0f - v);
-  } else if constexpr (SURR == MB_SURR_FAST_SIGMOID) {
-    const float dn = 1.0f + fabsf(c);
-    return __fdividef(0.5f, dn * dn);
-  } else if constexpr (SURR == MB_SURR_ATAN) {
-    const float u = 1.5707963267948966f * c;  // (pi / 2) * c
-    return __fdividef(0.5f, 1.0f + u * u);
-  } else if constexpr (SURR == MB_SURR_TRIANGULAR) {
-    const float sgn = c > 0.0f ? 1.0f : (c < 0.0f ? -1.0f : 0.0f);
-    return fabsf(c) < 1.0f ? -sgn : 0.0f;
-  } else if constexpr (SURR == MB_SURR_SUPERSPIKE) {
-    const float dn = 1.0f + fabsf(c);
-    return __fdividef(1.0f, dn * dn);
-  } else if constexpr (SURR == MB_SURR_MULTI_GAUSSIAN) {
-    // 0.6 * N(c; 0, 0.5) + 0.2 * N(c; 1, 1) + 0.2 * N(c; -1, 1)
-    const float cm = c - 1.0f;
-    const float cp = c + 1.0f;
-    const float center = 0.47873073648171924f * __expf(-2.0f * c * c);
-    const float right = 0.07978845608028655f * __expf(-0.5f * cm * cm);
-    const float left = 0.07978845608028655f * __expf(-0.5f * cp * cp);
-    return center + right + left;
-  } else {
-    return 0.0f;
-  }
-}
 
 // ---------------------------------------------------------------------------
 // Forward scan.
@@ -654,6 +562,10 @@ extern "C" int mb_scan_forward(int neuron, int dtype, const void* x, const void*
   a.decay = decay; a.threshold = threshold; a.reset = reset;
   a.adapt_decay = adapt_decay; a.beta = beta;
   cudaStream_t s = as_stream(stream);
+  if (launch_scan_fwd_fast(dtype, neuron, reset_mode, a, s)) {
+    MB_CHECK_LAUNCH("mb_scan_forward");
+    return 0;
+  }
   switch (dtype) {
     case MB_F32: dispatch_fwd<float>(neuron, reset_mode, a, s); break;
     case MB_BF16: dispatch_fwd<__nv_bfloat16>(neuron, reset_mode, a, s); break;
@@ -688,6 +600,10 @@ extern "C" int mb_scan_backward(int neuron, int dtype, const void* x, const floa
   a.decay = decay; a.threshold = threshold; a.reset = reset;
   a.adapt_decay = adapt_decay; a.beta = beta; a.slope = slope;
   cudaStream_t s = as_stream(stream);
+  if (launch_scan_bwd_fast(dtype, neuron, reset_mode, surrogate, a, s)) {
+    MB_CHECK_LAUNCH("mb_scan_backward");
+    return 0;
+  }
   switch (dtype) {
     case MB_F32: dispatch_bwd<float>(neuron, reset_mode, surrogate, a, s); break;
     case MB_BF16: dispatch_bwd<__nv_bfloat16>(neuron, reset_mode, surrogate, a, s); break;

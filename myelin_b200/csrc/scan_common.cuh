@@ -1,0 +1,202 @@
+// Shared definitions of the LIF/ALIF scan kernels: argument blocks, the
+// bit-exact neuron step, and the closed-form surrogate derivatives.
+#pragma once
+
+#include "common.cuh"
+
+namespace mb {
+
+constexpr int kChunk = MB_SCAN_CHUNK;
+constexpr int kBlock = 256;
+
+struct ScanFwdArgs {
+  const void* x;
+  const void* v0;
+  const void* a0;
+  void* vT;
+  void* aT;
+  void* spikes;
+  int32_t* packed;
+  void* rates;
+  float* ckpt_v;
+  float* ckpt_a;
+  int64_t T, B, N, BN;
+  int64_t words_per_row;   // ceil(N / 32)
+  int64_t groups_per_row;  // ceil(N / (32 * NPT))
+  float decay, threshold, reset, adapt_decay, beta;
+};
+
+struct ScanBwdArgs {
+  const void* x;
+  const float* ckpt_v;
+  const float* ckpt_a;
+  const void* grad_spikes;
+  const void* grad_rates;
+  const void* grad_vT;
+  const void* grad_aT;
+  void* grad_x;
+  void* grad_v0;
+  void* grad_a0;
+  int64_t T, B, N, BN;
+  int64_t groups_per_row;  // ceil(N / 32)
+  float decay, threshold, reset, adapt_decay, beta, slope;
+};
+
+// One step of the neuron recurrence, shared by the forward and the backward
+// replay so that both produce bit-identical membranes and spike decisions.
+template <int KIND, int RESET>
+struct Step {
+  float p;      // pre-reset membrane
+  float theta;  // (adaptive) threshold used for this step
+  bool s;       // spike
+  __device__ __forceinline__ void run(float& m, float& a, float x, const float decay,
+                                      const float thr, const float reset_v,
+                                      const float adapt_decay, const float beta) {
+    p = __fadd_rn(__fmul_rn(m, decay), x);
+    theta = (KIND == MB_ALIF) ? __fadd_rn(thr, __fmul_rn(beta, a)) : thr;
+    s = p >= theta;
+    if (RESET == MB_RESET_HARD) {
+      m = s ? reset_v : p;
+    } else {
+      m = s ? __fsub_rn(p, theta) : p;
+    }
+    if (KIND == MB_ALIF) {
+      a = __fadd_rn(__fmul_rn(a, adapt_decay), s ? 1.0f : 0.0f);
+    }
+  }
+};
+
+// Closed-form surrogate derivatives, as src/myelin/surrogates.py:78-102 and
+// src/myelin/triton/lif.py:225-249 (ids 0..5). MB_SURR_NONE returns 0: the
+// gradient of the hard threshold itself.
+template <int SURR>
+__device__ __forceinline__ float surrogate_grad(float c) {
+  if constexpr (SURR == MB_SURR_SIGMOID) {
+    const float v = __fdividef(1.0f, 1.0f + __expf(-c));
+    return v * (1.0f - v);
+  } else if constexpr (SURR == MB_SURR_FAST_SIGMOID) {
+    const float dn = 1.0f + fabsf(c);
+    return __fdividef(0.5f, dn * dn);
+  } else if constexpr (SURR == MB_SURR_ATAN) {
+    const float u = 1.5707963267948966f * c;  // (pi / 2) * c
+    return __fdividef(0.5f, 1.0f + u * u);
+  } else if constexpr (SURR == MB_SURR_TRIANGULAR) {
+    const float sgn = c > 0.0f ? 1.0f : (c < 0.0f ? -1.0f : 0.0f);
+    return fabsf(c) < 1.0f ? -sgn : 0.0f;
+  } else if constexpr (SURR == MB_SURR_SUPERSPIKE) {
+    const float dn = 1.0f + fabsf(c);
+    return __fdividef(1.0f, dn * dn);
+  } else if constexpr (SURR == MB_SURR_MULTI_GAUSSIAN) {
+    // 0.6 * N(c; 0, 0.5) + 0.2 * N(c; 1, 1) + 0.2 * N(c; -1, 1)
+    const float cm = c - 1.0f;
+    const float cp = c + 1.0f;
+    const float center = 0.47873073648171924f * __expf(-2.0f * c * c);
+    const float right = 0.07978845608028655f * __expf(-0.5f * cm * cm);
+    const float left = 0.07978845608028655f * __expf(-0.5f * cp * cp);
+    return center + right + left;
+  } else {
+    return 0.0f;
+  }
+}
+
+
+// Surrogate derivative with the slope folded in: d(diff) = slope * sg(slope * diff)
+// where diff = p - theta. Same functions as surrogate_grad, with the
+// constants pre-multiplied so the hot loop spends as few instructions as
+// possible (one reciprocal, a few multiply-adds).
+template <int SURR>
+struct SurrogateD {
+  float k0, k1;
+  __device__ __forceinline__ explicit SurrogateD(float slope) {
+    if (SURR == MB_SURR_ATAN) {
+      k0 = 1.5707963267948966f * slope;  // u = (pi/2) * slope * diff
+      k1 = 0.5f * slope;                 // d = 0.5 * slope / (1 + u^2)
+    } else if (SURR == MB_SURR_FAST_SIGMOID) {
+      k0 = slope;
+      k1 = 0.5f * slope;                 // d = 0.5 * slope / (1 + |slope diff|)^2
+    } else if (SURR == MB_SURR_SUPERSPIKE) {
+      k0 = slope;
+      k1 = slope;                        // d = slope / (1 + |slope diff|)^2
+    } else {
+      k0 = slope;
+      k1 = slope;
+    }
+  }
+  __device__ __forceinline__ float operator()(float diff) const {
+    if constexpr (SURR == MB_SURR_ATAN) {
+      const float u = k0 * diff;
+      return __fdividef(k1, 1.0f + u * u);
+    } else if constexpr (SURR == MB_SURR_FAST_SIGMOID || SURR == MB_SURR_SUPERSPIKE) {
+      const float dn = 1.0f + fabsf(k0 * diff);
+      return __fdividef(k1, dn * dn);
+    } else if constexpr (SURR == MB_SURR_NONE) {
+      return 0.0f;
+    } else {
+      return k1 * surrogate_grad<SURR>(k0 * diff);
+    }
+  }
+};
+
+// Two neighbouring neurons' I/O values moved as one 4- or 8-byte word.
+template <typename T>
+struct Pair;
+
+template <>
+struct Pair<float> {
+  using V = float2;
+  static __device__ __forceinline__ float2 to_f2(float2 v) { return v; }
+  static __device__ __forceinline__ float2 from_f2(float a, float b) { return make_float2(a, b); }
+  static __device__ __forceinline__ float2 spikes(bool s0, bool s1) {
+    return make_float2(s0 ? 1.0f : 0.0f, s1 ? 1.0f : 0.0f);
+  }
+};
+
+template <>
+struct Pair<__nv_bfloat16> {
+  using V = uint32_t;  // bf16x2, low half = first neuron
+  static __device__ __forceinline__ float2 to_f2(uint32_t v) {
+    return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+  }
+  static __device__ __forceinline__ uint32_t from_f2(float a, float b) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+  static __device__ __forceinline__ uint32_t spikes(bool s0, bool s1) {
+    return (s0 ? 0x00003f80u : 0u) | (s1 ? 0x3f800000u : 0u);
+  }
+};
+
+template <>
+struct Pair<__half> {
+  using V = uint32_t;  // f16x2, low half = first neuron
+  static __device__ __forceinline__ float2 to_f2(uint32_t v) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&v));
+  }
+  static __device__ __forceinline__ uint32_t from_f2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+  static __device__ __forceinline__ uint32_t spikes(bool s0, bool s1) {
+    return (s0 ? 0x00003c00u : 0u) | (s1 ? 0x3c000000u : 0u);
+  }
+};
+
+// Spread the low 16 bits of x to the even bit positions of a 32-bit word.
+__device__ __forceinline__ uint32_t spread_even_bits(uint32_t x) {
+  x &= 0xffffu;
+  x = (x | (x << 8)) & 0x00ff00ffu;
+  x = (x | (x << 4)) & 0x0f0f0f0fu;
+  x = (x | (x << 2)) & 0x33333333u;
+  x = (x | (x << 1)) & 0x55555555u;
+  return x;
+}
+
+// Host launchers of the warp-specialized two-neurons-per-thread kernels
+// (scan_fast.cu). They return false when the shape or alignment does not fit
+// their layout (the caller then uses the general kernels).
+bool launch_scan_fwd_fast(int dtype, int neuron, int reset_mode, const ScanFwdArgs& a,
+                          cudaStream_t stream);
+bool launch_scan_bwd_fast(int dtype, int neuron, int reset_mode, int surrogate,
+                          const ScanBwdArgs& a, cudaStream_t stream);
+
+}  // namespace mb

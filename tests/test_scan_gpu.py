@@ -266,7 +266,13 @@ def test_16bit_io_gradients_vs_fp32_carry_oracle(oracle, dtype, neuron):
     assert np.array_equal(host(spikes).astype(np.uint8), fwd["spikes"])
     (spikes * gs.to(DEV)).sum().backward()
     assert xd.grad.dtype == dtype
-    assert_close_scaled(host(xd.grad), ref["grad_x"], rtol=2e-2, what="grad_x")
+    got = host(xd.grad)
+    # gradients beyond the 16-bit range round to +-inf, exactly where the fp32 result does
+    expected = _round(ref["grad_x"], dtype)
+    overflow = ~np.isfinite(expected)
+    assert np.array_equal(~np.isfinite(got), overflow)
+    assert_close_scaled(np.where(overflow, 0, got), np.where(overflow, 0, ref["grad_x"]),
+                        rtol=2e-2, what="grad_x")
 
 
 def test_time_lengths_not_multiple_of_chunk_and_zero(oracle):
