@@ -173,6 +173,28 @@ int mb_count_columns(const int32_t* words, int64_t rows, int64_t n, int64_t* cou
                      int32_t* counts32, void* workspace, int64_t workspace_bytes,
                      void* stream);
 
+/* Largest scratch (bytes) mb_count_columns_noalloc can use: 4 MiB. */
+#define MB_COUNT_COLUMNS_NOALLOC_MAX_BYTES (4 << 20)
+
+/*
+ * mb_count_columns for callers that cannot allocate device memory when they
+ * count: for example code running under a host runtime that owns all device
+ * memory through its own fixed arena, or a latency-critical loop in which an
+ * allocation call would block on the device. The per-slice partial sums live
+ * in a fixed device array inside the library (MB_COUNT_COLUMNS_NOALLOC_MAX_BYTES,
+ * held on every GPU that loads the library until the process exits), so the
+ * caller passes only the words and the outputs. Same results as
+ * mb_count_columns. Shapes whose scratch (mb_count_columns_workspace_bytes)
+ * exceeds the limit are rejected with an error; the call allocates nothing.
+ * The first call on each device looks up the array's device address (a
+ * one-time set-up); make that first call before any stream capture. All calls
+ * share the array: calls whose kernels overlap on the GPU race and give wrong
+ * counts, so keep them ordered on one stream.
+ * No counterpart in the reference.
+ */
+int mb_count_columns_noalloc(const int32_t* words, int64_t rows, int64_t n, int64_t* counts64,
+                             int32_t* counts32, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -67,6 +67,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mb_count_rows": (_int, [_vp, _i64, _i64, _vp, _vp]),
     "mb_count_columns_workspace_bytes": (_i64, [_i64, _i64]),
     "mb_count_columns": (_int, [_vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp]),
+    "mb_count_columns_noalloc": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
 }
 
 EXPORTED_SYMBOLS = tuple(_SIGNATURES)

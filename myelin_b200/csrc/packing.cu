@@ -8,6 +8,8 @@
 // multiple of 32 and the base pointer is 16-byte aligned, every thread moves
 // exactly 16 bytes per access (fully coalesced); other shapes take a scalar
 // path with the same results.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace mb {
@@ -392,5 +394,86 @@ extern "C" int mb_count_columns(const int32_t* words, int64_t rows, int64_t n, i
   MB_CHECK_ARG(aligned_to(workspace, 4), "mb_count_columns: workspace misaligned");
   launch_count_columns(words, rows, n, counts64, counts32, static_cast<int32_t*>(workspace), s);
   MB_CHECK_LAUNCH("mb_count_columns");
+  return 0;
+}
+
+// ---------------------------------------------------------------------------
+// Column counts without any allocation.
+//
+// Some callers cannot allocate device memory at the point where they need a
+// count: code running under a host runtime that owns every byte of device
+// memory through its own fixed arena (and forbids other allocations), or a
+// latency-critical loop where an allocation call would block on the device.
+// For them the column count's per-slice partial sums live in this file-scope
+// device array instead of a caller-provided workspace. The array is part of
+// the library's device image: every GPU that loads the library holds it until
+// the process exits.
+//
+// Every call shares the one array and overwrites it. Each partial sum is
+// written before it is read within the same call, so nothing has to start at
+// zero and stale contents from an earlier call are never used. Two calls
+// whose kernels overlap on the GPU (different streams, or different host
+// threads on the same device) race on the array and give wrong counts: keep
+// such calls ordered on one stream.
+// ---------------------------------------------------------------------------
+namespace mb {
+
+constexpr int64_t kNoAllocScratchBytes = MB_COUNT_COLUMNS_NOALLOC_MAX_BYTES;
+static __device__ __align__(256) int32_t g_count_columns_scratch[kNoAllocScratchBytes / 4];
+
+constexpr int kMaxDevices = 64;
+static int32_t* g_scratch_ptr[kMaxDevices] = {nullptr};
+static std::mutex g_scratch_mutex;
+
+// Device address of the scratch array on the current device, looked up once
+// per device (the host-side name of a __device__ array is not a device
+// address). Returns nullptr and sets the error message on failure.
+static int32_t* noalloc_scratch_for_current_device() {
+  int dev = -1;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    set_error("mb_count_columns_noalloc: cannot query the current device (%s)",
+              err != cudaSuccess ? cudaGetErrorString(err) : "device index out of range");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    err = cudaGetSymbolAddress(&p, g_count_columns_scratch);
+    if (err != cudaSuccess || p == nullptr) {
+      set_error("mb_count_columns_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+                cudaGetErrorString(err));
+      return nullptr;
+    }
+    g_scratch_ptr[dev] = static_cast<int32_t*>(p);
+  }
+  return g_scratch_ptr[dev];
+}
+
+}  // namespace mb
+
+extern "C" int mb_count_columns_noalloc(const int32_t* words, int64_t rows, int64_t n,
+                                        int64_t* counts64, int32_t* counts32, void* stream) {
+  clear_error();
+  MB_CHECK_ARG(rows >= 0 && n > 0,
+               "mb_count_columns_noalloc: packed.original_shape must have non-empty last dimension");
+  MB_CHECK_ARG(counts64 != nullptr || counts32 != nullptr, "mb_count_columns_noalloc: no output");
+  MB_CHECK_ARG(rows == 0 || words != nullptr, "mb_count_columns_noalloc: null words");
+  const int64_t need = count_columns_workspace_bytes(rows, n);
+  MB_CHECK_ARG(need <= kNoAllocScratchBytes,
+               "mb_count_columns_noalloc: this shape needs %lld bytes of scratch, more than the "
+               "built-in %lld; use mb_count_columns with a caller-provided workspace",
+               (long long)need, (long long)kNoAllocScratchBytes);
+  cudaStream_t s = as_stream(stream);
+  if (rows == 0) {
+    if (counts64) cudaMemsetAsync(counts64, 0, n * sizeof(int64_t), s);
+    if (counts32) cudaMemsetAsync(counts32, 0, n * sizeof(int32_t), s);
+    MB_CHECK_LAUNCH("mb_count_columns_noalloc");
+    return 0;
+  }
+  int32_t* scratch = noalloc_scratch_for_current_device();
+  if (scratch == nullptr) return 3;
+  launch_count_columns(words, rows, n, counts64, counts32, scratch, s);
+  MB_CHECK_LAUNCH("mb_count_columns_noalloc");
   return 0;
 }
