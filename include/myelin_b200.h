@@ -131,6 +131,21 @@ int mb_scan_backward(int neuron, int dtype, const void* x, const float* ckpt_v,
                      int reset_mode, int surrogate, float slope, void* stream);
 
 /*
+ * Dense projection on the tcgen05 tensor cores:
+ *   C[M, N] = A[M, K] * B[N, K]^T (+ bias[N])
+ * A, B: `in_dtype` (MB_BF16 or MB_F16), rows of K contiguous elements with
+ * leading dimensions lda, ldb (multiples of 8, 16-byte aligned bases);
+ * fp32 accumulation; C: `out_dtype` (MB_F32 or in_dtype), leading dimension
+ * ldc; bias: optional, MB_F32/MB_BF16/MB_F16. Used for the stream synapse's
+ * currents x[T*B, F] * W^T and its input gradient G[T*B, N] * W.
+ * Replaces: the per-timestep tl.dot of src/myelin/triton/lif.py:554-612 and
+ *   the projections of src/myelin/autograd.py:445-556 (torch.matmul).
+ */
+int mb_gemm_tn(int in_dtype, const void* A, int64_t lda, const void* B, int64_t ldb,
+               const void* bias, int bias_dtype, int out_dtype, void* C, int64_t ldc, int64_t M,
+               int64_t N, int64_t K, void* stream);
+
+/*
  * Pack spikes[rows, n] (any dtype; nonzero = spike, -0.0 counts as zero) into
  * int32 words[rows, ceil(n/32)], LSB-first, zero padding bits.
  * Replaces: packing.pack_spikes (src/myelin/packing.py:45-71) and

@@ -62,6 +62,9 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_int, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
          _i64, _i64, _i64, _f, _f, _f, _f, _f, _int, _int, _f, _vp],
     ),
+    "mb_gemm_tn": (
+        _int, [_int, _vp, _i64, _vp, _i64, _vp, _int, _int, _vp, _i64, _i64, _i64, _i64, _vp]
+    ),
     "mb_pack_spikes": (_int, [_int, _vp, _vp, _i64, _i64, _vp]),
     "mb_unpack_spikes": (_int, [_vp, _int, _vp, _i64, _i64, _vp]),
     "mb_count_rows": (_int, [_vp, _i64, _i64, _vp, _vp]),
@@ -197,6 +200,37 @@ def scan_backward(
             surrogate, slope, stream_handle(x.device),
         )
     check(status, "mb_scan_backward")
+
+
+GEMM_DTYPES = (torch.bfloat16, torch.float16)
+
+
+def gemm_tn_supported(a: torch.Tensor, b: torch.Tensor) -> bool:
+    """Whether mb_gemm_tn takes these operands (16-bit, 16-byte rows and bases)."""
+
+    return (
+        a.dtype in GEMM_DTYPES and b.dtype == a.dtype and a.dim() == 2 and b.dim() == 2
+        and a.shape[1] == b.shape[1] and a.shape[1] % 8 == 0
+        and a.stride(1) == 1 and b.stride(1) == 1
+        and a.stride(0) % 8 == 0 and b.stride(0) % 8 == 0
+        and a.data_ptr() % 16 == 0 and b.data_ptr() % 16 == 0
+    )
+
+
+def gemm_tn(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor | None,
+            out: torch.Tensor) -> torch.Tensor:
+    """out[M, N] = a[M, K] @ b[N, K]^T (+ bias) on the tcgen05 tensor cores."""
+
+    M, K = a.shape
+    N = b.shape[0]
+    with torch.cuda.device(a.device):
+        status = lib().mb_gemm_tn(
+            dtype_code(a.dtype), ptr(a), a.stride(0), ptr(b), b.stride(0), ptr(bias),
+            dtype_code(bias.dtype) if bias is not None else 0, dtype_code(out.dtype), ptr(out),
+            out.stride(0), M, N, K, stream_handle(a.device),
+        )
+    check(status, "mb_gemm_tn")
+    return out
 
 
 def num_checkpoints(T: int) -> int:

@@ -121,6 +121,33 @@ class ALIFScanFunction(torch.autograd.Function):
         return (*grads, *tail)
 
 
+def _project(x2: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
+    """currents[T*B, N] = x2[T*B, F] @ weight[F, N] (+ bias).
+
+    16-bit inputs run on the tcgen05 GEMM (fp32 accumulation, bias added in
+    fp32, one rounding to the input type). fp32 inputs keep fp32 arithmetic
+    (cuBLAS SGEMM): the tensor cores have no fp32-exact mode, and spike
+    parity with the fp32 reference needs fp32 products.
+    """
+
+    wt = weight.t().contiguous()  # [N, F]: K-major B operand
+    if nat.gemm_tn_supported(x2, wt):
+        out = torch.empty((x2.shape[0], wt.shape[0]), dtype=x2.dtype, device=x2.device)
+        return nat.gemm_tn(x2, wt, bias, out)
+    if bias is not None:
+        return torch.addmm(bias, x2, weight)
+    return torch.mm(x2, weight)
+
+
+def _input_grad(g2: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """dX[T*B, F] = G[T*B, N] @ weight[F, N]^T."""
+
+    if nat.gemm_tn_supported(g2, weight):
+        out = torch.empty((g2.shape[0], weight.shape[0]), dtype=g2.dtype, device=g2.device)
+        return nat.gemm_tn(g2, weight, None, out)
+    return torch.mm(g2, weight.t())
+
+
 class LinearScanFunction(torch.autograd.Function):
     """Dense projection ``x_t @ W + b`` feeding the LIF scan from a zero membrane.
 
@@ -147,11 +174,7 @@ class LinearScanFunction(torch.autograd.Function):
         T, B, F = inputs.shape
         N = weight.shape[1]
         x2 = inputs.reshape(T * B, F)
-        if bias is not None:
-            currents = torch.addmm(bias, x2, weight)
-        else:
-            currents = torch.mm(x2, weight)
-        currents = currents.view(T, B, N)
+        currents = _project(x2, weight, bias).view(T, B, N)
         save = any(ctx.needs_input_grad[:3])
         ckpt_v, _ = _scan_scratch(currents, False, save)
         v0 = torch.zeros((B, N), dtype=inputs.dtype, device=inputs.device)
@@ -191,7 +214,7 @@ class LinearScanFunction(torch.autograd.Function):
             surrogate=surrogate, slope=slope,
         )
         g2 = grad_currents.view(T * B, N)
-        grad_inputs = torch.mm(g2, weight.t()).view(T, B, F) if need_x else None
+        grad_inputs = _input_grad(g2, weight).view(T, B, F) if need_x else None
         grad_weight = torch.mm(inputs.reshape(T * B, F).t(), g2) if need_w else None
         grad_bias = g2.sum(dim=0) if (need_b and ctx.has_bias) else None
         return (grad_inputs, grad_weight, grad_bias, *tail)

@@ -1,0 +1,426 @@
+// Dense projection GEMM on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+//   C[M, N] = A[M, K] * B[N, K]^T (+ bias[N]),   A, B bf16 or f16 (K contiguous),
+//   fp32 accumulation in tensor memory, C written as fp32 or the input type.
+//
+// This is the stream-synapse projection of the spiking layers: currents of all
+// time steps at once, x[T*B, F] * W^T, feeding the scan; and the input
+// gradient G[T*B, N] * W[F, N]^T of the backward.
+//
+// One persistent CTA per SM, 6 warps:
+//   warp 0    copy engine driver: 2-D tiled bulk tensor copies (TMA) of A and
+//             B K-slices into a 4-stage shared-memory ring (128-byte swizzle);
+//   warp 1    allocates 2*BN TMEM columns and issues tcgen05.mma (one thread),
+//             M=128 x N=BN x K=16 per instruction, committing each stage back
+//             to the producer and each finished tile to the epilogue;
+//   warps 2-5 epilogue: tcgen05.ld of the accumulator (each warp reads its own
+//             32-lane quarter of TMEM), bias add, conversion, global stores.
+// Two TMEM accumulators let the epilogue of one tile overlap the MMAs of the
+// next. Every mbarrier wait is bounded.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <type_traits>
+
+#include "async_copy.cuh"
+#include "common.cuh"
+
+namespace mb {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // one 128-byte swizzle row of 16-bit elements
+constexpr int kStages = 4;
+constexpr int kThreads = 192;
+constexpr int kUmmaK = 16;
+
+struct GemmArgs {
+  const void* bias;
+  void* C;
+  int64_t ldc;
+  int64_t M, N, K;
+  int bias_dtype;  // MB_F32 / MB_BF16 / MB_F16
+  int vec_ok;      // C rows 16-byte aligned: 16-byte stores
+};
+
+template <int BN>
+struct Layout {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarrierBytes = 256;
+  static constexpr size_t kSmem = size_t(kStages) * kStageBytes + kBarrierBytes + 1024;
+  static constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
+};
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of
+// 128 bytes, 8-row groups 1024 bytes apart (the layout the TMA copy writes).
+__device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= uint64_t((saddr >> 4) & 0x3fffu);  // start address
+  d |= uint64_t(1) << 16;                  // leading byte offset (16 B; unused for this layout)
+  d |= uint64_t(1024 >> 4) << 32;          // stride byte offset: 8 rows x 128 B
+  d |= uint64_t(1) << 46;                  // descriptor version
+  d |= uint64_t(2) << 61;                  // 128-byte swizzle
+  return d;
+}
+
+// Instruction descriptor of kind::f16: fp32 accumulate, A/B type, both K-major.
+template <typename TIn, int BN>
+__device__ __forceinline__ uint32_t mma_idesc() {
+  constexpr uint32_t ab = std::is_same<TIn, __nv_bfloat16>::value ? 1u : 0u;
+  return (1u << 4)            // D = F32
+         | (ab << 7)          // A format
+         | (ab << 10)         // B format
+         | (uint32_t(BN >> 3) << 17)
+         | (uint32_t(kBM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// Arrive on `bar` once every MMA issued so far by this thread has completed.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_addr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float load_bias(const void* bias, int dtype, int64_t j) {
+  if (dtype == MB_F32) return __ldg(static_cast<const float*>(bias) + j);
+  if (dtype == MB_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(bias)[j]);
+  return __half2float(static_cast<const __half*>(bias)[j]);
+}
+
+template <typename TOut>
+__device__ __forceinline__ void store_row32(TOut* dst, const float (&v)[32], int valid,
+                                            bool vec_ok) {
+  if (vec_ok && valid == 32) {
+    if constexpr (std::is_same<TOut, float>::value) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        reinterpret_cast<float4*>(dst)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t w[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float a = v[8 * q + 2 * h], b = v[8 * q + 2 * h + 1];
+          if constexpr (std::is_same<TOut, __nv_bfloat16>::value) {
+            const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
+            w[h] = *reinterpret_cast<const uint32_t*>(&p);
+          } else {
+            const __half2 p = __floats2half2_rn(a, b);
+            w[h] = *reinterpret_cast<const uint32_t*>(&p);
+          }
+        }
+        reinterpret_cast<uint4*>(dst)[q] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+    return;
+  }
+  for (int j = 0; j < valid; ++j) {
+    if constexpr (std::is_same<TOut, float>::value) dst[j] = v[j];
+    else if constexpr (std::is_same<TOut, __nv_bfloat16>::value) dst[j] = __float2bfloat16_rn(v[j]);
+    else dst[j] = __float2half_rn(v[j]);
+  }
+}
+
+template <typename TIn, typename TOut, int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tn_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                   const GemmArgs args) {
+  using L = Layout<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + kStages * L::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sb + kStages * L::kBBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* acc_full = empty + kStages;  // [2]
+  uint64_t* acc_empty = acc_full + 2;    // [2]
+  uint64_t* drained = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drained + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t m_tiles = (args.M + kBM - 1) / kBM;
+  const int64_t n_tiles = (args.N + BN - 1) / BN;
+  const int64_t tiles = m_tiles * n_tiles;
+  const int kblocks = static_cast<int>((args.K + kBK - 1) / kBK);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    mbar_init(drained, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_addr(tmem_slot)),
+                 "r"(L::kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        const int tm = static_cast<int>(tile / n_tiles);
+        const int tn = static_cast<int>(tile % n_tiles);
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = static_cast<int>(it % kStages);
+          const uint32_t use = it / kStages;
+          if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], L::kStageBytes);
+          tma_load_2d(sa + s * L::kABytes, &tma_a, kb * kBK, tm * kBM, &full[s]);
+          tma_load_2d(sb + s * L::kBBytes, &tma_b, kb * kBK, tn * BN, &full[s]);
+        }
+      }
+      // every issued copy has landed before the CTA can retire
+      const uint32_t issued = it;
+      for (uint32_t j = issued > kStages ? issued - kStages : 0; j < issued; ++j) {
+        mbar_wait_bounded(&full[j % kStages], (j / kStages) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = mma_idesc<TIn, BN>();
+      uint32_t it = 0, local = 0;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++local) {
+        const uint32_t b = local & 1;
+        const uint32_t use_b = local >> 1;
+        if (use_b > 0 && !mbar_wait_bounded(&acc_empty[b], (use_b - 1) & 1)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + b * BN;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = static_cast<int>(it % kStages);
+          if (!mbar_wait_bounded(&full[s], (it / kStages) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_addr(sa + s * L::kABytes);
+          const uint32_t b0 = smem_addr(sb + s * L::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / kUmmaK; ++k) {
+            mma_f16(d_tmem, sw128_kmajor_desc(a0 + k * kUmmaK * 2),
+                    sw128_kmajor_desc(b0 + k * kUmmaK * 2), idesc, (kb | k) != 0);
+          }
+          mma_commit(&empty[s]);  // the stage is free once these MMAs finish
+        }
+        if (ok) mma_commit(&acc_full[b]);  // the tile's accumulator is complete
+      }
+      // all issued MMAs have finished before TMEM is released
+      mma_commit(drained);
+      mbar_wait_bounded(drained, 0);
+    }
+  } else {
+    const int quarter = warp & 3;  // TMEM lanes this warp may access
+    const bool has_bias = args.bias != nullptr;
+    const bool vec_ok = args.vec_ok != 0;
+    uint32_t local = 0;
+    for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
+      const uint32_t b = local & 1;
+      if (!mbar_wait_bounded(&acc_full[b], (local >> 1) & 1)) break;
+      tc_fence_after();
+      const int64_t tm = tile / n_tiles;
+      const int64_t tn = tile % n_tiles;
+      const int64_t row = tm * kBM + quarter * 32 + lane;
+      TOut* crow = static_cast<TOut*>(args.C) + row * args.ldc;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + (uint32_t(quarter * 32) << 16) + b * BN + c, r);
+        const int64_t col0 = tn * BN + c;
+        const int valid = static_cast<int>(imin64(32, args.N - col0));
+        if (valid > 0 && row < args.M) {
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            v[j] = __uint_as_float(r[j]);
+            if (has_bias && j < valid) v[j] += load_bias(args.bias, args.bias_dtype, col0 + j);
+          }
+          store_row32<TOut>(crow + col0, v, valid, vec_ok);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(L::kTmemCols));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+  });
+  return fn;
+}
+
+// 2-D map over a row-major [rows, k] matrix with leading dimension ld
+// (elements); box = 64 k-elements x box_rows rows, 128-byte swizzle.
+bool make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int64_t ld,
+              int box_rows, bool bf16) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estride[2] = {1, 1};
+  const CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        2, const_cast<void*>(ptr), dims, strides, box, estride,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+template <typename TIn, typename TOut, int BN>
+int launch(const CUtensorMap& ma, const CUtensorMap& mb_, const GemmArgs& args, cudaStream_t s) {
+  auto kern = gemm_tn_kernel<TIn, TOut, BN>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       static_cast<int>(Layout<BN>::kSmem));
+  const int64_t tiles = ((args.M + kBM - 1) / kBM) * ((args.N + BN - 1) / BN);
+  const int grid = static_cast<int>(imin64(tiles, sm_count()));
+  kern<<<grid, kThreads, Layout<BN>::kSmem, s>>>(ma, mb_, args);
+  return 0;
+}
+
+template <typename TIn, typename TOut>
+int launch_bn(const void* A, int64_t lda, const void* B, int64_t ldb, const GemmArgs& args,
+              cudaStream_t s) {
+  const bool bf16 = std::is_same<TIn, __nv_bfloat16>::value;
+  CUtensorMap ma, mbm;
+  const int bn = args.N >= 192 ? 256 : (args.N > 64 ? 128 : 64);
+  if (!make_map(&ma, A, args.M, args.K, lda, kBM, bf16) ||
+      !make_map(&mbm, B, args.N, args.K, ldb, bn, bf16)) {
+    set_error("mb_gemm_tn: cuTensorMapEncodeTiled failed (shape or alignment)");
+    return 1;
+  }
+  if (bn == 256) return launch<TIn, TOut, 256>(ma, mbm, args, s);
+  if (bn == 128) return launch<TIn, TOut, 128>(ma, mbm, args, s);
+  return launch<TIn, TOut, 64>(ma, mbm, args, s);
+}
+
+}  // namespace
+}  // namespace mb
+
+using namespace mb;
+
+extern "C" int mb_gemm_tn(int in_dtype, const void* A, int64_t lda, const void* B, int64_t ldb,
+                          const void* bias, int bias_dtype, int out_dtype, void* C, int64_t ldc,
+                          int64_t M, int64_t N, int64_t K, void* stream) {
+  clear_error();
+  MB_CHECK_ARG(in_dtype == MB_BF16 || in_dtype == MB_F16,
+               "mb_gemm_tn: inputs must be bfloat16 or float16 (got dtype %d)", in_dtype);
+  MB_CHECK_ARG(out_dtype == MB_F32 || out_dtype == in_dtype,
+               "mb_gemm_tn: output must be float32 or the input type");
+  MB_CHECK_ARG(bias == nullptr || bias_dtype == MB_F32 || bias_dtype == MB_BF16 ||
+                   bias_dtype == MB_F16,
+               "mb_gemm_tn: bias must be float32, bfloat16 or float16");
+  MB_CHECK_ARG(M >= 0 && N >= 0 && K >= 0, "mb_gemm_tn: negative size");
+  if (M == 0 || N == 0) return 0;
+  MB_CHECK_ARG(K > 0, "mb_gemm_tn: K must be positive");
+  MB_CHECK_ARG(K % 8 == 0 && lda % 8 == 0 && ldb % 8 == 0 && lda >= K && ldb >= K,
+               "mb_gemm_tn: K and leading dimensions must be multiples of 8 (16-byte rows)");
+  MB_CHECK_ARG(aligned_to(A, 16) && aligned_to(B, 16), "mb_gemm_tn: A and B must be 16-byte aligned");
+  MB_CHECK_ARG(ldc >= N, "mb_gemm_tn: ldc < N");
+  MB_CHECK_ARG(M < (int64_t(1) << 31) && N < (int64_t(1) << 31), "mb_gemm_tn: M or N too large");
+  const int64_t out_elt = out_dtype == MB_F32 ? 4 : 2;
+  GemmArgs args{bias, C, ldc, M, N, K, bias_dtype,
+                (ldc * out_elt) % 16 == 0 && aligned_to(C, 16) ? 1 : 0};
+  cudaStream_t s = as_stream(stream);
+  int rc;
+  if (in_dtype == MB_BF16) {
+    rc = out_dtype == MB_F32 ? launch_bn<__nv_bfloat16, float>(A, lda, B, ldb, args, s)
+                             : launch_bn<__nv_bfloat16, __nv_bfloat16>(A, lda, B, ldb, args, s);
+  } else {
+    rc = out_dtype == MB_F32 ? launch_bn<__half, float>(A, lda, B, ldb, args, s)
+                             : launch_bn<__half, __half>(A, lda, B, ldb, args, s);
+  }
+  if (rc != 0) return rc;
+  MB_CHECK_LAUNCH("mb_gemm_tn");
+  return 0;
+}

@@ -20,7 +20,12 @@ from typing import Literal
 import torch
 
 from myelin_b200 import _native as nat
-from myelin_b200.autograd import ALIFScanFunction, LIFScanFunction, LinearScanFunction
+from myelin_b200.autograd import (
+    ALIFScanFunction,
+    LIFScanFunction,
+    LinearScanFunction,
+    _project,
+)
 from myelin_b200.checkpointing import CheckpointSize, resolve_checkpoint_size
 from myelin_b200.neurons import ALIFParams, ALIFState, LIFParams, LIFState
 from myelin_b200.packing import PackedSpikes
@@ -405,9 +410,7 @@ def linear_surrogate_lif_packed_forward(
         T, B, F = inputs.shape
         N = weight.shape[1]
         x2 = inputs.contiguous().reshape(T * B, F)
-        w = weight.contiguous()
-        currents = torch.addmm(bias, x2, w) if bias is not None else torch.mm(x2, w)
-        currents = currents.view(T, B, N)
+        currents = _project(x2, weight.contiguous(), bias).view(T, B, N)
         v0 = torch.zeros((B, N), dtype=inputs.dtype, device=inputs.device)
         vT = torch.empty_like(v0)
         words = torch.empty((T, B, (N + 31) // 32), dtype=torch.int32, device=inputs.device)

@@ -132,3 +132,41 @@ def test_modules_train_and_match_functional():
     unrolled = mb.LinearSurrogateLIF(40, 30, stream_synapse=False).to(DEV)
     unrolled.load_state_dict(layer.state_dict())
     assert (unrolled(x) != spikes).float().mean().item() <= 1e-3
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_16bit_stream_synapse_uses_tensor_core_projection(oracle, dtype):
+    """bf16/f16 layer: projection on the tcgen05 GEMM, scan bit-exact on its currents,
+    currents and gradients against an fp32 torch reference of the same op."""
+
+    from myelin_b200.autograd import _input_grad, _project
+
+    T, B, F, N = 12, 64, 256, 320
+    gen = torch.Generator().manual_seed(5)
+    x = (torch.rand((T, B, F), generator=gen) < 0.2).to(dtype)
+    w = (torch.randn((F, N), generator=gen) * 0.15).to(dtype)
+    b = (torch.randn((N,), generator=gen) * 0.1).to(dtype)
+    xd, wd, bd = (t.to(DEV).requires_grad_(True) for t in (x, w, b))
+    params = mb.LIFParams(tau_mem=20.0, threshold=1.0, reset=0.0)
+    state, spikes = mb.linear_surrogate_lif_forward(xd, wd, bd, params, surrogate="fast_sigmoid",
+                                                    surrogate_slope=25.0)
+    cur = _project(xd.detach().reshape(T * B, F), wd.detach(), bd.detach())
+    ref_cur = (x.float().reshape(T * B, F) @ w.float() + b.float()).to(dtype)
+    assert_close_scaled(host(cur), ref_cur.float().numpy(), rtol=1e-2, what="currents")
+    kw = dict(decay=np.float32(1 - 1 / 20.0), threshold=np.float32(1.0), reset=np.float32(0.0))
+    ref = oracle.scan_forward(host(cur).reshape(T, B, N), np.zeros((B, N), np.float32), **kw)
+    assert np.array_equal(host(spikes).astype(np.uint8), ref["spikes"])
+    gs = torch.randn((T, B, N), generator=gen).to(dtype)
+    (spikes * gs.to(DEV)).sum().backward()
+    bwd = oracle.scan_backward(host(cur).reshape(T, B, N), np.zeros((B, N), np.float32),
+                               grad_spikes=gs.float().numpy(), surrogate="fast_sigmoid",
+                               slope=25.0, **kw)
+    g_ref = torch.from_numpy(bwd["grad_x"]).to(dtype).float().reshape(T * B, N)
+    dx_ref = (g_ref @ w.float().t()).reshape(T, B, F)
+    dw_ref = x.float().reshape(T * B, F).t() @ g_ref
+    assert_close_scaled(host(xd.grad), dx_ref.numpy(), rtol=3e-2, what="grad_x")
+    assert_close_scaled(host(wd.grad), dw_ref.numpy(), rtol=3e-2, what="grad_w")
+    assert_close_scaled(host(bd.grad), g_ref.sum(0).numpy(), rtol=3e-2, what="grad_b")
+    g2 = torch.randn((T * B, N), device=DEV).to(dtype)
+    assert_close_scaled(host(_input_grad(g2, wd.detach())),
+                        (g2.float() @ wd.detach().float().t()).cpu().numpy(), rtol=1e-2)
