@@ -20,6 +20,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstring>
 #include <mutex>
 #include <type_traits>
 
@@ -42,6 +43,7 @@ struct GemmArgs {
   int64_t M, N, K;
   int bias_dtype;  // MB_F32 / MB_BF16 / MB_F16
   int vec_ok;      // C rows 16-byte aligned: 16-byte stores
+  int tma_store;   // write C through smem + bulk tensor stores (tma_c valid)
 };
 
 template <int BN>
@@ -50,7 +52,11 @@ struct Layout {
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kBarrierBytes = 256;
-  static constexpr size_t kSmem = size_t(kStages) * kStageBytes + kBarrierBytes + 1024;
+  // epilogue staging: 4 warps x 2 slots x (32 rows x 32 columns x up to 4 B)
+  static constexpr int kEpiSlotBytes = 32 * 32 * 4;
+  static constexpr int kEpiBytes = 4 * 2 * kEpiSlotBytes;
+  static constexpr size_t kSmem =
+      size_t(kStages) * kStageBytes + kEpiBytes + kBarrierBytes + 1024;
   static constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
 };
 
@@ -64,6 +70,26 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
           smem_addr(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_addr(bar))
       : "memory");
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0,
+                                             int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(c0), "r"(c1), "r"(smem_addr(src))
+      : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Wait until at most N of this thread's bulk stores still read shared memory.
+template <int N>
+__device__ __forceinline__ void tma_store_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void tma_store_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 // Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of
@@ -169,16 +195,52 @@ __device__ __forceinline__ void store_row32(TOut* dst, const float (&v)[32], int
   }
 }
 
+// One lane's row of a 32 x 32 output block into a staging slot laid out as
+// the bulk tensor store expects with a 128-byte (fp32 rows) or 64-byte
+// (16-bit rows) swizzle: 16-byte chunk q of row r sits at chunk
+// q ^ (r & 7) (128 B) or q ^ ((r >> 1) & 3) (64 B), so the 32 lanes of a
+// warp writing their rows hit distinct banks.
+template <typename TOut>
+__device__ __forceinline__ void stage_row32(uint8_t* slot, int r, const float (&v)[32]) {
+  if constexpr (std::is_same<TOut, float>::value) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int pq = q ^ (r & 7);
+      *reinterpret_cast<float4*>(slot + r * 128 + pq * 16) =
+          make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint32_t w[4];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float a = v[8 * q + 2 * h], b = v[8 * q + 2 * h + 1];
+        if constexpr (std::is_same<TOut, __nv_bfloat16>::value) {
+          const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
+          w[h] = *reinterpret_cast<const uint32_t*>(&p);
+        } else {
+          const __half2 p = __floats2half2_rn(a, b);
+          w[h] = *reinterpret_cast<const uint32_t*>(&p);
+        }
+      }
+      const int pq = q ^ ((r >> 1) & 3);
+      *reinterpret_cast<uint4*>(slot + r * 64 + pq * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
 template <typename TIn, typename TOut, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                   const GemmArgs args) {
+                   const __grid_constant__ CUtensorMap tma_c, const GemmArgs args) {
   using L = Layout<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = smem;
   uint8_t* sb = smem + kStages * L::kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sb + kStages * L::kBBytes);
+  uint8_t* sepi = sb + kStages * L::kBBytes;  // epilogue staging slots (1 KB aligned)
+  uint64_t* full = reinterpret_cast<uint64_t*>(sepi + L::kEpiBytes);
   uint64_t* empty = full + kStages;
   uint64_t* acc_full = empty + kStages;  // [2]
   uint64_t* acc_empty = acc_full + 2;    // [2]
@@ -277,6 +339,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;  // TMEM lanes this warp may access
     const bool has_bias = args.bias != nullptr;
     const bool vec_ok = args.vec_ok != 0;
+    const bool use_tma = args.tma_store != 0;
+    uint8_t* slots = sepi + (warp - 2) * 2 * L::kEpiSlotBytes;
+    uint32_t nstore = 0;
     uint32_t local = 0;
     for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
       const uint32_t b = local & 1;
@@ -284,7 +349,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int64_t tm = tile / n_tiles;
       const int64_t tn = tile % n_tiles;
-      const int64_t row = tm * kBM + quarter * 32 + lane;
+      const int64_t row0 = tm * kBM + quarter * 32;
+      const int64_t row = row0 + lane;
       TOut* crow = static_cast<TOut*>(args.C) + row * args.ldc;
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
@@ -292,13 +358,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32(tmem_base + (uint32_t(quarter * 32) << 16) + b * BN + c, r);
         const int64_t col0 = tn * BN + c;
         const int valid = static_cast<int>(imin64(32, args.N - col0));
-        if (valid > 0 && row < args.M) {
-          float v[32];
+        if (valid <= 0 || row0 >= args.M) continue;  // warp-uniform
+        float v[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            v[j] = __uint_as_float(r[j]);
-            if (has_bias && j < valid) v[j] += load_bias(args.bias, args.bias_dtype, col0 + j);
-          }
+        for (int j = 0; j < 32; ++j) {
+          v[j] = __uint_as_float(r[j]);
+          if (has_bias && j < valid) v[j] += load_bias(args.bias, args.bias_dtype, col0 + j);
+        }
+        if (use_tma) {
+          // the slot used two stores ago must have been read out
+          if (lane == 0) tma_store_wait_read<1>();
+          __syncwarp();
+          uint8_t* slot = slots + (nstore & 1) * L::kEpiSlotBytes;
+          stage_row32<TOut>(slot, lane, v);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) tma_store_2d(&tma_c, slot, static_cast<int>(col0), static_cast<int>(row0));
+          ++nstore;
+        } else if (row < args.M) {
           store_row32<TOut>(crow + col0, v, valid, vec_ok);
         }
       }
@@ -306,6 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
     }
+    if (use_tma && lane == 0) tma_store_wait_all();
   }
   tc_fence_before();
   __syncthreads();
@@ -351,6 +429,26 @@ bool make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int64_
   return r == CUDA_SUCCESS;
 }
 
+// 2-D map over C[M, N] (leading dimension ldc elements) for the epilogue's
+// bulk tensor stores: box 32 x 32, swizzle matching stage_row32.
+bool make_c_map(CUtensorMap* map, void* ptr, int64_t M, int64_t N, int64_t ldc, int out_dtype) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  const int elt = out_dtype == MB_F32 ? 4 : 2;
+  if (!aligned_to(ptr, 16) || (ldc * elt) % 16 != 0) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldc * elt)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estride[2] = {1, 1};
+  const CUtensorMapDataType dt = out_dtype == MB_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : out_dtype == MB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUresult r = fn(map, dt, 2, ptr, dims, strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        elt == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 int sm_count() {
   int dev = 0, n = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
@@ -358,19 +456,20 @@ int sm_count() {
 }
 
 template <typename TIn, typename TOut, int BN>
-int launch(const CUtensorMap& ma, const CUtensorMap& mb_, const GemmArgs& args, cudaStream_t s) {
+int launch(const CUtensorMap& ma, const CUtensorMap& mb_, const CUtensorMap& mc,
+           const GemmArgs& args, cudaStream_t s) {
   auto kern = gemm_tn_kernel<TIn, TOut, BN>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        static_cast<int>(Layout<BN>::kSmem));
   const int64_t tiles = ((args.M + kBM - 1) / kBM) * ((args.N + BN - 1) / BN);
   const int grid = static_cast<int>(imin64(tiles, sm_count()));
-  kern<<<grid, kThreads, Layout<BN>::kSmem, s>>>(ma, mb_, args);
+  kern<<<grid, kThreads, Layout<BN>::kSmem, s>>>(ma, mb_, mc, args);
   return 0;
 }
 
 template <typename TIn, typename TOut>
-int launch_bn(const void* A, int64_t lda, const void* B, int64_t ldb, const GemmArgs& args,
-              cudaStream_t s) {
+int launch_bn(const void* A, int64_t lda, const void* B, int64_t ldb, GemmArgs args,
+              int out_dtype, cudaStream_t s) {
   const bool bf16 = std::is_same<TIn, __nv_bfloat16>::value;
   CUtensorMap ma, mbm;
   const int bn = args.N >= 192 ? 256 : (args.N > 64 ? 128 : 64);
@@ -379,9 +478,12 @@ int launch_bn(const void* A, int64_t lda, const void* B, int64_t ldb, const Gemm
     set_error("mb_gemm_tn: cuTensorMapEncodeTiled failed (shape or alignment)");
     return 1;
   }
-  if (bn == 256) return launch<TIn, TOut, 256>(ma, mbm, args, s);
-  if (bn == 128) return launch<TIn, TOut, 128>(ma, mbm, args, s);
-  return launch<TIn, TOut, 64>(ma, mbm, args, s);
+  CUtensorMap mc;
+  memset(&mc, 0, sizeof(mc));
+  args.tma_store = make_c_map(&mc, args.C, args.M, args.N, args.ldc, out_dtype) ? 1 : 0;
+  if (bn == 256) return launch<TIn, TOut, 256>(ma, mbm, mc, args, s);
+  if (bn == 128) return launch<TIn, TOut, 128>(ma, mbm, mc, args, s);
+  return launch<TIn, TOut, 64>(ma, mbm, mc, args, s);
 }
 
 }  // namespace
@@ -410,15 +512,15 @@ extern "C" int mb_gemm_tn(int in_dtype, const void* A, int64_t lda, const void* 
   MB_CHECK_ARG(M < (int64_t(1) << 31) && N < (int64_t(1) << 31), "mb_gemm_tn: M or N too large");
   const int64_t out_elt = out_dtype == MB_F32 ? 4 : 2;
   GemmArgs args{bias, C, ldc, M, N, K, bias_dtype,
-                (ldc * out_elt) % 16 == 0 && aligned_to(C, 16) ? 1 : 0};
+                (ldc * out_elt) % 16 == 0 && aligned_to(C, 16) ? 1 : 0, 0};
   cudaStream_t s = as_stream(stream);
   int rc;
   if (in_dtype == MB_BF16) {
-    rc = out_dtype == MB_F32 ? launch_bn<__nv_bfloat16, float>(A, lda, B, ldb, args, s)
-                             : launch_bn<__nv_bfloat16, __nv_bfloat16>(A, lda, B, ldb, args, s);
+    rc = out_dtype == MB_F32 ? launch_bn<__nv_bfloat16, float>(A, lda, B, ldb, args, out_dtype, s)
+                             : launch_bn<__nv_bfloat16, __nv_bfloat16>(A, lda, B, ldb, args, out_dtype, s);
   } else {
-    rc = out_dtype == MB_F32 ? launch_bn<__half, float>(A, lda, B, ldb, args, s)
-                             : launch_bn<__half, __half>(A, lda, B, ldb, args, s);
+    rc = out_dtype == MB_F32 ? launch_bn<__half, float>(A, lda, B, ldb, args, out_dtype, s)
+                             : launch_bn<__half, __half>(A, lda, B, ldb, args, out_dtype, s);
   }
   if (rc != 0) return rc;
   MB_CHECK_LAUNCH("mb_gemm_tn");
