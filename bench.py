@@ -6,9 +6,13 @@ N=4096, bf16 currents ~ N(0.2, 0.6), tau_mem=10 (decay 0.9), tau_adaptation=50
 (rho 0.98), beta=1.8, threshold 1, subtractive reset, checkpoint_size="memory",
 upstream spike gradient ~ N(0, 1). A step is one forward + backward pass through
 the public API (``surrogate_alif_forward`` + autograd) over one batch.
-Other workloads: ``lif_fp32`` (same shape, LIF, fp32, hard reset) and
+Other workloads: ``lif_fp32`` (same shape, LIF, fp32, hard reset),
 ``pack_count`` (config 4 shard: Bernoulli(0.05) bool [128, 1024/N, 8192] ->
-packed words + per-neuron int32 counts).
+packed words + per-neuron int32 counts), ``mlp_fp32`` (config 2: one training
+step of the 784 -> 1024 -> 10 stream-synapse LIF MLP, fp32) and ``rate_net``
+(config 5: one training step of 4 x 4096 hidden stream-synapse LIF layers and
+a 4096 -> 10 rate readout, bf16, T=100, B=512 per GPU, with the gradient
+all-reduce across ranks).
 
 Multi-GPU (torchrun, one process per GPU): every rank runs its own batch shard
 of the same size (weak scaling, no collective on the data path); the value is
@@ -212,6 +216,8 @@ def run_gpu(args) -> None:
     name = args.workload
     if name == "pack_count":
         return run_pack_count(args, world, rank, local)
+    if name in ("mlp_fp32", "rate_net"):
+        return run_network(args, world, rank, local)
     x, gs, forward = scan_workload(name, rank)
     x.requires_grad_(True)
     stream = torch.cuda.current_stream()
@@ -328,8 +334,140 @@ def run_gpu(args) -> None:
         print(json.dumps(result), flush=True)
 
 
+def build_network(name: str, device: str, seed: int):
+    """Config-2 / config-5 models with seeded Kaiming-uniform weights ([in, out] layout)."""
+
+    import myelin_b200 as mb
+
+    torch.manual_seed(seed)
+    if name == "mlp_fp32":
+        params = mb.LIFParams(tau_mem=20.0, threshold=1.0, reset=0.0)
+        layers = [mb.LinearSurrogateLIF(784, 1024, params, surrogate=mb.fast_sigmoid_surrogate,
+                                        surrogate_slope=25.0, stream_synapse=True),
+                  mb.LinearSurrogateLIF(1024, 10, params, surrogate=mb.fast_sigmoid_surrogate,
+                                        surrogate_slope=25.0, stream_synapse=True)]
+        dtype = torch.float32
+    else:
+        params = mb.LIFParams(tau_mem=20.0, threshold=1.0, reset=0.0)
+        layers = [mb.LinearSurrogateLIF(f, 4096, params, surrogate=mb.superspike_surrogate,
+                                        surrogate_slope=10.0, stream_synapse=True)
+                  for f in (2048, 4096, 4096, 4096)]
+        layers.append(mb.LinearSurrogateLIFRate(4096, 10, params, surrogate=mb.superspike_surrogate,
+                                                surrogate_slope=10.0, reduction="none"))
+        dtype = torch.bfloat16
+    model = torch.nn.Sequential(*layers)
+    for layer in layers:
+        w = torch.empty(layer.synapse.weight.shape[::-1])
+        torch.nn.init.kaiming_uniform_(w, a=5 ** 0.5)
+        fan_in = w.shape[1]
+        with torch.no_grad():
+            layer.synapse.weight.copy_(w.t())
+            layer.synapse.bias.uniform_(-1 / fan_in ** 0.5, 1 / fan_in ** 0.5)
+    return model.to(device=device, dtype=dtype), dtype
+
+
+def run_network(args, world, rank, local) -> None:
+    """One training step of config 2 (fp32 MLP) or config 5 (bf16 rate network)."""
+
+    from myelin_b200 import _native as nat
+
+    name = args.workload
+    model, dtype = build_network(name, "cuda", 0)
+    gen = torch.Generator(device="cuda").manual_seed(100 + rank)
+    if name == "mlp_fp32":
+        T, B, F = 25, 256, 784
+        x = (torch.rand((T, B, F), generator=gen, device="cuda") < 0.2).to(dtype)
+        labels = torch.randint(0, 10, (B,), generator=gen, device="cuda")
+
+        def loss_fn():
+            counts = model(x).sum(dim=0)
+            return torch.nn.functional.cross_entropy(counts, labels)
+
+        neurons = 1024 + 10
+    else:
+        T, B, F = 100, 512, 2048
+        x = (torch.rand((T, B, F), generator=gen, device="cuda") < 0.1).to(dtype)
+        target = torch.rand((B, 10), generator=gen, device="cuda").mul(0.3).to(dtype)
+
+        def loss_fn():
+            return torch.nn.functional.mse_loss(model(x).float(), target.float())
+
+        neurons = 4 * 4096 + 10
+    params = [p for p in model.parameters()]
+    flat = torch.empty(sum(p.numel() for p in params), dtype=torch.float32, device="cuda")
+    opt = torch.optim.SGD(params, lr=1e-3)
+
+    def step():
+        opt.zero_grad(set_to_none=True)
+        loss = loss_fn()
+        loss.backward()
+        if world > 1:
+            import torch.distributed as dist
+
+            torch.cat([p.grad.reshape(-1).float() for p in params], out=flat)
+            dist.all_reduce(flat, op=dist.ReduceOp.SUM)
+            flat.div_(world)
+            offset = 0
+            for p in params:
+                n = p.numel()
+                p.grad.copy_(flat[offset:offset + n].view_as(p))
+                offset += n
+        opt.step()
+        return loss
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(args.steps):
+            loss = step()
+        stop.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+    ms = max_over_ranks(start.elapsed_time(stop), world) / args.steps
+    units = T * B * neurons
+    flops = 0
+    for layer in model:
+        fi, fo = layer.synapse.weight.shape
+        flops += 2 * T * B * fi * fo * 3  # forward projection, input grad, weight grad
+    result = {
+        "metric": "LIF/ALIF fwd+bwd neuron-timesteps/s (training step)",
+        "value": units * world / (ms / 1e3), "unit": "neuron-steps/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32" if name == "mlp_fp32" else "bf16", "data": "synthetic Bernoulli spikes",
+        "config": {"workload": name + (" (BASELINE config 2)" if name == "mlp_fp32" else
+                                       " (BASELINE config 5)"),
+                   "T": T, "B_per_gpu": B, "global_batch": B * world, "F": F,
+                   "parallelism": f"dp{world} (gradient all-reduce, NCCL)" if world > 1 else "dp1"},
+        "tflops_per_gpu": round(flops / (ms / 1e3) / 1e12, 1),
+        "loss": float(loss.item()),
+        "device_status": nat.device_status(clear=True),
+    }
+    clk = clocks.summary()
+    if clk is not None:
+        result["clocks"] = clk
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
 def run_pack_count(args, world, rank, local) -> None:
-    """BASELINE config 4 shard: pack [128, 1024/world, 8192] bool spikes + int32 column counts."""
+    """Bernoulli(0.05) spikes [128, 1024, 8192], batch sharded over ranks.
+
+    A step packs this rank's [128, 1024/world, 8192] spikes into int32 words,
+    counts spikes per neuron (int32, summed over T and the local batch), then
+    all-gathers the packed words and all-reduces the counts (NCCL over NVLink).
+    """
 
     import myelin_b200 as mb
     from myelin_b200 import _native as nat
@@ -338,39 +476,59 @@ def run_pack_count(args, world, rank, local) -> None:
     gen = torch.Generator(device="cuda").manual_seed(77 + rank)
     spikes = torch.rand((T, B, N), generator=gen, device="cuda") < 0.05
     stream = torch.cuda.current_stream()
+    gather_buf = torch.empty((world, T, B, N // 32), dtype=torch.int32, device="cuda")
+    if world > 1:
+        import torch.distributed as dist
 
     def step():
         packed = mb.pack_spikes(spikes)
-        mb.packed_spike_counts_over_leading_dims(packed, dtype=torch.int32)
+        counts = mb.packed_spike_counts_over_leading_dims(packed, dtype=torch.int32)
+        if world > 1:
+            mb.packed_spike_all_gather_into_tensor(packed, out=gather_buf)
+            dist.all_reduce(counts, op=dist.ReduceOp.SUM)
+        return counts
 
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    start.record(stream)
-    for _ in range(args.steps):
-        step()
-    stop.record(stream)
-    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(args.steps):
+            counts = step()
+        stop.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
     ms = max_over_ranks(start.elapsed_time(stop), world) / args.steps
+    total = int(counts.sum().item())
     units = T * B * N
     peak, peak_kind = load_peak_hbm()
-    algo = units * (1 + 0.125) + units * 0.125  # read bool, write words, re-read words
-    achieved = algo / (ms / 1e3) / 1e9
+    # pack kernel: read 1 B bool + write 1/8 B per spike; count kernel: re-read the words
+    algo = units * (1 + 0.125) + units * 0.125
+    words_bytes = units // 8
     result = {
-        "metric": "packed spikes/s (pack + per-neuron count)", "value": units * world / (ms / 1e3),
-        "unit": "spikes/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "u8", "data": "synthetic Bernoulli(0.05)",
-        "config": {"workload": "pack_count (BASELINE config 4 shard)", "T": T, "B_per_gpu": B, "N": N},
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None},
+        "metric": "spikes/s (pack + per-neuron count + packed all-gather + count all-reduce)",
+        "value": units * world / (ms / 1e3), "unit": "spikes/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+        "vs_baseline": None, "dtype": "u8", "data": "synthetic Bernoulli(0.05)",
+        "config": {"workload": "pack_count (BASELINE config 4)", "T": T, "B_total": B * world,
+                   "B_per_gpu": B, "N": N, "parallelism": f"dp{world} (batch-sharded)"},
+        "allgather_busbw_gbs": (round(words_bytes * world * (world - 1) / world / (ms / 1e3) / 1e9, 1)
+                                if world > 1 else None),
+        "roofline": {"bound": "hbm", "achieved": round(algo / (ms / 1e3) / 1e9, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(algo / (ms / 1e3) / 1e9 / peak, 4),
+                     "peak_kind": peak_kind, "traffic": None,
+                     "note": "pack+count bytes over the whole step (collectives included)"},
+        "spike_count_check": total,
         "gpu_launches": 3 * args.steps, "device_status": nat.device_status(clear=True),
     }
+    clk = clocks.summary()
+    if clk is not None:
+        result["clocks"] = clk
     if world > 1:
-        import torch.distributed as dist
-
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
@@ -427,7 +585,7 @@ def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    name = args.workload if args.workload != "pack_count" else "alif_bf16"
+    name = args.workload if args.workload in ("alif_bf16", "lif_fp32") else "alif_bf16"
     rows = 4
     step, units, threads = _oracle_sample(name, rows)
     for _ in range(args.warmup):
@@ -464,7 +622,8 @@ def main() -> None:
     parser.add_argument("--steps", type=int, default=50)
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("mine", "reference"), default="mine")
-    parser.add_argument("--workload", choices=("alif_bf16", "lif_fp32", "pack_count"),
+    parser.add_argument("--workload",
+                        choices=("alif_bf16", "lif_fp32", "pack_count", "mlp_fp32", "rate_net"),
                         default="alif_bf16")
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--no-cpu-baseline", action="store_true")

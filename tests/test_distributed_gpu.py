@@ -1,0 +1,80 @@
+"""Packed collectives over NCCL on 2 GPUs (skipped with fewer devices).
+
+Each rank packs its own seeded Bernoulli spikes with the CUDA kernel; the
+all-gather must return every rank's words bit for bit in rank order, and the
+count all-reduce must equal the per-neuron counts of all ranks' spikes.
+"""
+
+from __future__ import annotations
+
+import multiprocessing
+import os
+from pathlib import Path
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _rank_spikes(rank: int) -> torch.Tensor:
+    gen = torch.Generator().manual_seed(900 + rank)
+    return torch.rand((16, 8, 256), generator=gen) < 0.1
+
+
+def _worker(rank: int, world: int, init: str, queue) -> None:
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=init, rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    try:
+        import myelin_b200 as mb
+
+        packed = mb.pack_spikes(_rank_spikes(rank).cuda())
+        gathered = mb.packed_spike_all_gather(packed)
+        ok = len(gathered) == world
+        for r, item in enumerate(gathered):
+            ref = mb.pack_spikes(_rank_spikes(r).cuda())
+            ok = ok and torch.equal(item.data, ref.data) and item.original_shape == ref.original_shape
+        counts = mb.packed_spike_count_all_reduce(packed, dim=(0, 1))
+        expected = sum(_rank_spikes(r).sum(dim=(0, 1)) for r in range(world)).cuda()
+        ok = ok and counts.dtype == torch.int64 and torch.equal(counts, expected)
+        rows = mb.packed_spike_count_all_reduce(packed, dim=-1)
+        ok = ok and torch.equal(rows, sum(_rank_spikes(r).sum(-1) for r in range(world)).cuda())
+        rate = mb.packed_spike_rate_all_reduce(packed)
+        total = float(sum(_rank_spikes(r).sum() for r in range(world)))
+        ok = ok and abs(rate.item() - total / (16 * 8 * 256 * world)) < 1e-7
+        torch.cuda.synchronize()
+        queue.put((rank, bool(ok), ""))
+    except Exception as exc:
+        queue.put((rank, False, f"{type(exc).__name__}: {exc}"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_packed_collectives_over_nccl(tmp_path: Path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    world = 2
+    ctx = multiprocessing.get_context("spawn")
+    queue = ctx.Queue()
+    init = f"file://{tmp_path / 'rdzv'}"
+    procs = [ctx.Process(target=_worker, args=(r, world, init, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    failures = []
+    for p in procs:
+        p.join(timeout=180)
+        if p.is_alive():
+            p.terminate()
+            failures.append(f"rank {p.pid} timed out")
+    results = []
+    while not queue.empty():
+        results.append(queue.get(timeout=1))
+    failures += [m for _, ok, m in results if not ok]
+    if len(results) != world:
+        failures.append(f"expected {world} results, got {len(results)}")
+    assert not failures, failures
