@@ -138,7 +138,8 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+// Issue a 32-column TMEM load of this warp's 32 lanes; complete it with tmem_wait_ld().
+__device__ __forceinline__ void tmem_ld32_issue(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -150,7 +151,50 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
         "=r"(r[31])
       : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// bias[j0 .. j0+31] as floats; 16-byte loads when the run is complete and aligned
+// (all lanes read the same addresses: one broadcast per load).
+__device__ __forceinline__ void load_bias32(const void* bias, int dtype, int64_t j0, int valid,
+                                            float (&bv)[32]) {
+  if (dtype == MB_F32) {
+    const float* p = static_cast<const float*>(bias) + j0;
+    if (valid == 32 && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 f = __ldg(reinterpret_cast<const float4*>(p) + q);
+        bv[4 * q] = f.x; bv[4 * q + 1] = f.y; bv[4 * q + 2] = f.z; bv[4 * q + 3] = f.w;
+      }
+      return;
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) bv[j] = j < valid ? __ldg(p + j) : 0.0f;
+    return;
+  }
+  const uint16_t* p = static_cast<const uint16_t*>(bias) + j0;
+  const bool is_bf16 = dtype == MB_BF16;
+  auto cvt = [is_bf16](uint32_t h) {
+    return is_bf16 ? __uint_as_float(h << 16) : __half2float(__ushort_as_half(uint16_t(h)));
+  };
+  if (valid == 32 && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(p) + q);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        bv[8 * q + 2 * h] = cvt(w[h] & 0xffffu);
+        bv[8 * q + 2 * h + 1] = cvt(w[h] >> 16);
+      }
+    }
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) bv[j] = j < valid ? cvt(p[j]) : 0.0f;
 }
 
 __device__ __forceinline__ float load_bias(const void* bias, int dtype, int64_t j) {
@@ -341,6 +385,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool vec_ok = args.vec_ok != 0;
     const bool use_tma = args.tma_store != 0;
     uint8_t* slots = sepi + (warp - 2) * 2 * L::kEpiSlotBytes;
+    constexpr int kSlotBytes = 32 * 32 * int(sizeof(TOut));
+    constexpr int kSlots = 2 * L::kEpiSlotBytes / kSlotBytes;  // 2 (fp32) or 4 (16-bit)
     uint32_t nstore = 0;
     uint32_t local = 0;
     for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
@@ -352,24 +398,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t row0 = tm * kBM + quarter * 32;
       const int64_t row = row0 + lane;
       TOut* crow = static_cast<TOut*>(args.C) + row * args.ldc;
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(tmem_base + (uint32_t(quarter * 32) << 16) + b * BN + c, r);
+      const uint32_t tbase = tmem_base + (uint32_t(quarter * 32) << 16) + b * BN;
+      uint32_t r[2][32];
+      tmem_ld32_issue(tbase, r[0]);
+#pragma unroll
+      for (int ci = 0; ci < BN / 32; ++ci) {
+        const int c = ci * 32;
+        tmem_wait_ld();  // chunk ci has landed
+        if (ci + 1 < BN / 32) tmem_ld32_issue(tbase + c + 32, r[(ci + 1) & 1]);  // overlap the next
+        const uint32_t(&rc)[32] = r[ci & 1];
         const int64_t col0 = tn * BN + c;
         const int valid = static_cast<int>(imin64(32, args.N - col0));
         if (valid <= 0 || row0 >= args.M) continue;  // warp-uniform
         float v[32];
+        if (has_bias) {
+          float bv[32];
+          load_bias32(args.bias, args.bias_dtype, col0, valid, bv);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          v[j] = __uint_as_float(r[j]);
-          if (has_bias && j < valid) v[j] += load_bias(args.bias, args.bias_dtype, col0 + j);
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(rc[j]) + bv[j];
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(rc[j]);
         }
         if (use_tma) {
-          // the slot used two stores ago must have been read out
-          if (lane == 0) tma_store_wait_read<1>();
+          // the slot used kSlots stores ago must have been read out
+          if (lane == 0) tma_store_wait_read<kSlots - 1>();
           __syncwarp();
-          uint8_t* slot = slots + (nstore & 1) * L::kEpiSlotBytes;
+          uint8_t* slot = slots + (nstore % kSlots) * kSlotBytes;
           stage_row32<TOut>(slot, lane, v);
           fence_proxy_async_smem();
           __syncwarp();
