@@ -26,6 +26,7 @@
 
 #include "async_copy.cuh"
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace mb {
 namespace {
@@ -452,20 +453,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess) {
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    }
-  });
-  return fn;
-}
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() { return tma_encode_fn(); }
 
 // 2-D map over a row-major [rows, k] matrix with leading dimension ld
 // (elements); box = 64 k-elements x box_rows rows, 128-byte swizzle.

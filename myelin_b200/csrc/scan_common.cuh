@@ -107,7 +107,7 @@ __device__ __forceinline__ float surrogate_grad(float c) {
 template <int SURR>
 struct SurrogateD {
   float k0, k1;
-  __device__ __forceinline__ explicit SurrogateD(float slope) {
+  __host__ __device__ __forceinline__ explicit SurrogateD(float slope) {
     if (SURR == MB_SURR_ATAN) {
       k0 = 1.5707963267948966f * slope;  // u = (pi/2) * slope * diff
       k1 = 0.5f * slope;                 // d = 0.5 * slope / (1 + u^2)
@@ -178,6 +178,108 @@ struct Pair<__half> {
   }
   static __device__ __forceinline__ uint32_t spikes(bool s0, bool s1) {
     return (s0 ? 0x00003c00u : 0u) | (s1 ? 0x3c000000u : 0u);
+  }
+};
+
+// ---------------------------------------------------------------------------
+// Two fp32 lanes (a float2) operated on by the sm_100 packed instructions
+// through the builtins __fadd2_rn / __fmul2_rn / __ffma2_rn: one instruction
+// for both lanes, each lane rounded like the scalar __fadd_rn / __fmul_rn /
+// __fmaf_rn. A packed product followed by a packed sum is contracted into a
+// fused multiply-add by the compiler (measured on B200 with CUDA 12.9 for the
+// builtins and for PTX mul.rn/add.rn .f32x2 alike, despite the explicit
+// rounding modes), while a scalar __fmul_rn is never merged. So the bit-exact
+// neuron step multiplies lane by lane (mul2_exact) and adds in pairs.
+// ---------------------------------------------------------------------------
+using F2 = float2;
+
+__device__ __forceinline__ F2 f2(float lo, float hi) { return make_float2(lo, hi); }
+__device__ __forceinline__ F2 f2(float both) { return make_float2(both, both); }
+__device__ __forceinline__ F2 f2(float2 v) { return v; }
+__device__ __forceinline__ float2 split(F2 x) { return x; }
+__device__ __forceinline__ F2 add2(F2 a, F2 b) { return __fadd2_rn(a, b); }
+// a - b == a + (-b) exactly (negation is exact)
+__device__ __forceinline__ F2 sub2(F2 a, F2 b) { return __fadd2_rn(a, make_float2(-b.x, -b.y)); }
+__device__ __forceinline__ F2 mul2(F2 a, F2 b) { return __fmul2_rn(a, b); }
+// a * b + c, one rounding per lane
+__device__ __forceinline__ F2 fma2(F2 a, F2 b, F2 c) { return __ffma2_rn(a, b, c); }
+// a * b per lane with the scalar __fmul_rn, which is never merged into a
+// fused multiply-add (see the note above)
+__device__ __forceinline__ F2 mul2_exact(F2 a, F2 b) {
+  return make_float2(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y));
+}
+// 1.0f where a >= b, else 0.0f (NaN compares false)
+__device__ __forceinline__ float ge_f(float a, float b) {
+  float r;
+  asm("set.ge.f32.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+// 1.0f where a < b, else 0.0f (NaN compares false)
+__device__ __forceinline__ float lt_f(float a, float b) {
+  float r;
+  asm("set.lt.f32.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+// Approximate reciprocal (PTX rcp.approx: max 1 ulp error, subnormals flushed).
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+// Step for a pair of neurons: per lane the same operations and roundings as
+// Step, so membranes and spike decisions are bit-identical. It works with the
+// negated threshold nth = -theta (exact: fl(-thr + fl(-beta * a)) is
+// -fl(thr + fl(beta * a))), so that p - theta = p + nth needs no negation.
+template <int KIND, int RESET>
+struct Step2 {
+  F2 p;     // pre-reset membranes
+  F2 nth;   // minus the thresholds used this step
+  F2 diff;  // p - theta (subtractive reset only)
+  bool s0, s1;
+  __device__ __forceinline__ void run(F2& m, F2& a, F2 x, const F2 decay, const F2 nthr,
+                                      const float reset_v, const F2 adapt_decay,
+                                      const F2 nbeta) {
+    p = add2(mul2_exact(m, decay), x);
+    nth = (KIND == MB_ALIF) ? add2(nthr, mul2_exact(nbeta, a)) : nthr;
+    s0 = p.x >= -nth.x;
+    s1 = p.y >= -nth.y;
+    if (RESET == MB_RESET_HARD) {
+      m = f2(s0 ? reset_v : p.x, s1 ? reset_v : p.y);
+    } else {
+      diff = add2(p, nth);
+      m = f2(s0 ? diff.x : p.x, s1 ? diff.y : p.y);
+    }
+    if (KIND == MB_ALIF) {
+      a = add2(mul2_exact(a, adapt_decay), f2(s0 ? 1.0f : 0.0f, s1 ? 1.0f : 0.0f));
+    }
+  }
+};
+
+// SurrogateD on a pair of differences p - theta; k0, k1 are SurrogateD's
+// constants in both lanes, `one` is 1.0f in both lanes.
+template <int SURR>
+struct SurrogateD2 {
+  SurrogateD<SURR> scalar;
+  F2 k0, k1, one;
+  __device__ __forceinline__ SurrogateD2(float slope, F2 k0_, F2 k1_, F2 one_)
+      : scalar(slope), k0(k0_), k1(k1_), one(one_) {}
+  __device__ __forceinline__ F2 operator()(F2 diff) const {
+    if constexpr (SURR == MB_SURR_ATAN) {
+      const F2 u = mul2(k0, diff);
+      const float2 dn = split(fma2(u, u, one));
+      return mul2(k1, f2(rcp_approx(dn.x), rcp_approx(dn.y)));
+    } else if constexpr (SURR == MB_SURR_FAST_SIGMOID || SURR == MB_SURR_SUPERSPIKE) {
+      const float2 u = split(mul2(k0, diff));
+      const F2 dn = add2(one, f2(fabsf(u.x), fabsf(u.y)));
+      const float2 dd = split(mul2(dn, dn));
+      return mul2(k1, f2(rcp_approx(dd.x), rcp_approx(dd.y)));
+    } else if constexpr (SURR == MB_SURR_NONE) {
+      return f2(0.0f);
+    } else {
+      const float2 df = split(diff);
+      return f2(scalar(df.x), scalar(df.y));
+    }
   }
 };
 

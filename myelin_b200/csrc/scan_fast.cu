@@ -13,11 +13,14 @@
 // two 32-neuron words per warp), and at each chunk start the fp32 checkpoint.
 // Backward: chunks run last to first; each is replayed from its checkpoint
 // into registers (bit-identical to the forward) and then walked in reverse.
+#include <climits>
+#include <cstring>
 #include <initializer_list>
 
 #include "async_copy.cuh"
 #include "common.cuh"
 #include "scan_common.cuh"
+#include "tma.cuh"
 
 namespace mb {
 
@@ -31,7 +34,7 @@ constexpr int kBwdRing = 3;                      // stages in flight, backward
 
 template <typename T>
 __host__ __device__ constexpr size_t fwd_smem() {
-  return size_t(kFwdRing) * kChunk * kTileN * sizeof(T) + 2 * kFwdRing * sizeof(uint64_t);
+  return size_t(kFwdRing) * kChunk * kTileN * sizeof(T) + 3 * kFwdRing * sizeof(uint64_t);
 }
 
 // Backward stage: kChunk rows of x, kChunk rows of grad_spikes, then the fp32
@@ -43,7 +46,7 @@ __host__ __device__ constexpr size_t bwd_stage_bytes() {
 
 template <typename T>
 __host__ __device__ constexpr size_t bwd_smem() {
-  return size_t(kBwdRing) * bwd_stage_bytes<T>() + 2 * kBwdRing * sizeof(uint64_t);
+  return size_t(kBwdRing) * bwd_stage_bytes<T>() + 3 * kBwdRing * sizeof(uint64_t);
 }
 
 // Output modes of the forward (what the caller asked for), fixed at compile
@@ -52,6 +55,30 @@ __host__ __device__ constexpr size_t bwd_smem() {
 enum FwdMode { kFwdDense = 0, kFwdPacked = 1, kFwdRates = 2, kFwdAny = 3 };
 // Backward inputs: spike gradients, rate gradients, or any combination.
 enum BwdMode { kBwdSpikes = 0, kBwdRates = 1, kBwdAny = 2 };
+
+// Resident CTAs per SM the backward is compiled for: ALIF keeps two state
+// adjoints and replays two state variables, and the exp-based surrogates
+// (sigmoid, multi-Gaussian) hold more temporaries; fewer CTAs give them
+// registers enough not to spill.
+constexpr int bwd_min_blocks(int kind, int surr) {
+  return kind == MB_LIF ? 4 : (surr == MB_SURR_SIGMOID || surr == MB_SURR_MULTI_GAUSSIAN ? 2 : 3);
+}
+
+// Per-launch fp32 constants, each duplicated into both lanes of a float2 for
+// the packed instructions; passed as a kernel parameter.
+struct PairConsts {
+  float2 decay, nthr, adapt_decay, nbeta, reset, k0, k1, one;
+};
+
+inline float2 dup2(float v) { return make_float2(v, v); }
+
+template <int SURR>
+PairConsts pair_consts(float decay, float thr, float adapt_decay, float beta, float reset,
+                       float slope) {
+  const SurrogateD<SURR> sd(slope);
+  return PairConsts{dup2(decay), dup2(-thr), dup2(adapt_decay), dup2(-beta), dup2(reset),
+                    dup2(sd.k0), dup2(sd.k1), dup2(1.0f)};
+}
 
 template <typename T>
 __device__ __forceinline__ void queue_chunk_rows(T* dst, const T* src, int64_t t0, int len,
@@ -62,28 +89,55 @@ __device__ __forceinline__ void queue_chunk_rows(T* dst, const T* src, int64_t t
   }
 }
 
+// A compute thread's part in writing a finished stage back to global memory.
+// Every compute thread orders its shared-memory writes for the async proxy;
+// each warp then arrives on `done`; thread 0 waits (bounded) for all warps,
+// issues one bulk tensor store of the stage at (c0, c1), waits until the
+// store has read the stage, and releases it on `empty` (count 1). Returns
+// false if the wait ran out (status recorded).
+__device__ __forceinline__ bool store_stage(const void* stage, uint64_t* done, uint64_t* empty,
+                                            int64_t use, int ring, const CUtensorMap* map,
+                                            int64_t c0, int64_t c1) {
+  fence_proxy_async_smem();
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(done);
+  if (threadIdx.x == 0) {
+    if (!mbar_wait_bounded(done, static_cast<uint32_t>((use / ring) & 1))) return false;
+    tma_store_box_2d(map, stage, static_cast<int>(c0), static_cast<int>(c1));
+    bulk_wait_read_all();
+    mbar_arrive(empty);
+  }
+  return true;
+}
+
 // ---------------------------------------------------------------------------
 // Forward
 // ---------------------------------------------------------------------------
 template <typename T, int KIND, int RESET, int MODE>
-__global__ void __launch_bounds__(kThreads) scan_fwd_fast_kernel(const ScanFwdArgs a) {
+__global__ void __launch_bounds__(kThreads, 6) scan_fwd_fast_kernel(
+    const ScanFwdArgs a, const PairConsts c, const __grid_constant__ CUtensorMap out_map) {
   using P = Pair<T>;
   using V = typename P::V;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   T* ring = reinterpret_cast<T*>(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + size_t(kFwdRing) * kChunk * kTileN * sizeof(T));
   uint64_t* empty = full + kFwdRing;
+  uint64_t* done = empty + kFwdRing;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t e0 = int64_t(blockIdx.x) * kTileN;
   const int tile_n = static_cast<int>(imin64(kTileN, a.BN - e0));
   const int64_t K = (a.T + kChunk - 1) / kChunk;
+  constexpr bool kDense = MODE == kFwdDense || MODE == kFwdAny;
+  const bool do_dense = kDense && (MODE != kFwdAny || a.spikes != nullptr);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kFwdRing; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
+      // with dense output the stage is released by the thread that stores it
+      mbar_init(&empty[s], do_dense ? 1 : kConsumerWarps);
+      mbar_init(&done[s], kConsumerWarps);
     }
     fence_barrier_init();
   }
@@ -112,29 +166,23 @@ __global__ void __launch_bounds__(kThreads) scan_fwd_fast_kernel(const ScanFwdAr
   const int tid = threadIdx.x;  // 0 .. 32*kConsumerWarps-1
   const bool valid = 2 * tid < tile_n;  // tile_n is even
   const int64_t e = e0 + 2 * tid;
-  const int64_t half_bn = a.BN >> 1;  // BN is even on this path
-
-  float m0 = 0.f, m1 = 0.f, ad0 = 0.f, ad1 = 0.f;
+  F2 m = f2(0.0f), ad = f2(0.0f);
   int c0 = 0, c1 = 0;
   if (valid) {
-    const float2 v = P::to_f2(reinterpret_cast<const V*>(a.v0)[e >> 1]);
-    m0 = v.x;
-    m1 = v.y;
-    if (KIND == MB_ALIF) {
-      const float2 av = P::to_f2(reinterpret_cast<const V*>(a.a0)[e >> 1]);
-      ad0 = av.x;
-      ad1 = av.y;
-    }
+    m = f2(P::to_f2(reinterpret_cast<const V*>(a.v0)[e >> 1]));
+    if (KIND == MB_ALIF) ad = f2(P::to_f2(reinterpret_cast<const V*>(a.a0)[e >> 1]));
   }
-  const float decay = a.decay, thr = a.threshold, reset_v = a.reset;
-  const float adapt_decay = a.adapt_decay, beta = a.beta;
+  const F2 decay = c.decay, nthr = c.nthr, adapt_decay = c.adapt_decay, nbeta = c.nbeta;
+  const float reset_v = a.reset;
 
-  constexpr bool kDense = MODE == kFwdDense || MODE == kFwdAny;
   constexpr bool kPacked = MODE == kFwdPacked || MODE == kFwdAny;
   constexpr bool kRates = MODE == kFwdRates || MODE == kFwdAny;
-  const bool do_dense = kDense && (MODE != kFwdAny || a.spikes != nullptr);
   const bool do_packed = kPacked && (MODE != kFwdAny || a.packed != nullptr);
-  V* sp = do_dense ? reinterpret_cast<V*>(a.spikes) + (e >> 1) : nullptr;
+  // Dense spikes overwrite the x values they came from in the stage (each
+  // thread its own pair); when all compute warps are done with a chunk, one
+  // thread writes the whole stage [16 rows x 256 neurons] with one bulk tensor
+  // store (clipped at the tensor's edges) and then releases the stage. The
+  // per-step global store and its address arithmetic disappear.
   // packed words: this warp's 64 neurons are flat words q and q+1; with
   // N % 32 == 0 every word lies wholly inside or wholly outside the tile
   const int64_t words_per_t = a.BN >> 5;
@@ -143,22 +191,17 @@ __global__ void __launch_bounds__(kThreads) scan_fwd_fast_kernel(const ScanFwdAr
   const bool pk_lane = (lane & 15) == 0 && (q << 5) < a.BN;
   const int sh = lane & 16;  // lanes 0-15 -> word q, lanes 16-31 -> word q+1
 
-  auto step = [&](V xv) {
-    const float2 xf = P::to_f2(xv);
-    Step<KIND, RESET> s0, s1;
-    s0.run(m0, ad0, xf.x, decay, thr, reset_v, adapt_decay, beta);
-    s1.run(m1, ad1, xf.y, decay, thr, reset_v, adapt_decay, beta);
+  auto step = [&](V* slot) {
+    Step2<KIND, RESET> st;
+    st.run(m, ad, f2(P::to_f2(*slot)), decay, nthr, reset_v, adapt_decay, nbeta);
     if (kRates) {
-      c0 += s0.s ? 1 : 0;
-      c1 += s1.s ? 1 : 0;
+      c0 += st.s0 ? 1 : 0;
+      c1 += st.s1 ? 1 : 0;
     }
-    if (kDense && (MODE != kFwdAny || sp != nullptr)) {
-      if (valid) *sp = P::spikes(s0.s, s1.s);
-      sp += half_bn;
-    }
+    if (kDense && (MODE != kFwdAny || do_dense)) *slot = P::spikes(st.s0, st.s1);
     if (kPacked && (MODE != kFwdAny || pk != nullptr)) {
-      const uint32_t even = __ballot_sync(0xffffffffu, s0.s);
-      const uint32_t odd = __ballot_sync(0xffffffffu, s1.s);
+      const uint32_t even = __ballot_sync(0xffffffffu, st.s0);
+      const uint32_t odd = __ballot_sync(0xffffffffu, st.s1);
       const uint32_t word = spread_even_bits(even >> sh) | (spread_even_bits(odd >> sh) << 1);
       if (pk_lane) *pk = static_cast<int32_t>(word);
       pk += words_per_t;
@@ -167,26 +210,38 @@ __global__ void __launch_bounds__(kThreads) scan_fwd_fast_kernel(const ScanFwdAr
 
   for (int64_t k = 0; k < K; ++k) {
     const int s = static_cast<int>(k % kFwdRing);
-    if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>((k / kFwdRing) & 1))) return;
-    if (a.ckpt_v != nullptr && valid) {
-      reinterpret_cast<float2*>(a.ckpt_v + k * a.BN)[e >> 1] = make_float2(m0, m1);
-      if (KIND == MB_ALIF) reinterpret_cast<float2*>(a.ckpt_a + k * a.BN)[e >> 1] = make_float2(ad0, ad1);
+    if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>((k / kFwdRing) & 1))) {
+      bulk_wait_all();  // stores of earlier chunks finish before the early exit
+      return;
     }
-    const V* row = reinterpret_cast<const V*>(ring + s * kChunk * kTileN) + tid;
+    if (a.ckpt_v != nullptr && valid) {
+      reinterpret_cast<float2*>(a.ckpt_v + k * a.BN)[e >> 1] = split(m);
+      if (KIND == MB_ALIF) reinterpret_cast<float2*>(a.ckpt_a + k * a.BN)[e >> 1] = split(ad);
+    }
+    T* stage = ring + s * kChunk * kTileN;
+    V* row = reinterpret_cast<V*>(stage) + tid;
     const int len = static_cast<int>(imin64(kChunk, a.T - k * kChunk));
     if (len == kChunk) {
 #pragma unroll
-      for (int j = 0; j < kChunk; ++j) step(row[j * (kTileN / 2)]);
+      for (int j = 0; j < kChunk; ++j) step(row + j * (kTileN / 2));
     } else {
-      for (int j = 0; j < len; ++j) step(row[j * (kTileN / 2)]);
+      for (int j = 0; j < len; ++j) step(row + j * (kTileN / 2));
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
+    if (kDense && (MODE != kFwdAny || do_dense)) {
+      if (!store_stage(stage, &done[s], &empty[s], k, kFwdRing, &out_map, e0, k * kChunk)) {
+        bulk_wait_all();
+        return;
+      }
+    } else {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
   }
+  if (kDense && (MODE != kFwdAny || do_dense)) bulk_wait_all();
 
   if (!valid) return;
-  if (a.vT) reinterpret_cast<V*>(a.vT)[e >> 1] = P::from_f2(m0, m1);
-  if (KIND == MB_ALIF && a.aT) reinterpret_cast<V*>(a.aT)[e >> 1] = P::from_f2(ad0, ad1);
+  if (a.vT) reinterpret_cast<V*>(a.vT)[e >> 1] = P::from_f2(split(m).x, split(m).y);
+  if (KIND == MB_ALIF && a.aT) reinterpret_cast<V*>(a.aT)[e >> 1] = P::from_f2(split(ad).x, split(ad).y);
   if (kRates && a.rates) {
     const float tf = static_cast<float>(a.T);
     reinterpret_cast<V*>(a.rates)[e >> 1] =
@@ -198,12 +253,14 @@ __global__ void __launch_bounds__(kThreads) scan_fwd_fast_kernel(const ScanFwdAr
 // Backward
 // ---------------------------------------------------------------------------
 template <typename T, int KIND, int RESET, int SURR, int MODE>
-__global__ void __launch_bounds__(kThreads, KIND == MB_ALIF ? 3 : 4) scan_bwd_fast_kernel(const ScanBwdArgs a) {
+__global__ void __launch_bounds__(kThreads, bwd_min_blocks(KIND, SURR)) scan_bwd_fast_kernel(
+    const ScanBwdArgs a, const PairConsts c, const __grid_constant__ CUtensorMap out_map) {
   using P = Pair<T>;
   using V = typename P::V;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + kBwdRing * bwd_stage_bytes<T>());
   uint64_t* empty = full + kBwdRing;
+  uint64_t* done = empty + kBwdRing;
   auto stage_x = [&](int s) { return reinterpret_cast<T*>(smem_raw + s * bwd_stage_bytes<T>()); };
   auto stage_g = [&](int s) { return stage_x(s) + kChunk * kTileN; };
   auto stage_c = [&](int s) { return reinterpret_cast<float*>(stage_g(s) + kChunk * kTileN); };
@@ -221,7 +278,8 @@ __global__ void __launch_bounds__(kThreads, KIND == MB_ALIF ? 3 : 4) scan_bwd_fa
   if (threadIdx.x == 0) {
     for (int s = 0; s < kBwdRing; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
+      mbar_init(&empty[s], 1);  // released by the thread that stores the stage
+      mbar_init(&done[s], kConsumerWarps);
     }
     fence_barrier_init();
   }
@@ -256,105 +314,92 @@ __global__ void __launch_bounds__(kThreads, KIND == MB_ALIF ? 3 : 4) scan_bwd_fa
   const int tid = threadIdx.x;
   const bool valid = 2 * tid < tile_n;
   const int64_t e = e0 + 2 * tid;
-  const int64_t half_bn = a.BN >> 1;
-  const float decay = a.decay, thr = a.threshold, reset_v = a.reset;
-  const float adapt_decay = a.adapt_decay, beta = a.beta;
-  const SurrogateD<SURR> dfun(a.slope);
+  const F2 decay = c.decay, nthr = c.nthr, adapt_decay = c.adapt_decay, nbeta = c.nbeta;
+  const F2 reset2 = c.reset;
+  const float reset_v = a.reset;
+  const SurrogateD2<SURR> dfun(a.slope, c.k0, c.k1, c.one);
 
-  float gm0 = 0.f, gm1 = 0.f, ga0 = 0.f, ga1 = 0.f, gr0 = 0.f, gr1 = 0.f;
+  F2 gm = f2(0.0f), ga = f2(0.0f), gr = f2(0.0f);
   if (valid) {
-    if (a.grad_vT) {
-      const float2 v = P::to_f2(reinterpret_cast<const V*>(a.grad_vT)[e >> 1]);
-      gm0 = v.x;
-      gm1 = v.y;
-    }
+    if (a.grad_vT) gm = f2(P::to_f2(reinterpret_cast<const V*>(a.grad_vT)[e >> 1]));
     if (KIND == MB_ALIF && a.grad_aT) {
-      const float2 v = P::to_f2(reinterpret_cast<const V*>(a.grad_aT)[e >> 1]);
-      ga0 = v.x;
-      ga1 = v.y;
+      ga = f2(P::to_f2(reinterpret_cast<const V*>(a.grad_aT)[e >> 1]));
     }
     if (kRateGrad && a.grad_rates) {
       // the grad of a rate output reaches every step as grad_rates / T
       // (src/myelin/autograd.py:842-844)
       const float2 v = P::to_f2(reinterpret_cast<const V*>(a.grad_rates)[e >> 1]);
       const float tf = static_cast<float>(a.T);
-      gr0 = __fdiv_rn(v.x, tf);
-      gr1 = __fdiv_rn(v.y, tf);
+      gr = f2(__fdiv_rn(v.x, tf), __fdiv_rn(v.y, tf));
     }
   }
 
-  // One reverse step for one neuron; returns dL/dx_t and updates gm, ga.
-  auto adjoint = [&](float p, float th, float gsum, float& gm, float& ga) -> float {
-    const float d = dfun(p - th);
-    float gp;
+  // One reverse step for a pair of neurons; returns dL/dx_t and updates gm, ga.
+  // pv is what the replay kept: p - theta (subtractive reset) or p (hard
+  // reset); nth = -theta. The spike is diff >= 0, which equals p >= theta for
+  // finite values (a NaN or infinite membrane gives NaN gradients either way).
+  auto adjoint = [&](F2 pv, F2 nth, F2 gsum) -> F2 {
+    const F2 diff = (RESET == MB_RESET_SUBTRACT) ? pv : add2(pv, nth);
+    const F2 d = dfun(diff);
+    F2 gp;
     if (KIND == MB_LIF) {
       if (RESET == MB_RESET_HARD) {
-        const float sf = p >= th ? 1.0f : 0.0f;
-        gp = gm * ((1.0f - sf) + (reset_v - p) * d) + gsum * d;
+        const F2 nsf = f2(lt_f(diff.x, 0.0f), lt_f(diff.y, 0.0f));  // 1 - s
+        gp = fma2(gm, fma2(sub2(reset2, pv), d, nsf), mul2(gsum, d));
       } else {
-        gp = gm + (gsum - gm * th) * d;
+        gp = fma2(fma2(gm, nth, gsum), d, gm);
       }
     } else {
       if (RESET == MB_RESET_HARD) {
-        const float Gs = gsum + gm * (reset_v - p) + ga;
-        const float Gd = Gs * d;
-        gp = (p >= th ? 0.0f : gm) + Gd;
-        ga = ga * adapt_decay - beta * Gd;
+        const F2 nsf = f2(lt_f(diff.x, 0.0f), lt_f(diff.y, 0.0f));  // 1 - s
+        const F2 Gd = mul2(add2(fma2(gm, sub2(reset2, pv), gsum), ga), d);
+        gp = fma2(gm, nsf, Gd);
+        ga = fma2(nbeta, Gd, mul2(ga, adapt_decay));
       } else {
-        const float Gs = gsum - gm * th + ga;
-        const float Gd = Gs * d;
-        gp = gm + Gd;
-        ga = ga * adapt_decay - beta * ((p >= th ? gm : 0.0f) + Gd);
+        const F2 sf = f2(ge_f(diff.x, 0.0f), ge_f(diff.y, 0.0f));
+        const F2 Gd = mul2(add2(fma2(gm, nth, gsum), ga), d);
+        gp = add2(gm, Gd);
+        ga = fma2(nbeta, fma2(sf, gm, Gd), mul2(ga, adapt_decay));
       }
     }
-    gm = gp * decay;
+    gm = mul2(gp, decay);
     return gp;
   };
 
-  V* gxp = reinterpret_cast<V*>(a.grad_x) + (e >> 1);
+  // grad_x overwrites the x values of the stage (x is dead once the chunk is
+  // replayed; each thread its own pair) and the finished stage goes out with
+  // one bulk tensor store (store_stage).
   for (int64_t i = 0; i < K; ++i) {
     const int s = static_cast<int>(i % kBwdRing);
     const int64_t k = K - 1 - i;
     const int64_t t0 = k * kChunk;
     const int len = static_cast<int>(imin64(kChunk, a.T - t0));
-    if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>((i / kBwdRing) & 1))) return;
-    const V* xrow = reinterpret_cast<const V*>(stage_x(s)) + tid;
+    if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>((i / kBwdRing) & 1))) {
+      bulk_wait_all();  // stores of earlier chunks finish before the early exit
+      return;
+    }
+    V* xrow = reinterpret_cast<V*>(stage_x(s)) + tid;
     const V* grow = reinterpret_cast<const V*>(stage_g(s)) + tid;
     if (valid) {
-      const float2 mv = reinterpret_cast<const float2*>(stage_c(s))[tid];
-      float m0 = mv.x, m1 = mv.y, av0 = 0.f, av1 = 0.f;
-      if (KIND == MB_ALIF) {
-        const float2 avv = reinterpret_cast<const float2*>(stage_c(s) + kTileN)[tid];
-        av0 = avv.x;
-        av1 = avv.y;
-      }
-      float P0[kChunk], P1[kChunk], TH0[kChunk], TH1[kChunk];
-      V* out = gxp + (t0 + len - 1) * half_bn;
+      F2 m = f2(reinterpret_cast<const float2*>(stage_c(s))[tid]), av = f2(0.0f);
+      if (KIND == MB_ALIF) av = f2(reinterpret_cast<const float2*>(stage_c(s) + kTileN)[tid]);
+      F2 PV[kChunk], TH[kChunk];
       auto replay = [&](int j) {
-        const float2 xf = P::to_f2(xrow[j * (kTileN / 2)]);
-        Step<KIND, RESET> s0, s1;
-        s0.run(m0, av0, xf.x, decay, thr, reset_v, adapt_decay, beta);
-        s1.run(m1, av1, xf.y, decay, thr, reset_v, adapt_decay, beta);
-        P0[j] = s0.p;
-        P1[j] = s1.p;
-        TH0[j] = s0.theta;
-        TH1[j] = s1.theta;
+        Step2<KIND, RESET> st;
+        st.run(m, av, f2(P::to_f2(xrow[j * (kTileN / 2)])), decay, nthr, reset_v, adapt_decay,
+               nbeta);
+        PV[j] = (RESET == MB_RESET_SUBTRACT) ? st.diff : st.p;
+        TH[j] = st.nth;
       };
       auto reverse = [&](int j) {
-        float g0 = gr0, g1 = gr1;
+        F2 g = gr;
         if (MODE == kBwdSpikes) {
-          const float2 gf = P::to_f2(grow[j * (kTileN / 2)]);
-          g0 = gf.x;
-          g1 = gf.y;
+          g = f2(P::to_f2(grow[j * (kTileN / 2)]));
         } else if (has_gs) {
-          const float2 gf = P::to_f2(grow[j * (kTileN / 2)]);
-          g0 += gf.x;
-          g1 += gf.y;
+          g = add2(g, f2(P::to_f2(grow[j * (kTileN / 2)])));
         }
-        const float gp0 = adjoint(P0[j], TH0[j], g0, gm0, ga0);
-        const float gp1 = adjoint(P1[j], TH1[j], g1, gm1, ga1);
-        *out = P::from_f2(gp0, gp1);
-        out -= half_bn;
+        const float2 gp = split(adjoint(PV[j], TH[j], g));
+        xrow[j * (kTileN / 2)] = P::from_f2(gp.x, gp.y);
       };
       if (len == kChunk) {
 #pragma unroll
@@ -372,12 +417,17 @@ __global__ void __launch_bounds__(kThreads, KIND == MB_ALIF ? 3 : 4) scan_bwd_fa
         }
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
+    if (!store_stage(stage_x(s), &done[s], &empty[s], i, kBwdRing, &out_map, e0, t0)) {
+      bulk_wait_all();
+      return;
+    }
   }
+  bulk_wait_all();
   if (!valid) return;
-  if (a.grad_v0) reinterpret_cast<V*>(a.grad_v0)[e >> 1] = P::from_f2(gm0, gm1);
-  if (KIND == MB_ALIF && a.grad_a0) reinterpret_cast<V*>(a.grad_a0)[e >> 1] = P::from_f2(ga0, ga1);
+  if (a.grad_v0) reinterpret_cast<V*>(a.grad_v0)[e >> 1] = P::from_f2(split(gm).x, split(gm).y);
+  if (KIND == MB_ALIF && a.grad_a0) {
+    reinterpret_cast<V*>(a.grad_a0)[e >> 1] = P::from_f2(split(ga).x, split(ga).y);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -402,74 +452,103 @@ bool fast_layout_ok(int64_t BN, size_t elt, std::initializer_list<const void*> r
   return true;
 }
 
+using Map = CUtensorMap;
+
 template <typename T, int KIND, int RESET, int MODE>
-void fwd_fast_mode(const ScanFwdArgs& a, cudaStream_t stream) {
+void fwd_fast_mode(const ScanFwdArgs& a, const Map& om, cudaStream_t stream) {
   auto k = scan_fwd_fast_kernel<T, KIND, RESET, MODE>;
   allow_smem(k, fwd_smem<T>());
-  k<<<static_cast<unsigned>(ceil_div(a.BN, kTileN)), kThreads, fwd_smem<T>(), stream>>>(a);
+  k<<<static_cast<unsigned>(ceil_div(a.BN, kTileN)), kThreads, fwd_smem<T>(), stream>>>(
+      a, pair_consts<MB_SURR_NONE>(a.decay, a.threshold, a.adapt_decay, a.beta, a.reset, 0.0f),
+      om);
 }
 
 template <typename T, int KIND, int RESET>
-void fwd_fast(const ScanFwdArgs& a, cudaStream_t stream) {
+void fwd_fast(const ScanFwdArgs& a, const Map& om, cudaStream_t stream) {
   const bool d = a.spikes != nullptr, p = a.packed != nullptr, r = a.rates != nullptr;
-  if (d && !p && !r) fwd_fast_mode<T, KIND, RESET, kFwdDense>(a, stream);
-  else if (!d && p && !r) fwd_fast_mode<T, KIND, RESET, kFwdPacked>(a, stream);
-  else if (!d && !p && r) fwd_fast_mode<T, KIND, RESET, kFwdRates>(a, stream);
-  else fwd_fast_mode<T, KIND, RESET, kFwdAny>(a, stream);
+  if (d && !p && !r) fwd_fast_mode<T, KIND, RESET, kFwdDense>(a, om, stream);
+  else if (!d && p && !r) fwd_fast_mode<T, KIND, RESET, kFwdPacked>(a, om, stream);
+  else if (!d && !p && r) fwd_fast_mode<T, KIND, RESET, kFwdRates>(a, om, stream);
+  else fwd_fast_mode<T, KIND, RESET, kFwdAny>(a, om, stream);
 }
 
 template <typename T>
-void fwd_fast_dispatch(int neuron, int reset_mode, const ScanFwdArgs& a, cudaStream_t stream) {
+void fwd_fast_dispatch(int neuron, int reset_mode, const ScanFwdArgs& a, const Map& om,
+                       cudaStream_t stream) {
   if (neuron == MB_LIF) {
-    if (reset_mode == MB_RESET_HARD) fwd_fast<T, MB_LIF, MB_RESET_HARD>(a, stream);
-    else fwd_fast<T, MB_LIF, MB_RESET_SUBTRACT>(a, stream);
+    if (reset_mode == MB_RESET_HARD) fwd_fast<T, MB_LIF, MB_RESET_HARD>(a, om, stream);
+    else fwd_fast<T, MB_LIF, MB_RESET_SUBTRACT>(a, om, stream);
   } else {
-    if (reset_mode == MB_RESET_HARD) fwd_fast<T, MB_ALIF, MB_RESET_HARD>(a, stream);
-    else fwd_fast<T, MB_ALIF, MB_RESET_SUBTRACT>(a, stream);
+    if (reset_mode == MB_RESET_HARD) fwd_fast<T, MB_ALIF, MB_RESET_HARD>(a, om, stream);
+    else fwd_fast<T, MB_ALIF, MB_RESET_SUBTRACT>(a, om, stream);
   }
 }
 
 template <typename T, int KIND, int RESET, int SURR, int MODE>
-void bwd_fast_mode(const ScanBwdArgs& a, cudaStream_t stream) {
+void bwd_fast_mode(const ScanBwdArgs& a, const Map& om, cudaStream_t stream) {
   auto k = scan_bwd_fast_kernel<T, KIND, RESET, SURR, MODE>;
   allow_smem(k, bwd_smem<T>());
-  k<<<static_cast<unsigned>(ceil_div(a.BN, kTileN)), kThreads, bwd_smem<T>(), stream>>>(a);
+  k<<<static_cast<unsigned>(ceil_div(a.BN, kTileN)), kThreads, bwd_smem<T>(), stream>>>(
+      a, pair_consts<SURR>(a.decay, a.threshold, a.adapt_decay, a.beta, a.reset, a.slope), om);
 }
 
 template <typename T, int KIND, int RESET, int SURR>
-void bwd_fast(const ScanBwdArgs& a, cudaStream_t stream) {
+void bwd_fast(const ScanBwdArgs& a, const Map& om, cudaStream_t stream) {
   const bool g = a.grad_spikes != nullptr, r = a.grad_rates != nullptr;
-  if (g && !r) bwd_fast_mode<T, KIND, RESET, SURR, kBwdSpikes>(a, stream);
-  else if (!g && r) bwd_fast_mode<T, KIND, RESET, SURR, kBwdRates>(a, stream);
-  else bwd_fast_mode<T, KIND, RESET, SURR, kBwdAny>(a, stream);
+  if (g && !r) bwd_fast_mode<T, KIND, RESET, SURR, kBwdSpikes>(a, om, stream);
+  else if (!g && r) bwd_fast_mode<T, KIND, RESET, SURR, kBwdRates>(a, om, stream);
+  else bwd_fast_mode<T, KIND, RESET, SURR, kBwdAny>(a, om, stream);
 }
 
 template <typename T, int KIND, int RESET>
-void bwd_fast_surr(int surrogate, const ScanBwdArgs& a, cudaStream_t stream) {
+void bwd_fast_surr(int surrogate, const ScanBwdArgs& a, const Map& om, cudaStream_t stream) {
   switch (surrogate) {
-    case MB_SURR_SIGMOID: bwd_fast<T, KIND, RESET, MB_SURR_SIGMOID>(a, stream); break;
-    case MB_SURR_FAST_SIGMOID: bwd_fast<T, KIND, RESET, MB_SURR_FAST_SIGMOID>(a, stream); break;
-    case MB_SURR_ATAN: bwd_fast<T, KIND, RESET, MB_SURR_ATAN>(a, stream); break;
-    case MB_SURR_TRIANGULAR: bwd_fast<T, KIND, RESET, MB_SURR_TRIANGULAR>(a, stream); break;
-    case MB_SURR_SUPERSPIKE: bwd_fast<T, KIND, RESET, MB_SURR_SUPERSPIKE>(a, stream); break;
-    case MB_SURR_MULTI_GAUSSIAN: bwd_fast<T, KIND, RESET, MB_SURR_MULTI_GAUSSIAN>(a, stream); break;
-    default: bwd_fast<T, KIND, RESET, MB_SURR_NONE>(a, stream); break;
+    case MB_SURR_SIGMOID: bwd_fast<T, KIND, RESET, MB_SURR_SIGMOID>(a, om, stream); break;
+    case MB_SURR_FAST_SIGMOID: bwd_fast<T, KIND, RESET, MB_SURR_FAST_SIGMOID>(a, om, stream); break;
+    case MB_SURR_ATAN: bwd_fast<T, KIND, RESET, MB_SURR_ATAN>(a, om, stream); break;
+    case MB_SURR_TRIANGULAR: bwd_fast<T, KIND, RESET, MB_SURR_TRIANGULAR>(a, om, stream); break;
+    case MB_SURR_SUPERSPIKE: bwd_fast<T, KIND, RESET, MB_SURR_SUPERSPIKE>(a, om, stream); break;
+    case MB_SURR_MULTI_GAUSSIAN:
+      bwd_fast<T, KIND, RESET, MB_SURR_MULTI_GAUSSIAN>(a, om, stream);
+      break;
+    default: bwd_fast<T, KIND, RESET, MB_SURR_NONE>(a, om, stream); break;
   }
 }
 
 template <typename T>
 void bwd_fast_dispatch(int neuron, int reset_mode, int surrogate, const ScanBwdArgs& a,
-                       cudaStream_t stream) {
+                       const Map& om, cudaStream_t stream) {
   if (neuron == MB_LIF) {
-    if (reset_mode == MB_RESET_HARD) bwd_fast_surr<T, MB_LIF, MB_RESET_HARD>(surrogate, a, stream);
-    else bwd_fast_surr<T, MB_LIF, MB_RESET_SUBTRACT>(surrogate, a, stream);
+    if (reset_mode == MB_RESET_HARD) bwd_fast_surr<T, MB_LIF, MB_RESET_HARD>(surrogate, a, om, stream);
+    else bwd_fast_surr<T, MB_LIF, MB_RESET_SUBTRACT>(surrogate, a, om, stream);
   } else {
-    if (reset_mode == MB_RESET_HARD) bwd_fast_surr<T, MB_ALIF, MB_RESET_HARD>(surrogate, a, stream);
-    else bwd_fast_surr<T, MB_ALIF, MB_RESET_SUBTRACT>(surrogate, a, stream);
+    if (reset_mode == MB_RESET_HARD) bwd_fast_surr<T, MB_ALIF, MB_RESET_HARD>(surrogate, a, om, stream);
+    else bwd_fast_surr<T, MB_ALIF, MB_RESET_SUBTRACT>(surrogate, a, om, stream);
   }
 }
 
 size_t dtype_size(int dtype) { return dtype == MB_F32 ? 4 : 2; }
+
+// Tensor map over a [T, BN] output written stage by stage: box = one stage
+// (kTileN neurons x kChunk rows), no swizzle (the stage is dense row-major).
+bool make_stage_map(Map* map, void* ptr, int dtype, int64_t BN, int64_t T) {
+  std::memset(map, 0, sizeof(Map));
+  if (ptr == nullptr) return true;  // no such output: the kernel never uses the map
+  auto fn = tma_encode_fn();
+  if (fn == nullptr) return false;
+  // coordinates are 32-bit in the store instruction
+  if (BN > INT32_MAX || T > INT32_MAX) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(BN), static_cast<cuuint64_t>(T)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(BN) * dtype_size(dtype)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kTileN), static_cast<cuuint32_t>(kChunk)};
+  cuuint32_t estride[2] = {1, 1};
+  const CUtensorMapDataType dt = dtype == MB_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : dtype == MB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                    : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return fn(map, dt, 2, ptr, dims, strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 }  // namespace
 
@@ -478,14 +557,16 @@ bool launch_scan_fwd_fast(int dtype, int neuron, int reset_mode, const ScanFwdAr
   const size_t elt = dtype_size(dtype);
   if (a.T <= 0) return false;
   if (a.packed != nullptr && (a.N % 32) != 0) return false;
-  if (!fast_layout_ok(a.BN, elt, {a.x}, {a.v0, a.a0, a.vT, a.aT, a.spikes, a.rates, a.ckpt_v,
-                                        a.ckpt_a})) {
+  if (!fast_layout_ok(a.BN, elt, {a.x, a.spikes}, {a.v0, a.a0, a.vT, a.aT, a.rates, a.ckpt_v,
+                                                   a.ckpt_a})) {
     return false;
   }
+  Map om;
+  if (!make_stage_map(&om, a.spikes, dtype, a.BN, a.T)) return false;
   switch (dtype) {
-    case MB_F32: fwd_fast_dispatch<float>(neuron, reset_mode, a, stream); break;
-    case MB_BF16: fwd_fast_dispatch<__nv_bfloat16>(neuron, reset_mode, a, stream); break;
-    default: fwd_fast_dispatch<__half>(neuron, reset_mode, a, stream); break;
+    case MB_F32: fwd_fast_dispatch<float>(neuron, reset_mode, a, om, stream); break;
+    case MB_BF16: fwd_fast_dispatch<__nv_bfloat16>(neuron, reset_mode, a, om, stream); break;
+    default: fwd_fast_dispatch<__half>(neuron, reset_mode, a, om, stream); break;
   }
   return true;
 }
@@ -494,14 +575,18 @@ bool launch_scan_bwd_fast(int dtype, int neuron, int reset_mode, int surrogate,
                           const ScanBwdArgs& a, cudaStream_t stream) {
   const size_t elt = dtype_size(dtype);
   if (a.T <= 0) return false;
-  if (!fast_layout_ok(a.BN, elt, {a.x, a.grad_spikes, a.ckpt_v, a.ckpt_a},
-                      {a.grad_x, a.grad_rates, a.grad_vT, a.grad_aT, a.grad_v0, a.grad_a0})) {
+  if (!fast_layout_ok(a.BN, elt, {a.x, a.grad_x, a.grad_spikes, a.ckpt_v, a.ckpt_a},
+                      {a.grad_rates, a.grad_vT, a.grad_aT, a.grad_v0, a.grad_a0})) {
     return false;
   }
+  Map om;
+  if (!make_stage_map(&om, a.grad_x, dtype, a.BN, a.T)) return false;
   switch (dtype) {
-    case MB_F32: bwd_fast_dispatch<float>(neuron, reset_mode, surrogate, a, stream); break;
-    case MB_BF16: bwd_fast_dispatch<__nv_bfloat16>(neuron, reset_mode, surrogate, a, stream); break;
-    default: bwd_fast_dispatch<__half>(neuron, reset_mode, surrogate, a, stream); break;
+    case MB_F32: bwd_fast_dispatch<float>(neuron, reset_mode, surrogate, a, om, stream); break;
+    case MB_BF16:
+      bwd_fast_dispatch<__nv_bfloat16>(neuron, reset_mode, surrogate, a, om, stream);
+      break;
+    default: bwd_fast_dispatch<__half>(neuron, reset_mode, surrogate, a, om, stream); break;
   }
   return true;
 }

@@ -1,0 +1,42 @@
+// Tensor-map (TMA descriptor) creation shared by the kernels that move tiles
+// with cp.async.bulk.tensor: the driver's cuTensorMapEncodeTiled, looked up
+// once through the runtime (no link-time dependency on libcuda).
+#pragma once
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+namespace mb {
+
+inline PFN_cuTensorMapEncodeTiled_v12000 tma_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+  });
+  return fn;
+}
+
+// 2-D bulk tensor store of a dense shared-memory box to global memory, tracked
+// in the issuing thread's bulk async-group (committed here). Elements of the
+// box outside the tensor are not written.
+__device__ __forceinline__ void tma_store_box_2d(const CUtensorMap* map, const void* src, int c0,
+                                                 int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(c0), "r"(c1), "r"(static_cast<uint32_t>(__cvta_generic_to_shared(src)))
+      : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+}  // namespace mb
