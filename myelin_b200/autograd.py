@@ -14,30 +14,15 @@ from typing import Any
 import torch
 
 from myelin_b200 import _native as nat
-
-
-def _scan_scratch(x: torch.Tensor, alif: bool, save: bool):
-    T, B, N = x.shape
-    if not save or T == 0:
-        return None, None
-    K = nat.num_checkpoints(T)
-    ckpt_v = torch.empty((K, B, N), dtype=torch.float32, device=x.device)
-    ckpt_a = torch.empty_like(ckpt_v) if alif else None
-    return ckpt_v, ckpt_a
+from myelin_b200 import compile_ops as cops
 
 
 def _scan_forward(ctx: Any, x, v0, a0, neuron, decay, threshold, reset, adapt_decay, beta,
                   reset_mode, surrogate, slope, reject_spike_grad):
-    alif = neuron == nat.MB_ALIF
     save = any(ctx.needs_input_grad[:3])
-    ckpt_v, ckpt_a = _scan_scratch(x, alif, save)
-    vT = torch.empty_like(v0)
-    aT = torch.empty_like(a0) if alif else None
-    spikes = torch.empty_like(x)
-    nat.scan_forward(
-        neuron=neuron, x=x, v0=v0, a0=a0, vT=vT, aT=aT, spikes=spikes, packed=None,
-        rates=None, ckpt_v=ckpt_v, ckpt_a=ckpt_a, decay=decay, threshold=threshold,
-        reset=reset, adapt_decay=adapt_decay, beta=beta, reset_mode=reset_mode,
+    vT, aT, spikes, _, _, ckpt_v, ckpt_a = cops.scan_forward(
+        x, v0, a0, neuron, decay, threshold, reset, adapt_decay, beta, reset_mode,
+        dense=True, checkpoints=save,
     )
     ctx.set_materialize_grads(False)
     ctx.save_for_backward(x, ckpt_v, ckpt_a)
@@ -49,31 +34,17 @@ def _scan_forward(ctx: Any, x, v0, a0, neuron, decay, threshold, reset, adapt_de
 def _scan_backward(ctx: Any, g_vT, g_aT, g_spikes):
     """Returns (grad_x, grad_v0, grad_a0) or None when no gradient flows."""
 
-    if ctx.reject_spike_grad:
-        if g_spikes is not None and bool(torch.any(g_spikes != 0)):
-            raise NotImplementedError(
-                "spike-output backward of the hard LIF forward is not defined; use "
-                "surrogate_lif_forward for surrogate-gradient training."
-            )
-        g_spikes = None
     if g_vT is None and g_aT is None and g_spikes is None:
         return None
     x, ckpt_v, ckpt_a = ctx.saved_tensors
     neuron, decay, threshold, reset, adapt_decay, beta, reset_mode, surrogate, slope = ctx.cfg
-    alif = neuron == nat.MB_ALIF
     need_x, need_v0, need_a0 = ctx.needs_input_grad[:3]
-    grad_x = torch.empty_like(x)
-    grad_v0 = torch.empty(x.shape[1:], dtype=x.dtype, device=x.device) if need_v0 else None
-    grad_a0 = torch.empty(x.shape[1:], dtype=x.dtype, device=x.device) if alif and need_a0 else None
-    nat.scan_backward(
-        neuron=neuron, x=x, ckpt_v=ckpt_v, ckpt_a=ckpt_a,
-        grad_spikes=None if g_spikes is None else g_spikes.contiguous(),
-        grad_rates=None,
-        grad_vT=None if g_vT is None else g_vT.contiguous(),
-        grad_aT=None if (g_aT is None or not alif) else g_aT.contiguous(),
-        grad_x=grad_x, grad_v0=grad_v0, grad_a0=grad_a0, decay=decay, threshold=threshold,
-        reset=reset, adapt_decay=adapt_decay, beta=beta, reset_mode=reset_mode,
-        surrogate=surrogate, slope=slope,
+    grad_x, grad_v0, grad_a0 = cops.scan_backward(
+        x, ckpt_v, ckpt_a, grad_spikes=g_spikes, grad_vT=g_vT,
+        grad_aT=g_aT if neuron == nat.MB_ALIF else None, neuron=neuron, decay=decay,
+        threshold=threshold, reset=reset, adapt_decay=adapt_decay, beta=beta,
+        reset_mode=reset_mode, surrogate=surrogate, slope=slope, need_v0=need_v0,
+        need_a0=need_a0, reject_spike_grad=ctx.reject_spike_grad,
     )
     return (grad_x if need_x else None), grad_v0, grad_a0
 
@@ -131,9 +102,8 @@ def _project(x2: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None) 
     """
 
     wt = weight.t().contiguous()  # [N, F]: K-major B operand
-    if nat.gemm_tn_supported(x2, wt):
-        out = torch.empty((x2.shape[0], wt.shape[0]), dtype=x2.dtype, device=x2.device)
-        return nat.gemm_tn(x2, wt, bias, out)
+    if cops.gemm_tn_dtype_ok(x2, wt):
+        return cops.gemm_tn(x2, wt, bias)
     if bias is not None:
         return torch.addmm(bias, x2, weight)
     return torch.mm(x2, weight)
@@ -142,9 +112,8 @@ def _project(x2: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None) 
 def _input_grad(g2: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     """dX[T*B, F] = G[T*B, N] @ weight[F, N]^T."""
 
-    if nat.gemm_tn_supported(g2, weight):
-        out = torch.empty((g2.shape[0], weight.shape[0]), dtype=g2.dtype, device=g2.device)
-        return nat.gemm_tn(g2, weight, None, out)
+    if cops.gemm_tn_dtype_ok(g2, weight):
+        return cops.gemm_tn(g2, weight)
     return torch.mm(g2, weight.t())
 
 
@@ -176,17 +145,12 @@ class LinearScanFunction(torch.autograd.Function):
         x2 = inputs.reshape(T * B, F)
         currents = _project(x2, weight, bias).view(T, B, N)
         save = any(ctx.needs_input_grad[:3])
-        ckpt_v, _ = _scan_scratch(currents, False, save)
         v0 = torch.zeros((B, N), dtype=inputs.dtype, device=inputs.device)
-        vT = torch.empty_like(v0)
-        out = torch.empty_like(v0) if rate_output else torch.empty_like(currents)
-        nat.scan_forward(
-            neuron=nat.MB_LIF, x=currents, v0=v0, a0=None, vT=vT, aT=None,
-            spikes=None if rate_output else out, packed=None,
-            rates=out if rate_output else None, ckpt_v=ckpt_v, ckpt_a=None, decay=decay,
-            threshold=threshold, reset=reset, adapt_decay=0.0, beta=0.0,
-            reset_mode=nat.MB_RESET_HARD,
+        vT, _, spikes, _, rates, ckpt_v, _ = cops.scan_forward(
+            currents, v0, None, nat.MB_LIF, decay, threshold, reset, 0.0, 0.0,
+            nat.MB_RESET_HARD, dense=not rate_output, rates=rate_output, checkpoints=save,
         )
+        out = rates if rate_output else spikes
         ctx.set_materialize_grads(False)
         ctx.save_for_backward(inputs, weight, currents, ckpt_v)
         ctx.has_bias = bias is not None
@@ -203,15 +167,12 @@ class LinearScanFunction(torch.autograd.Function):
         need_x, need_w, need_b = ctx.needs_input_grad[:3]
         T, B, F = inputs.shape
         N = weight.shape[1]
-        grad_currents = torch.empty_like(currents)
-        g = None if g_out is None else g_out.contiguous()
-        nat.scan_backward(
-            neuron=nat.MB_LIF, x=currents, ckpt_v=ckpt_v, ckpt_a=None,
-            grad_spikes=None if rate_output else g, grad_rates=g if rate_output else None,
-            grad_vT=None if g_vT is None else g_vT.contiguous(), grad_aT=None,
-            grad_x=grad_currents, grad_v0=None, grad_a0=None, decay=decay, threshold=threshold,
-            reset=reset, adapt_decay=0.0, beta=0.0, reset_mode=nat.MB_RESET_HARD,
-            surrogate=surrogate, slope=slope,
+        grad_currents, _, _ = cops.scan_backward(
+            currents, ckpt_v, None, grad_spikes=None if rate_output else g_out,
+            grad_rates=g_out if rate_output else None, grad_vT=g_vT, neuron=nat.MB_LIF,
+            decay=decay, threshold=threshold, reset=reset, adapt_decay=0.0, beta=0.0,
+            reset_mode=nat.MB_RESET_HARD, surrogate=surrogate, slope=slope, need_v0=False,
+            need_a0=False,
         )
         g2 = grad_currents.view(T * B, N)
         grad_inputs = _input_grad(g2, weight).view(T, B, F) if need_x else None

@@ -61,7 +61,7 @@ enum BwdMode { kBwdSpikes = 0, kBwdRates = 1, kBwdAny = 2 };
 // (sigmoid, multi-Gaussian) hold more temporaries; fewer CTAs give them
 // registers enough not to spill.
 constexpr int bwd_min_blocks(int kind, int surr) {
-  return kind == MB_LIF ? 4 : (surr == MB_SURR_SIGMOID || surr == MB_SURR_MULTI_GAUSSIAN ? 2 : 3);
+  return kind == MB_LIF ? 4 : (surr == MB_SURR_SIGMOID || surr == MB_SURR_MULTI_GAUSSIAN ? 2 : 4);
 }
 
 // Per-launch fp32 constants, each duplicated into both lanes of a float2 for
@@ -191,9 +191,9 @@ __global__ void __launch_bounds__(kThreads, 6) scan_fwd_fast_kernel(
   const bool pk_lane = (lane & 15) == 0 && (q << 5) < a.BN;
   const int sh = lane & 16;  // lanes 0-15 -> word q, lanes 16-31 -> word q+1
 
-  auto step = [&](V* slot) {
+  auto step = [&](V xv, V* slot) {
     Step2<KIND, RESET> st;
-    st.run(m, ad, f2(P::to_f2(*slot)), decay, nthr, reset_v, adapt_decay, nbeta);
+    st.run(m, ad, f2(P::to_f2(xv)), decay, nthr, reset_v, adapt_decay, nbeta);
     if (kRates) {
       c0 += st.s0 ? 1 : 0;
       c1 += st.s1 ? 1 : 0;
@@ -222,10 +222,14 @@ __global__ void __launch_bounds__(kThreads, 6) scan_fwd_fast_kernel(
     V* row = reinterpret_cast<V*>(stage) + tid;
     const int len = static_cast<int>(imin64(kChunk, a.T - k * kChunk));
     if (len == kChunk) {
+      // all loads first: the spike stores below alias the same stage
+      V xv[kChunk];
 #pragma unroll
-      for (int j = 0; j < kChunk; ++j) step(row + j * (kTileN / 2));
+      for (int j = 0; j < kChunk; ++j) xv[j] = row[j * (kTileN / 2)];
+#pragma unroll
+      for (int j = 0; j < kChunk; ++j) step(xv[j], row + j * (kTileN / 2));
     } else {
-      for (int j = 0; j < len; ++j) step(row + j * (kTileN / 2));
+      for (int j = 0; j < len; ++j) step(row[j * (kTileN / 2)], row + j * (kTileN / 2));
     }
     if (kDense && (MODE != kFwdAny || do_dense)) {
       if (!store_stage(stage, &done[s], &empty[s], k, kFwdRing, &out_map, e0, k * kChunk)) {

@@ -20,6 +20,7 @@ from typing import Literal
 import torch
 
 from myelin_b200 import _native as nat
+from myelin_b200 import compile_ops as cops
 from myelin_b200.autograd import (
     ALIFScanFunction,
     LIFScanFunction,
@@ -142,14 +143,9 @@ def lif_forward_packed_spikes(
     _validate_scan(inputs, [("membrane", initial_state.membrane)])
     x = inputs.contiguous()
     v0 = initial_state.membrane.contiguous()
-    T, B, N = x.shape
-    words = torch.empty((T, B, (N + 31) // 32), dtype=torch.int32, device=x.device)
-    vT = torch.empty_like(v0)
-    nat.scan_forward(
-        neuron=nat.MB_LIF, x=x, v0=v0, a0=None, vT=vT, aT=None, spikes=None, packed=words,
-        rates=None, ckpt_v=None, ckpt_a=None, decay=params.decay,
-        threshold=float(params.threshold), reset=float(params.reset), adapt_decay=0.0, beta=0.0,
-        reset_mode=rc,
+    vT, _, _, words, _, _, _ = cops.scan_forward(
+        x, v0, None, nat.MB_LIF, params.decay, float(params.threshold), float(params.reset),
+        0.0, 0.0, rc, packed=True,
     )
     return LIFState(membrane=vT), PackedSpikes(data=words, original_shape=tuple(x.shape))
 
@@ -412,12 +408,8 @@ def linear_surrogate_lif_packed_forward(
         x2 = inputs.contiguous().reshape(T * B, F)
         currents = _project(x2, weight.contiguous(), bias).view(T, B, N)
         v0 = torch.zeros((B, N), dtype=inputs.dtype, device=inputs.device)
-        vT = torch.empty_like(v0)
-        words = torch.empty((T, B, (N + 31) // 32), dtype=torch.int32, device=inputs.device)
-        nat.scan_forward(
-            neuron=nat.MB_LIF, x=currents, v0=v0, a0=None, vT=vT, aT=None, spikes=None,
-            packed=words, rates=None, ckpt_v=None, ckpt_a=None, decay=params.decay,
-            threshold=float(params.threshold), reset=float(params.reset), adapt_decay=0.0,
-            beta=0.0, reset_mode=nat.MB_RESET_HARD,
+        vT, _, _, words, _, _, _ = cops.scan_forward(
+            currents, v0, None, nat.MB_LIF, params.decay, float(params.threshold),
+            float(params.reset), 0.0, 0.0, nat.MB_RESET_HARD, packed=True,
         )
     return LIFState(membrane=vT), PackedSpikes(data=words, original_shape=(T, B, N))

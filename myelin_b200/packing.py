@@ -17,6 +17,7 @@ from typing import TypeAlias
 import torch
 
 from myelin_b200 import _native as nat
+from myelin_b200 import compile_ops as cops
 
 BITS_PER_WORD = 32
 CountDim: TypeAlias = int | Sequence[int] | None
@@ -70,11 +71,8 @@ def pack_spikes(spikes: torch.Tensor) -> PackedSpikes:
     nat.require_cuda(spikes, "spikes")
     original_shape = tuple(spikes.shape)
     n = original_shape[-1]
-    src = spikes.contiguous()
-    words = torch.empty(
-        (*original_shape[:-1], packed_last_dim_size(n)), dtype=torch.int32, device=spikes.device
-    )
-    nat.pack(src, words, _rows(original_shape), n)
+    words = cops.pack(spikes.contiguous(), _rows(original_shape), n)
+    words = words.view(*original_shape[:-1], packed_last_dim_size(n))
     return PackedSpikes(data=words, original_shape=original_shape)
 
 
@@ -83,19 +81,18 @@ def unpack_spikes(packed: PackedSpikes, *, dtype: torch.dtype = torch.float32) -
 
     _validate_packed_spikes(packed)
     nat.require_cuda(packed.data, "packed.data")
-    out = torch.empty(packed.original_shape, dtype=dtype, device=packed.data.device)
-    nat.unpack(packed.data.contiguous(), out, _rows(packed.original_shape), packed.original_shape[-1])
-    return out
+    out = cops.unpack(packed.data.contiguous(), _rows(packed.original_shape),
+                      packed.original_shape[-1], dtype)
+    return out.view(packed.original_shape)
 
 
 def _row_counts(packed: PackedSpikes) -> torch.Tensor:
     _validate_packed_spikes(packed)
     nat.require_cuda(packed.data, "packed.data")
     lead = packed.original_shape[:-1]
-    counts = torch.empty(lead, dtype=torch.int64, device=packed.data.device)
-    nat.count_rows(packed.data.contiguous(), counts, _rows(packed.original_shape),
-                   packed.original_shape[-1])
-    return counts
+    counts = cops.count_rows(packed.data.contiguous(), _rows(packed.original_shape),
+                             packed.original_shape[-1])
+    return counts.view(lead)
 
 
 def packed_spike_counts_over_leading_dims(
@@ -110,16 +107,10 @@ def packed_spike_counts_over_leading_dims(
     _validate_packed_spikes(packed)
     nat.require_cuda(packed.data, "packed.data")
     n = packed.original_shape[-1]
-    device = packed.data.device
-    if dtype == torch.int64:
-        out = torch.empty((n,), dtype=torch.int64, device=device)
-        nat.count_columns(packed.data.contiguous(), _rows(packed.original_shape), n, out, None)
-    elif dtype == torch.int32:
-        out = torch.empty((n,), dtype=torch.int32, device=device)
-        nat.count_columns(packed.data.contiguous(), _rows(packed.original_shape), n, None, out)
-    else:
+    if dtype not in (torch.int64, torch.int32):
         raise ValueError("dtype must be torch.int64 or torch.int32")
-    return out
+    return cops.count_columns(packed.data.contiguous(), _rows(packed.original_shape), n,
+                              wide=dtype == torch.int64)
 
 
 def packed_spike_count(packed: PackedSpikes, dim: CountDim = None) -> torch.Tensor:
