@@ -375,7 +375,7 @@ def run_network(args, world, rank, local) -> None:
     model, dtype = build_network(name, "cuda", 0)
     gen = torch.Generator(device="cuda").manual_seed(100 + rank)
     if name == "mlp_fp32":
-        T, B, F = 25, 256, 784
+        T, B, F = 25, args.batch or 256, 784
         x = (torch.rand((T, B, F), generator=gen, device="cuda") < 0.2).to(dtype)
         labels = torch.randint(0, 10, (B,), generator=gen, device="cuda")
 
@@ -385,7 +385,7 @@ def run_network(args, world, rank, local) -> None:
 
         neurons = 1024 + 10
     else:
-        T, B, F = 100, 512, 2048
+        T, B, F = 100, args.batch or 512, 2048
         x = (torch.rand((T, B, F), generator=gen, device="cuda") < 0.1).to(dtype)
         target = torch.rand((B, 10), generator=gen, device="cuda").mul(0.3).to(dtype)
 
@@ -627,6 +627,9 @@ def main() -> None:
                         default="alif_bf16")
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--batch", type=int, default=None,
+                        help="per-GPU batch of the network workloads (default: the BASELINE "
+                             "config's); smaller values are for profiling captures")
     args = parser.parse_args()
     if args.warmup < 3:
         args.warmup = 3
