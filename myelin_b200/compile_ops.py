@@ -58,25 +58,32 @@ def _scan_forward_shapes(x, neuron, dense, packed, rates, checkpoints):
     }
 
 
+def _scan_forward_eager(x, v0, a0, neuron, decay, threshold, reset, adapt_decay, beta,
+                        reset_mode, dense, packed, rates, checkpoints):
+    """Allocates only the requested outputs; the others are None."""
+
+    shapes = _scan_forward_shapes(x, neuron, dense, packed, rates, checkpoints)
+    out = {k: (torch.empty(s, dtype=d, device=x.device) if len(s) > 1 else None)
+           for k, (s, d) in shapes.items()}
+    nat.scan_forward(
+        neuron=neuron, x=x, v0=v0, a0=a0 if neuron == nat.MB_ALIF else None, vT=out["vT"],
+        aT=out["aT"], spikes=out["spikes"], packed=out["packed"], rates=out["rates"],
+        ckpt_v=out["ckpt_v"], ckpt_a=out["ckpt_a"], decay=decay, threshold=threshold,
+        reset=reset, adapt_decay=adapt_decay, beta=beta, reset_mode=reset_mode,
+    )
+    return tuple(out.values())
+
+
 def _scan_forward_impl(
     x: torch.Tensor, v0: torch.Tensor, a0: torch.Tensor | None, neuron: int, decay: float,
     threshold: float, reset: float, adapt_decay: float, beta: float, reset_mode: int,
     dense: bool, packed: bool, rates: bool, checkpoints: bool,
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
            torch.Tensor]:
-    shapes = _scan_forward_shapes(x, neuron, dense, packed, rates, checkpoints)
-    out = {k: torch.empty(s, dtype=d, device=x.device) for k, (s, d) in shapes.items()}
-    alif = neuron == nat.MB_ALIF
-    nat.scan_forward(
-        neuron=neuron, x=x, v0=v0, a0=a0 if alif else None, vT=out["vT"],
-        aT=out["aT"] if alif else None, spikes=out["spikes"] if dense else None,
-        packed=out["packed"] if packed else None, rates=out["rates"] if rates else None,
-        ckpt_v=out["ckpt_v"] if checkpoints and x.shape[0] > 0 else None,
-        ckpt_a=out["ckpt_a"] if checkpoints and alif and x.shape[0] > 0 else None,
-        decay=decay, threshold=threshold, reset=reset, adapt_decay=adapt_decay, beta=beta,
-        reset_mode=reset_mode,
-    )
-    return tuple(out.values())  # type: ignore[return-value]
+    outs = _scan_forward_eager(x, v0, a0, neuron, decay, threshold, reset, adapt_decay, beta,
+                               reset_mode, dense, packed, rates, checkpoints)
+    # an op returns tensors only: zero-element placeholders for the unrequested ones
+    return tuple(x.new_empty(0) if t is None else t for t in outs)  # type: ignore[return-value]
 
 
 scan_forward_op = torch.library.custom_op(f"{_NS}::scan_forward", _scan_forward_impl,
@@ -101,20 +108,19 @@ def scan_forward(x, v0, a0, neuron, decay, threshold, reset, adapt_decay, beta, 
     args = (x, v0, a0, int(neuron), float(decay), float(threshold), float(reset),
             float(adapt_decay), float(beta), int(reset_mode), bool(dense), bool(packed),
             bool(rates), bool(checkpoints))
-    outs = scan_forward_op(*args) if _tracing() else _scan_forward_impl(*args)
-    return tuple(_none0(t) for t in outs)
+    if _tracing():
+        return tuple(_none0(t) for t in scan_forward_op(*args))
+    return _scan_forward_eager(*args)
 
 
 # ---------------------------------------------------------------------------
 # scan backward
 # ---------------------------------------------------------------------------
-def _scan_backward_impl(
-    x: torch.Tensor, ckpt_v: torch.Tensor | None, ckpt_a: torch.Tensor | None,
-    grad_spikes: torch.Tensor | None, grad_rates: torch.Tensor | None,
-    grad_vT: torch.Tensor | None, grad_aT: torch.Tensor | None, neuron: int, decay: float,
-    threshold: float, reset: float, adapt_decay: float, beta: float, reset_mode: int,
-    surrogate: int, slope: float, need_v0: bool, need_a0: bool, reject_spike_grad: bool,
-) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+def _scan_backward_eager(x, ckpt_v, ckpt_a, grad_spikes, grad_rates, grad_vT, grad_aT, neuron,
+                         decay, threshold, reset, adapt_decay, beta, reset_mode, surrogate,
+                         slope, need_v0, need_a0, reject_spike_grad):
+    """Allocates only the requested gradients; the others are None."""
+
     if reject_spike_grad and grad_spikes is not None:
         # the hard forward's spike output has no gradient (src/myelin/autograd.py:46-53)
         if bool(torch.any(grad_spikes != 0)):
@@ -126,20 +132,32 @@ def _scan_backward_impl(
     T, B, N = x.shape
     alif = neuron == nat.MB_ALIF
     grad_x = torch.empty_like(x)
-    grad_v0 = torch.empty((B, N) if need_v0 else (0,), dtype=x.dtype, device=x.device)
-    grad_a0 = torch.empty((B, N) if alif and need_a0 else (0,), dtype=x.dtype, device=x.device)
+    grad_v0 = torch.empty((B, N), dtype=x.dtype, device=x.device) if need_v0 else None
+    grad_a0 = torch.empty((B, N), dtype=x.dtype, device=x.device) if alif and need_a0 else None
     nat.scan_backward(
         neuron=neuron, x=x, ckpt_v=ckpt_v, ckpt_a=ckpt_a if alif else None,
         grad_spikes=None if grad_spikes is None else grad_spikes.contiguous(),
         grad_rates=None if grad_rates is None else grad_rates.contiguous(),
         grad_vT=None if grad_vT is None else grad_vT.contiguous(),
         grad_aT=None if (grad_aT is None or not alif) else grad_aT.contiguous(),
-        grad_x=grad_x, grad_v0=grad_v0 if need_v0 else None,
-        grad_a0=grad_a0 if alif and need_a0 else None, decay=decay, threshold=threshold,
+        grad_x=grad_x, grad_v0=grad_v0, grad_a0=grad_a0, decay=decay, threshold=threshold,
         reset=reset, adapt_decay=adapt_decay, beta=beta, reset_mode=reset_mode,
         surrogate=surrogate, slope=slope,
     )
     return grad_x, grad_v0, grad_a0
+
+
+def _scan_backward_impl(
+    x: torch.Tensor, ckpt_v: torch.Tensor | None, ckpt_a: torch.Tensor | None,
+    grad_spikes: torch.Tensor | None, grad_rates: torch.Tensor | None,
+    grad_vT: torch.Tensor | None, grad_aT: torch.Tensor | None, neuron: int, decay: float,
+    threshold: float, reset: float, adapt_decay: float, beta: float, reset_mode: int,
+    surrogate: int, slope: float, need_v0: bool, need_a0: bool, reject_spike_grad: bool,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    outs = _scan_backward_eager(x, ckpt_v, ckpt_a, grad_spikes, grad_rates, grad_vT, grad_aT,
+                                neuron, decay, threshold, reset, adapt_decay, beta, reset_mode,
+                                surrogate, slope, need_v0, need_a0, reject_spike_grad)
+    return tuple(x.new_empty(0) if t is None else t for t in outs)  # type: ignore[return-value]
 
 
 scan_backward_op = torch.library.custom_op(f"{_NS}::scan_backward", _scan_backward_impl,
@@ -169,8 +187,9 @@ def scan_backward(x, ckpt_v, ckpt_a, *, grad_spikes=None, grad_rates=None, grad_
             float(decay), float(threshold), float(reset), float(adapt_decay), float(beta),
             int(reset_mode), int(surrogate), float(slope), bool(need_v0), bool(need_a0),
             bool(reject_spike_grad))
-    outs = scan_backward_op(*args) if _tracing() else _scan_backward_impl(*args)
-    return tuple(_none0(t) for t in outs)
+    if _tracing():
+        return tuple(_none0(t) for t in scan_backward_op(*args))
+    return _scan_backward_eager(*args)
 
 
 # ---------------------------------------------------------------------------
