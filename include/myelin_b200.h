@@ -188,6 +188,25 @@ int mb_count_columns(const int32_t* words, int64_t rows, int64_t n, int64_t* cou
                      int32_t* counts32, void* workspace, int64_t workspace_bytes,
                      void* stream);
 
+/* Workspace (bytes, device memory) that mb_pack_count_spikes needs. */
+int64_t mb_pack_count_workspace_bytes(int64_t rows, int64_t n);
+
+/*
+ * Pack spikes[rows, n] into words (as mb_pack_spikes) and count spikes per
+ * neuron over all rows (as mb_count_columns on the words) in one call. For
+ * aligned 1-byte spikes (bool / uint8 / int8) with n % 32 == 0 and a 16-byte
+ * aligned workspace this is one pass over the spikes; other inputs run the
+ * pack and the count kernels in sequence. Same results either way.
+ * `workspace` must hold mb_pack_count_workspace_bytes(rows, n) bytes.
+ * Replaces: the pair packing.pack_spikes (src/myelin/packing.py:45-71) +
+ *   _packed_spike_counts_over_leading_dims (packing.py:209-216) that one
+ *   step of a packed-spike all-gather / count all-reduce runs
+ *   (distributed.py:63-109).
+ */
+int mb_pack_count_spikes(int dtype, const void* spikes, int32_t* words, int64_t rows, int64_t n,
+                         int64_t* counts64, int32_t* counts32, void* workspace,
+                         int64_t workspace_bytes, void* stream);
+
 /* Largest scratch (bytes) mb_count_columns_noalloc can use: 4 MiB. */
 #define MB_COUNT_COLUMNS_NOALLOC_MAX_BYTES (4 << 20)
 

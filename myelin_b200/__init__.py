@@ -55,6 +55,7 @@ from myelin_b200.packing import (
     packed_spike_count,
     packed_spike_counts,
     packed_spike_counts_over_leading_dims,
+    pack_spikes_with_counts,
     packed_spike_rate,
     spike_compression_ratio,
     unpack_spikes,

@@ -71,6 +71,8 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mb_count_columns_workspace_bytes": (_i64, [_i64, _i64]),
     "mb_count_columns": (_int, [_vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp]),
     "mb_count_columns_noalloc": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
+    "mb_pack_count_workspace_bytes": (_i64, [_i64, _i64]),
+    "mb_pack_count_spikes": (_int, [_int, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp]),
 }
 
 EXPORTED_SYMBOLS = tuple(_SIGNATURES)
@@ -275,3 +277,23 @@ def count_columns(
             stream_handle(words.device),
         )
     check(status, "mb_count_columns")
+
+
+def pack_count(
+    spikes: torch.Tensor,
+    words: torch.Tensor,
+    rows: int,
+    n: int,
+    counts64: torch.Tensor | None,
+    counts32: torch.Tensor | None,
+) -> None:
+    """Pack ``spikes[rows, n]`` into ``words`` and count spikes per neuron in one call."""
+
+    need = int(lib().mb_pack_count_workspace_bytes(rows, n))
+    workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=spikes.device)
+    with torch.cuda.device(spikes.device):
+        status = lib().mb_pack_count_spikes(
+            dtype_code(spikes.dtype), ptr(spikes), ptr(words), rows, n, ptr(counts64),
+            ptr(counts32), ptr(workspace), need, stream_handle(spikes.device),
+        )
+    check(status, "mb_pack_count_spikes")

@@ -311,5 +311,32 @@ def count_columns(words: torch.Tensor, rows: int, n: int, wide: bool = True) -> 
     return _count_columns_impl(words, rows, n, wide)
 
 
+def _pack_count_impl(spikes: torch.Tensor, rows: int, n: int,
+                     wide: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    words = torch.empty((rows, (n + 31) // 32), dtype=torch.int32, device=spikes.device)
+    counts = torch.empty((n,), dtype=torch.int64 if wide else torch.int32, device=spikes.device)
+    nat.pack_count(spikes, words, rows, n, counts if wide else None, None if wide else counts)
+    return words, counts
+
+
+pack_count_op = torch.library.custom_op(f"{_NS}::pack_count_spikes", _pack_count_impl,
+                                        mutates_args=())
+
+
+@pack_count_op.register_fake
+def _pack_count_fake(spikes, rows, n, wide):
+    return (spikes.new_empty((rows, (n + 31) // 32), dtype=torch.int32),
+            spikes.new_empty((n,), dtype=torch.int64 if wide else torch.int32))
+
+
+def pack_count(spikes: torch.Tensor, rows: int, n: int,
+               wide: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
+    """Packed words ``[rows, ceil(n/32)]`` and per-neuron counts ``[n]`` in one call."""
+
+    if _tracing():
+        return pack_count_op(spikes, rows, n, wide)
+    return _pack_count_impl(spikes, rows, n, wide)
+
+
 OPS = (scan_forward_op, scan_backward_op, gemm_tn_op, pack_op, unpack_op, count_rows_op,
-       count_columns_op)
+       count_columns_op, pack_count_op)

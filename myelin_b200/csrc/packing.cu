@@ -243,6 +243,99 @@ __global__ void __launch_bounds__(256) count_columns_final_kernel(const int32_t*
 }
 
 // ---------------------------------------------------------------------------
+// Fused pack + per-neuron count for 1-byte spikes (bool / uint8 / int8),
+// n % 32 == 0, 16-byte aligned: one pass over the spikes instead of a pack
+// pass plus a count pass over the words.
+//
+// Thread = one word column (32 neurons = 32 bytes of every row); a block's
+// kPackCountThreads threads take consecutive word columns of the rows of its
+// slice. Per row and 4 bytes w:
+//   m   = ((w & 0x7f7f7f7f) + 0x7f7f7f7f | w) & 0x80808080   bit 7 of each
+//         byte set iff the byte is nonzero (no carry crosses a byte)
+//   b   = m >> 7                                             0/1 per byte
+//   (b * 0x01020408) >> 24                                   the 4 bits, LSB =
+//         first byte: each byte's term lands on bit 24 + k; the other
+//         products fall on distinct bits below 24 (no carry) or above 31
+//   acc += b                                                 four 8-bit counters
+// The 8-bit counters are flushed every 255 rows into 32 int32 counters per
+// thread kept in shared memory (registers go to loads in flight instead: rows
+// are processed kRowUnroll at a time, kRowUnroll x 32 bytes per thread).
+// Per-slice partial counts go to the workspace and
+// count_columns_final_kernel sums the slices (deterministic).
+// ---------------------------------------------------------------------------
+constexpr int kRowUnroll = 8;
+constexpr int kPackCountThreads = 128;
+
+__device__ __forceinline__ uint32_t nonzero_bytes(uint32_t w) {
+  return ((((w & 0x7f7f7f7fu) + 0x7f7f7f7fu) | w) & 0x80808080u) >> 7;
+}
+
+__global__ void __launch_bounds__(kPackCountThreads) pack_count_u8_kernel(
+    const uint4* __restrict__ in, uint32_t* __restrict__ words, int32_t* __restrict__ partial,
+    int64_t rows, int64_t W, int64_t rows_per_slice) {
+  __shared__ int32_t cnt[32][kPackCountThreads];  // [neuron in word][thread]: conflict-free
+  const int tid = threadIdx.x;
+  const int64_t wc = int64_t(blockIdx.x) * kPackCountThreads + tid;  // word column
+  const int64_t r_begin = int64_t(blockIdx.y) * rows_per_slice;
+  const int64_t r_end = imin64(rows, r_begin + rows_per_slice);
+  if (wc >= W) return;  // no block-wide barrier below: early exit is safe
+
+#pragma unroll
+  for (int k = 0; k < 32; ++k) cnt[k][tid] = 0;
+  uint32_t acc[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) acc[q] = 0;
+  int pending = 0;  // rows added to the 8-bit counters since the last flush
+
+  auto flush = [&]() {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) cnt[4 * q + k][tid] += (acc[q] >> (8 * k)) & 0xffu;
+      acc[q] = 0;
+    }
+    pending = 0;
+  };
+  auto consume = [&](uint4 lo, uint4 hi, int64_t r) {
+    const uint32_t v[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+    uint32_t word = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const uint32_t b = nonzero_bytes(v[q]);
+      word |= ((b * 0x01020408u) >> 24) << (4 * q);
+      acc[q] += b;
+    }
+    words[r * W + wc] = word;
+  };
+
+  const uint4* src = in + wc * 2;  // 2 x 16 bytes per row
+  const int64_t row_vec = W * 2;
+  int64_t r = r_begin;
+  for (; r + kRowUnroll <= r_end; r += kRowUnroll) {
+    uint4 lo[kRowUnroll], hi[kRowUnroll];
+#pragma unroll
+    for (int u = 0; u < kRowUnroll; ++u) {
+      lo[u] = src[(r + u) * row_vec];
+      hi[u] = src[(r + u) * row_vec + 1];
+    }
+#pragma unroll
+    for (int u = 0; u < kRowUnroll; ++u) consume(lo[u], hi[u], r + u);
+    pending += kRowUnroll;
+    if (pending > 255 - kRowUnroll) flush();
+  }
+  for (; r < r_end; ++r) {
+    consume(src[r * row_vec], src[r * row_vec + 1], r);
+    if (++pending == 255) flush();
+  }
+  flush();
+  int4* dst = reinterpret_cast<int4*>(partial + int64_t(blockIdx.y) * W * 32 + wc * 32);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    dst[k] = make_int4(cnt[4 * k][tid], cnt[4 * k + 1][tid], cnt[4 * k + 2][tid], cnt[4 * k + 3][tid]);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side.
 // ---------------------------------------------------------------------------
 static int grid_for(int64_t work_items, int block = 256) {
@@ -323,6 +416,52 @@ int64_t count_columns_workspace_bytes(int64_t rows, int64_t n) {
   return column_slices(rows, n) * n * int64_t(sizeof(int32_t));
 }
 
+// Row slices of the fused pack + count: about five blocks per SM (the register
+// limit; each thread keeps kRowUnroll x 32 bytes in flight), at least 64 rows
+// each.
+static int64_t pack_count_slices(int64_t rows, int64_t n) {
+  const int64_t col_blocks = ceil_div(n / 32, kPackCountThreads);
+  int64_t slices = ceil_div(148 * 5, col_blocks);
+  const int64_t max_by_rows = ceil_div(rows, 64);
+  if (slices > max_by_rows) slices = max_by_rows;
+  if (slices < 1) slices = 1;
+  return slices;
+}
+
+static bool pack_count_fused_ok(int dtype, const void* spikes, int64_t n, const void* workspace) {
+  return dtype == MB_U8 && n % 32 == 0 && aligned_to(spikes, 16) && aligned_to(workspace, 16);
+}
+
+int64_t pack_count_workspace_bytes(int64_t rows, int64_t n) {
+  if (rows <= 0 || n <= 0) return 0;
+  const int64_t fused = n % 32 == 0 ? pack_count_slices(rows, n) * n * int64_t(sizeof(int32_t)) : 0;
+  const int64_t split = count_columns_workspace_bytes(rows, n);
+  return fused > split ? fused : split;
+}
+
+// Pack + per-neuron count: one fused pass for aligned 1-byte spikes with
+// n % 32 == 0, else the pack kernel followed by the column count of the words.
+template <int DT>
+static void launch_pack_count(const void* spikes, int32_t* words, int64_t rows, int64_t n,
+                              int64_t* counts64, int32_t* counts32, void* workspace,
+                              cudaStream_t s) {
+  if (pack_count_fused_ok(DT, spikes, n, workspace)) {
+    const int64_t W = n / 32;
+    const int64_t slices = pack_count_slices(rows, n);
+    dim3 grid(static_cast<unsigned>(ceil_div(W, kPackCountThreads)),
+              static_cast<unsigned>(slices));
+    pack_count_u8_kernel<<<grid, kPackCountThreads, 0, s>>>(static_cast<const uint4*>(spikes),
+                                              reinterpret_cast<uint32_t*>(words),
+                                              static_cast<int32_t*>(workspace), rows, W,
+                                              ceil_div(rows, slices));
+    count_columns_final_kernel<<<grid_for(n), 256, 0, s>>>(static_cast<int32_t*>(workspace),
+                                                           slices, n, counts64, counts32);
+    return;
+  }
+  launch_pack<DT>(spikes, words, rows, n, s);
+  launch_count_columns(words, rows, n, counts64, counts32, static_cast<int32_t*>(workspace), s);
+}
+
 }  // namespace mb
 
 using namespace mb;
@@ -394,6 +533,36 @@ extern "C" int mb_count_columns(const int32_t* words, int64_t rows, int64_t n, i
   MB_CHECK_ARG(aligned_to(workspace, 4), "mb_count_columns: workspace misaligned");
   launch_count_columns(words, rows, n, counts64, counts32, static_cast<int32_t*>(workspace), s);
   MB_CHECK_LAUNCH("mb_count_columns");
+  return 0;
+}
+
+extern "C" int64_t mb_pack_count_workspace_bytes(int64_t rows, int64_t n) {
+  return pack_count_workspace_bytes(rows, n);
+}
+
+extern "C" int mb_pack_count_spikes(int dtype, const void* spikes, int32_t* words, int64_t rows,
+                                    int64_t n, int64_t* counts64, int32_t* counts32,
+                                    void* workspace, int64_t workspace_bytes, void* stream) {
+  clear_error();
+  MB_CHECK_ARG(valid_io_dtype(dtype), "mb_pack_count_spikes: unknown dtype %d", dtype);
+  MB_CHECK_ARG(rows >= 0 && n > 0, "mb_pack_count_spikes: cannot pack an empty last dimension");
+  MB_CHECK_ARG(counts64 != nullptr || counts32 != nullptr, "mb_pack_count_spikes: no output");
+  cudaStream_t s = as_stream(stream);
+  if (rows == 0) {
+    if (counts64) cudaMemsetAsync(counts64, 0, n * sizeof(int64_t), s);
+    if (counts32) cudaMemsetAsync(counts32, 0, n * sizeof(int32_t), s);
+    MB_CHECK_LAUNCH("mb_pack_count_spikes");
+    return 0;
+  }
+  MB_CHECK_ARG(spikes != nullptr && words != nullptr, "mb_pack_count_spikes: null pointer");
+  const int64_t need = pack_count_workspace_bytes(rows, n);
+  MB_CHECK_ARG(workspace != nullptr && workspace_bytes >= need,
+               "mb_pack_count_spikes: workspace of %lld bytes required, got %lld",
+               (long long)need, (long long)workspace_bytes);
+  MB_CHECK_ARG(aligned_to(workspace, 4), "mb_pack_count_spikes: workspace misaligned");
+  MB_DISPATCH_DTYPE(dtype, launch_pack_count, spikes, words, rows, n, counts64, counts32,
+                    workspace, s);
+  MB_CHECK_LAUNCH("mb_pack_count_spikes");
   return 0;
 }
 

@@ -76,6 +76,33 @@ def pack_spikes(spikes: torch.Tensor) -> PackedSpikes:
     return PackedSpikes(data=words, original_shape=original_shape)
 
 
+def pack_spikes_with_counts(
+    spikes: torch.Tensor, *, dtype: torch.dtype = torch.int64
+) -> tuple[PackedSpikes, torch.Tensor]:
+    """``pack_spikes(spikes)`` and its per-neuron counts over every leading dimension.
+
+    Equals ``(p, packed_spike_counts_over_leading_dims(p, dtype=dtype))`` for
+    ``p = pack_spikes(spikes)``, computed in one pass over the spikes for
+    aligned 1-byte inputs (bool / uint8 / int8) whose last dimension is a
+    multiple of 32 — the step before a packed all-gather and a count
+    all-reduce (src/myelin/distributed.py:63-109). Not in the reference API.
+    """
+
+    if spikes.ndim == 0:
+        raise ValueError("spikes must have at least one dimension")
+    if spikes.shape[-1] == 0:
+        raise ValueError("cannot pack an empty last dimension")
+    if dtype not in (torch.int64, torch.int32):
+        raise ValueError("dtype must be torch.int64 or torch.int32")
+    nat.require_cuda(spikes, "spikes")
+    original_shape = tuple(spikes.shape)
+    n = original_shape[-1]
+    words, counts = cops.pack_count(spikes.contiguous(), _rows(original_shape), n,
+                                    wide=dtype == torch.int64)
+    words = words.view(*original_shape[:-1], packed_last_dim_size(n))
+    return PackedSpikes(data=words, original_shape=original_shape), counts
+
+
 def unpack_spikes(packed: PackedSpikes, *, dtype: torch.dtype = torch.float32) -> torch.Tensor:
     """Unpack to the original shape with 0/1 values of ``dtype``."""
 

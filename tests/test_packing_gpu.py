@@ -103,3 +103,46 @@ def test_config4_shard_properties(oracle):
     # one slice against the oracle bit for bit
     sl = spikes[:4].cpu().numpy()
     assert np.array_equal(packed.data[:4].cpu().numpy(), oracle.pack(sl))
+
+
+@pytest.mark.parametrize("n", WIDTHS)
+def test_pack_with_counts_matches_reference_golden(n):
+    g = load_golden("packing")
+    spikes = torch.from_numpy(g[f"spikes_{n}"]).to(DEV)
+    packed, counts = mb.pack_spikes_with_counts(spikes)
+    assert np.array_equal(packed.data.cpu().numpy(), g[f"packed_{n}"])
+    assert counts.dtype == torch.int64
+    assert np.array_equal(counts.cpu().numpy(), g[f"cols_{n}"])
+
+
+@pytest.mark.parametrize("dtype", [torch.bool, torch.uint8, torch.int8, torch.float32,
+                                   torch.bfloat16])
+@pytest.mark.parametrize("shape", [(3, 1, 32), (5, 7, 64), (300, 96), (37, 3, 256),
+                                   (1000, 8192), (6, 5, 33), (2, 513)])
+@pytest.mark.parametrize("count_dtype", [torch.int64, torch.int32])
+def test_pack_with_counts_matches_oracle(oracle, dtype, shape, count_dtype):
+    """Fused path (1-byte, n % 32 == 0) and the pack-then-count path agree
+    bit for bit with the oracle, including 1-byte values other than 0/1."""
+
+    spikes = _random_spikes(shape, dtype, hash((shape, str(dtype), "pc")) % 991)
+    if dtype in (torch.uint8, torch.int8):
+        spikes.view(-1)[:7] = torch.tensor([1, 2, 127, -128 if dtype == torch.int8 else 128, 255
+                                            if dtype == torch.uint8 else -1, 0, 64]).to(dtype)
+    host = spikes.float().numpy() if dtype == torch.bfloat16 else spikes.numpy()
+    packed, counts = mb.pack_spikes_with_counts(spikes.to(DEV), dtype=count_dtype)
+    assert np.array_equal(packed.data.cpu().numpy(), oracle.pack(host))
+    n = shape[-1]
+    expected = (host.reshape(-1, n) != 0).sum(axis=0)
+    assert counts.dtype == count_dtype
+    assert np.array_equal(counts.cpu().numpy().astype(np.int64), expected)
+
+
+def test_pack_with_counts_long_columns_flush():
+    """More rows than the 8-bit counters hold between flushes (255), all ones:
+    every column count equals the row count."""
+
+    rows, n = 70000, 64
+    spikes = torch.ones((rows, n), dtype=torch.bool, device=DEV)
+    packed, counts = mb.pack_spikes_with_counts(spikes)
+    assert bool(torch.all(counts == rows))
+    assert bool(torch.all(packed.data == -1))
