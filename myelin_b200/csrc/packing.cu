@@ -229,16 +229,30 @@ __global__ void __launch_bounds__(256) count_columns_partial_kernel(
   }
 }
 
+// Sum of the per-slice partial counts: block = 32 neurons, its 8 warps take
+// interleaved slices (coalesced 128-byte rows), then warp 0 adds the 8 warp
+// sums in a fixed order (deterministic).
 __global__ void __launch_bounds__(256) count_columns_final_kernel(const int32_t* __restrict__ partial,
                                                                   int64_t slices, int64_t n,
                                                                   int64_t* __restrict__ out64,
                                                                   int32_t* __restrict__ out32) {
-  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
-  for (int64_t j = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; j < n; j += stride) {
-    int64_t s = 0;
-    for (int64_t q = 0; q < slices; ++q) s += partial[q * n + j];
-    if (out64) out64[j] = s;
-    if (out32) out32[j] = static_cast<int32_t>(s);
+  __shared__ int64_t red[8][32];
+  const int lane = threadIdx.x & 31;
+  const int wid = threadIdx.x >> 5;
+  const int64_t j = int64_t(blockIdx.x) * 32 + lane;
+  int64_t s = 0;
+  if (j < n) {
+#pragma unroll 4
+    for (int64_t q = wid; q < slices; q += 8) s += partial[q * n + j];
+  }
+  red[wid][lane] = s;
+  __syncthreads();
+  if (wid == 0 && j < n) {
+    int64_t t = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += red[w][lane];
+    if (out64) out64[j] = t;
+    if (out32) out32[j] = static_cast<int32_t>(t);
   }
 }
 
@@ -270,6 +284,9 @@ __device__ __forceinline__ uint32_t nonzero_bytes(uint32_t w) {
   return ((((w & 0x7f7f7f7fu) + 0x7f7f7f7fu) | w) & 0x80808080u) >> 7;
 }
 
+// COUNT = false packs only (the plain pack of 1-byte spikes: no counters, no
+// partials).
+template <bool COUNT>
 __global__ void __launch_bounds__(kPackCountThreads) pack_count_u8_kernel(
     const uint4* __restrict__ in, uint32_t* __restrict__ words, int32_t* __restrict__ partial,
     int64_t rows, int64_t W, int64_t rows_per_slice) {
@@ -280,19 +297,23 @@ __global__ void __launch_bounds__(kPackCountThreads) pack_count_u8_kernel(
   const int64_t r_end = imin64(rows, r_begin + rows_per_slice);
   if (wc >= W) return;  // no block-wide barrier below: early exit is safe
 
+  if (COUNT) {
 #pragma unroll
-  for (int k = 0; k < 32; ++k) cnt[k][tid] = 0;
+    for (int k = 0; k < 32; ++k) cnt[k][tid] = 0;
+  }
   uint32_t acc[8];
 #pragma unroll
   for (int q = 0; q < 8; ++q) acc[q] = 0;
   int pending = 0;  // rows added to the 8-bit counters since the last flush
 
   auto flush = [&]() {
+    if constexpr (COUNT) {
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
+      for (int q = 0; q < 8; ++q) {
 #pragma unroll
-      for (int k = 0; k < 4; ++k) cnt[4 * q + k][tid] += (acc[q] >> (8 * k)) & 0xffu;
-      acc[q] = 0;
+        for (int k = 0; k < 4; ++k) cnt[4 * q + k][tid] += (acc[q] >> (8 * k)) & 0xffu;
+        acc[q] = 0;
+      }
     }
     pending = 0;
   };
@@ -303,7 +324,7 @@ __global__ void __launch_bounds__(kPackCountThreads) pack_count_u8_kernel(
     for (int q = 0; q < 8; ++q) {
       const uint32_t b = nonzero_bytes(v[q]);
       word |= ((b * 0x01020408u) >> 24) << (4 * q);
-      acc[q] += b;
+      if (COUNT) acc[q] += b;
     }
     words[r * W + wc] = word;
   };
@@ -327,6 +348,7 @@ __global__ void __launch_bounds__(kPackCountThreads) pack_count_u8_kernel(
     consume(src[r * row_vec], src[r * row_vec + 1], r);
     if (++pending == 255) flush();
   }
+  if (!COUNT) return;
   flush();
   int4* dst = reinterpret_cast<int4*>(partial + int64_t(blockIdx.y) * W * 32 + wc * 32);
 #pragma unroll
@@ -346,12 +368,22 @@ static int grid_for(int64_t work_items, int block = 256) {
   return static_cast<int>(g);
 }
 
+static int64_t pack_count_slices(int64_t rows, int64_t n);
+
 template <int DT>
 static void launch_pack(const void* spikes, int32_t* words, int64_t rows, int64_t n,
                         cudaStream_t s) {
   using U = typename Raw<DT>::U;
   const int64_t W = ceil_div(n, 32);
-  if (n % 32 == 0 && aligned_to(spikes, 16)) {
+  if (DT == MB_U8 && n % 32 == 0 && aligned_to(spikes, 16)) {
+    // 1-byte spikes: the fused kernel without its counters (8 rows in flight)
+    const int64_t slices = pack_count_slices(rows, n);
+    dim3 grid(static_cast<unsigned>(ceil_div(W, kPackCountThreads)),
+              static_cast<unsigned>(slices));
+    pack_count_u8_kernel<false><<<grid, kPackCountThreads, 0, s>>>(
+        static_cast<const uint4*>(spikes), reinterpret_cast<uint32_t*>(words), nullptr, rows, W,
+        ceil_div(rows, slices));
+  } else if (n % 32 == 0 && aligned_to(spikes, 16)) {
     const int64_t n_vec = rows * n * int64_t(sizeof(U)) / 16;
     pack_vec_kernel<DT><<<grid_for(n_vec), 256, 0, s>>>(static_cast<const uint4*>(spikes), words,
                                                         n_vec);
@@ -407,7 +439,7 @@ int launch_count_columns(const int32_t* words, int64_t rows, int64_t n, int64_t*
   dim3 grid(static_cast<unsigned>(ceil_div(W, 32)), static_cast<unsigned>(slices));
   count_columns_partial_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const uint32_t*>(words),
                                                     workspace, rows, W, n, rows_per_slice);
-  count_columns_final_kernel<<<grid_for(n), 256, 0, s>>>(workspace, slices, n, counts64, counts32);
+  count_columns_final_kernel<<<static_cast<unsigned>(ceil_div(n, 32)), 256, 0, s>>>(workspace, slices, n, counts64, counts32);
   return 0;
 }
 
@@ -450,11 +482,11 @@ static void launch_pack_count(const void* spikes, int32_t* words, int64_t rows, 
     const int64_t slices = pack_count_slices(rows, n);
     dim3 grid(static_cast<unsigned>(ceil_div(W, kPackCountThreads)),
               static_cast<unsigned>(slices));
-    pack_count_u8_kernel<<<grid, kPackCountThreads, 0, s>>>(static_cast<const uint4*>(spikes),
+    pack_count_u8_kernel<true><<<grid, kPackCountThreads, 0, s>>>(static_cast<const uint4*>(spikes),
                                               reinterpret_cast<uint32_t*>(words),
                                               static_cast<int32_t*>(workspace), rows, W,
                                               ceil_div(rows, slices));
-    count_columns_final_kernel<<<grid_for(n), 256, 0, s>>>(static_cast<int32_t*>(workspace),
+    count_columns_final_kernel<<<static_cast<unsigned>(ceil_div(n, 32)), 256, 0, s>>>(static_cast<int32_t*>(workspace),
                                                            slices, n, counts64, counts32);
     return;
   }
