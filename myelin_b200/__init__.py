@@ -27,6 +27,7 @@ from myelin_b200.kernels import (
     lif_forward_packed_spikes,
     linear_surrogate_lif_forward,
     linear_surrogate_lif_packed_forward,
+    two_layer_surrogate_lif_rate_packed_hidden_forward,
     linear_surrogate_lif_rate_forward,
     surrogate_alif_forward,
     surrogate_lif_forward,

@@ -179,3 +179,81 @@ class LinearScanFunction(torch.autograd.Function):
         grad_weight = torch.mm(inputs.reshape(T * B, F).t(), g2) if need_w else None
         grad_bias = g2.sum(dim=0) if (need_b and ctx.has_bias) else None
         return (grad_inputs, grad_weight, grad_bias, *tail)
+
+
+class TwoLayerPackedHiddenRateFunction(torch.autograd.Function):
+    """Two stream-synapse LIF layers: hidden spikes, then output spike rates,
+    with the hidden spikes kept bit-packed between forward and backward.
+
+    Forward: currents1 = X W1 + b1 -> scan writing packed hidden words (and
+    checkpoints) -> hidden = unpack(words), transient -> currents2 = hidden W2
+    + b2 -> rate scan. Saved: inputs, weights, biases, the two layers'
+    checkpoints and the packed words (1 bit per hidden spike instead of a
+    dense [T, B, H] tensor and two current tensors). Backward recomputes both
+    projections (same deterministic kernels, so the same bits) and runs the
+    two reverse scans. Reference: src/myelin/autograd.py:1129-1387.
+    """
+
+    @staticmethod
+    def forward(ctx: Any, inputs, hidden_weight, hidden_bias, output_weight, output_bias,
+                decay: float, threshold: float, reset: float, surrogate: int, slope: float):
+        T, B, F = inputs.shape
+        H = hidden_weight.shape[1]
+        O = output_weight.shape[1]
+        save = any(ctx.needs_input_grad[:5])
+        cur1 = _project(inputs.reshape(T * B, F), hidden_weight, hidden_bias).view(T, B, H)
+        v0 = torch.zeros((B, H), dtype=inputs.dtype, device=inputs.device)
+        _, _, _, words, _, ckpt1, _ = cops.scan_forward(
+            cur1, v0, None, nat.MB_LIF, decay, threshold, reset, 0.0, 0.0, nat.MB_RESET_HARD,
+            packed=True, checkpoints=save,
+        )
+        del cur1
+        hidden = cops.unpack(words, T * B, H, inputs.dtype)
+        cur2 = _project(hidden, output_weight, output_bias).view(T, B, O)
+        del hidden
+        vo = torch.zeros((B, O), dtype=inputs.dtype, device=inputs.device)
+        _, _, _, _, rates, ckpt2, _ = cops.scan_forward(
+            cur2, vo, None, nat.MB_LIF, decay, threshold, reset, 0.0, 0.0, nat.MB_RESET_HARD,
+            rates=True, checkpoints=save,
+        )
+        ctx.set_materialize_grads(False)
+        ctx.save_for_backward(inputs, hidden_weight, hidden_bias, output_weight, output_bias,
+                              ckpt1, ckpt2, words)
+        ctx.cfg = (decay, threshold, reset, surrogate, slope)
+        return rates
+
+    @staticmethod
+    def backward(ctx: Any, g_rates):
+        tail = (None,) * 5
+        if g_rates is None:
+            return (None,) * 5 + tail
+        inputs, w1, b1, w2, b2, ckpt1, ckpt2, words = ctx.saved_tensors
+        decay, threshold, reset, surrogate, slope = ctx.cfg
+        need_x, need_w1, need_b1, need_w2, need_b2 = ctx.needs_input_grad[:5]
+        T, B, F = inputs.shape
+        H, O = w1.shape[1], w2.shape[1]
+        scan_kw = dict(neuron=nat.MB_LIF, decay=decay, threshold=threshold, reset=reset,
+                       adapt_decay=0.0, beta=0.0, reset_mode=nat.MB_RESET_HARD,
+                       surrogate=surrogate, slope=slope, need_v0=False, need_a0=False)
+
+        hidden = cops.unpack(words, T * B, H, inputs.dtype)  # [T*B, H]
+        cur2 = _project(hidden, w2, b2).view(T, B, O)
+        g_cur2, _, _ = cops.scan_backward(cur2, ckpt2, None, grad_rates=g_rates, **scan_kw)
+        del cur2
+        g2 = g_cur2.view(T * B, O)
+        grad_w2 = torch.mm(hidden.t(), g2) if need_w2 else None
+        grad_b2 = g2.sum(dim=0) if (need_b2 and b2 is not None) else None
+        del hidden
+
+        grad_x = grad_w1 = grad_b1 = None
+        if need_x or need_w1 or need_b1:
+            g_hidden = _input_grad(g2, w2).view(T, B, H)
+            x2 = inputs.reshape(T * B, F)
+            cur1 = _project(x2, w1, b1).view(T, B, H)
+            g_cur1, _, _ = cops.scan_backward(cur1, ckpt1, None, grad_spikes=g_hidden, **scan_kw)
+            del cur1, g_hidden
+            g1 = g_cur1.view(T * B, H)
+            grad_x = _input_grad(g1, w1).view(T, B, F) if need_x else None
+            grad_w1 = torch.mm(x2.t(), g1) if need_w1 else None
+            grad_b1 = g1.sum(dim=0) if (need_b1 and b1 is not None) else None
+        return (grad_x, grad_w1, grad_b1, grad_w2, grad_b2, *tail)

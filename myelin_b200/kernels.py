@@ -25,6 +25,7 @@ from myelin_b200.autograd import (
     ALIFScanFunction,
     LIFScanFunction,
     LinearScanFunction,
+    TwoLayerPackedHiddenRateFunction,
     _project,
 )
 from myelin_b200.checkpointing import CheckpointSize, resolve_checkpoint_size
@@ -376,6 +377,55 @@ def linear_surrogate_lif_rate_forward(
     if reduction == "mean":
         return LIFState(membrane=vT), rates.mean()
     return LIFState(membrane=vT), rates
+
+
+def two_layer_surrogate_lif_rate_packed_hidden_forward(
+    inputs: torch.Tensor,
+    hidden_weight: torch.Tensor,
+    hidden_bias: torch.Tensor | None,
+    output_weight: torch.Tensor,
+    output_bias: torch.Tensor | None,
+    params: LIFParams,
+    *,
+    surrogate: SurrogateName = "fast_sigmoid",
+    surrogate_slope: float = 5.0,
+    hard_forward: bool = True,
+    checkpoint_size: CheckpointSize = 25,
+    block_b: int = 16,
+    block_n: int = 32,
+    block_f: int = 32,
+) -> torch.Tensor:
+    """Two-layer LIF rate model storing the hidden spikes bit-packed.
+
+    Rates ``[B, O]`` of ``linear_surrogate_lif_rate_forward`` applied to the
+    spikes of ``linear_surrogate_lif_forward``; between forward and backward
+    the hidden spikes are kept as packed words (src/myelin/kernels.py:811-846,
+    src/myelin/autograd.py:1129-1387). Tile arguments are accepted and ignored.
+    """
+
+    sid = surrogate_id(surrogate)
+    resolve_checkpoint_size(int(inputs.shape[0]), checkpoint_size)
+    if not hard_forward:
+        raise ValueError("packed-hidden two-layer rate training supports only hard_forward=True")
+    _validate_linear(inputs, hidden_weight, hidden_bias)
+    if output_weight.ndim != 2 or output_weight.shape[0] != hidden_weight.shape[1]:
+        raise ValueError("output_weight must be shaped [hidden_features, output_features]")
+    if output_bias is not None and tuple(output_bias.shape) != (output_weight.shape[1],):
+        raise ValueError("output_bias must be shaped [output_features]")
+    if output_weight.dtype != inputs.dtype or output_weight.device != inputs.device:
+        raise ValueError("output_weight must match the inputs' dtype and device")
+    return TwoLayerPackedHiddenRateFunction.apply(
+        inputs.contiguous(),
+        hidden_weight.contiguous(),
+        None if hidden_bias is None else hidden_bias.contiguous(),
+        output_weight.contiguous(),
+        None if output_bias is None else output_bias.contiguous(),
+        params.decay,
+        float(params.threshold),
+        float(params.reset),
+        sid,
+        float(surrogate_slope),
+    )
 
 
 def linear_surrogate_lif_packed_forward(
