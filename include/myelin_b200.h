@@ -40,6 +40,20 @@ enum mb_dtype {
 /* Neuron models on the scan path. */
 enum mb_neuron { MB_LIF = 0, MB_ALIF = 1 };
 
+/* Izhikevich parameters, the fields and defaults of the reference's
+ * IzhikevichParams (src/myelin/neurons.py:74-96); dt must be positive. */
+typedef struct mb_izhikevich_params {
+  float recovery_decay;       /* a, default 0.02 */
+  float recovery_coupling;    /* b, default 0.2 */
+  float reset_voltage;        /* default -65 */
+  float recovery_jump;        /* default 8 */
+  float threshold;            /* default 30 */
+  float dt;                   /* default 1 */
+  float voltage_square_coeff; /* default 0.04 */
+  float voltage_coeff;        /* default 5 */
+  float voltage_bias;         /* default 140 */
+} mb_izhikevich_params;
+
 /* Reset rule after a spike: HARD sets the membrane to `reset`
  * (src/myelin/neurons.py:113, functional.py:143); SUBTRACT removes the
  * (adaptive) threshold, m <- p - theta (extension, not in the reference). */
@@ -129,6 +143,23 @@ int mb_scan_backward(int neuron, int dtype, const void* x, const float* ckpt_v,
                      void* grad_a0, int64_t T, int64_t B, int64_t N, float decay,
                      float threshold, float reset, float adapt_decay, float beta,
                      int reset_mode, int surrogate, float slope, void* stream);
+
+/*
+ * Fused-time Izhikevich forward over x[T,B,N] (dtype MB_F32/BF16/F16):
+ *   dv  = ((c2 * v) * v + c1 * v) + bias - u + x_t     (one rounding per op)
+ *   p_v = v + dt * dv;   p_u = u + dt * (a * (b * v - u))
+ *   s_t = p_v >= threshold
+ *   v = s_t ? reset_voltage : p_v;   u = s_t ? p_u + recovery_jump : p_u
+ * Inputs: x, v0, u0 [B,N]. Outputs (each may be NULL): vT, uT [B,N] and dense
+ * 0/1 spikes [T,B,N], all of dtype. fp32 state carry; bit-exact with the
+ * reference's torch path for fp32. Forward only.
+ * Replaces: kernels.izhikevich_forward (src/myelin/kernels.py:202-246) ->
+ *   triton/generated.py:1192-1227 / functional.izhikevich_unroll
+ *   (functional.py:81-112).
+ */
+int mb_izhikevich_forward(int dtype, const void* x, const void* v0, const void* u0, void* vT,
+                          void* uT, void* spikes, int64_t T, int64_t B, int64_t N,
+                          const mb_izhikevich_params* params, void* stream);
 
 /*
  * Dense projection on the tcgen05 tensor cores:

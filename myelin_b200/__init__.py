@@ -22,6 +22,8 @@ from myelin_b200.distributed import (
 from myelin_b200.kernels import (
     Backend,
     alif_forward,
+    izhikevich_forward,
+    izhikevich_step,
     fused_lif_unroll,
     lif_forward,
     lif_forward_packed_spikes,
@@ -34,6 +36,7 @@ from myelin_b200.kernels import (
 )
 from myelin_b200.modules import (
     ALIFCell,
+    IzhikevichCell,
     LIFCell,
     LinearLIF,
     LinearSurrogateLIF,
@@ -45,7 +48,14 @@ from myelin_b200.modules import (
     SurrogateLIFCell,
     TimeUnroll,
 )
-from myelin_b200.neurons import ALIFParams, ALIFState, LIFParams, LIFState
+from myelin_b200.neurons import (
+    ALIFParams,
+    ALIFState,
+    IzhikevichParams,
+    IzhikevichState,
+    LIFParams,
+    LIFState,
+)
 from myelin_b200.packing import (
     BITS_PER_WORD,
     PackedSpikes,

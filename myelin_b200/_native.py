@@ -73,6 +73,9 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mb_count_columns_noalloc": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "mb_pack_count_workspace_bytes": (_i64, [_i64, _i64]),
     "mb_pack_count_spikes": (_int, [_int, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp]),
+    "mb_izhikevich_forward": (
+        _int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp]
+    ),
 }
 
 EXPORTED_SYMBOLS = tuple(_SIGNATURES)
@@ -297,3 +300,29 @@ def pack_count(
             ptr(counts32), ptr(workspace), need, stream_handle(spikes.device),
         )
     check(status, "mb_pack_count_spikes")
+
+
+class IzhikevichParamsC(ctypes.Structure):
+    """``mb_izhikevich_params`` (include/myelin_b200.h)."""
+
+    _fields_ = [(name, ctypes.c_float) for name in (
+        "recovery_decay", "recovery_coupling", "reset_voltage", "recovery_jump", "threshold",
+        "dt", "voltage_square_coeff", "voltage_coeff", "voltage_bias")]
+
+
+def izhikevich_forward(
+    x: torch.Tensor,
+    v0: torch.Tensor,
+    u0: torch.Tensor,
+    vT: torch.Tensor | None,
+    uT: torch.Tensor | None,
+    spikes: torch.Tensor | None,
+    params: IzhikevichParamsC,
+) -> None:
+    T, B, N = x.shape
+    with torch.cuda.device(x.device):
+        status = lib().mb_izhikevich_forward(
+            dtype_code(x.dtype), ptr(x), ptr(v0), ptr(u0), ptr(vT), ptr(uT), ptr(spikes),
+            T, B, N, ctypes.addressof(params), stream_handle(x.device),
+        )
+    check(status, "mb_izhikevich_forward")

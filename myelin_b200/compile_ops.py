@@ -338,5 +338,37 @@ def pack_count(spikes: torch.Tensor, rows: int, n: int,
     return _pack_count_impl(spikes, rows, n, wide)
 
 
+IZH_FIELDS = ("recovery_decay", "recovery_coupling", "reset_voltage", "recovery_jump",
+              "threshold", "dt", "voltage_square_coeff", "voltage_coeff", "voltage_bias")
+
+
+def _izhikevich_impl(x: torch.Tensor, v0: torch.Tensor, u0: torch.Tensor,
+                     params: list[float]) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    vT = torch.empty_like(v0)
+    uT = torch.empty_like(u0)
+    spikes = torch.empty_like(x)
+    nat.izhikevich_forward(x, v0, u0, vT, uT, spikes,
+                           nat.IzhikevichParamsC(*[float(p) for p in params]))
+    return vT, uT, spikes
+
+
+izhikevich_op = torch.library.custom_op(f"{_NS}::izhikevich_forward", _izhikevich_impl,
+                                        mutates_args=())
+
+
+@izhikevich_op.register_fake
+def _izhikevich_fake(x, v0, u0, params):
+    return torch.empty_like(v0), torch.empty_like(u0), torch.empty_like(x)
+
+
+def izhikevich_forward(x: torch.Tensor, v0: torch.Tensor, u0: torch.Tensor,
+                       params: list[float]) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Fused-time Izhikevich forward: (vT, uT, spikes); ``params`` in IZH_FIELDS order."""
+
+    if _tracing():
+        return izhikevich_op(x, v0, u0, list(params))
+    return _izhikevich_impl(x, v0, u0, list(params))
+
+
 OPS = (scan_forward_op, scan_backward_op, gemm_tn_op, pack_op, unpack_op, count_rows_op,
-       count_columns_op, pack_count_op)
+       count_columns_op, pack_count_op, izhikevich_op)

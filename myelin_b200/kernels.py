@@ -29,7 +29,14 @@ from myelin_b200.autograd import (
     _project,
 )
 from myelin_b200.checkpointing import CheckpointSize, resolve_checkpoint_size
-from myelin_b200.neurons import ALIFParams, ALIFState, LIFParams, LIFState
+from myelin_b200.neurons import (
+    ALIFParams,
+    ALIFState,
+    IzhikevichParams,
+    IzhikevichState,
+    LIFParams,
+    LIFState,
+)
 from myelin_b200.packing import PackedSpikes
 from myelin_b200.surrogates import SurrogateName, surrogate_id
 
@@ -377,6 +384,76 @@ def linear_surrogate_lif_rate_forward(
     if reduction == "mean":
         return LIFState(membrane=vT), rates.mean()
     return LIFState(membrane=vT), rates
+
+
+def _izhikevich_params(params: IzhikevichParams) -> list[float]:
+    params.validate()
+    return [float(getattr(params, k)) for k in cops.IZH_FIELDS]
+
+
+def izhikevich_forward(
+    inputs: torch.Tensor,
+    initial_state: IzhikevichState,
+    params: IzhikevichParams,
+    *,
+    backend: Backend = "auto",
+    block_size: int = 256,
+) -> tuple[IzhikevichState, torch.Tensor]:
+    """Fused-time Izhikevich forward (src/myelin/kernels.py:202-246).
+
+    Spikes and final states are bit-exact with ``izhikevich_unroll`` for
+    fp32 inputs. Forward only, like the reference's generated kernel: no
+    gradient flows through it. Every ``backend`` runs the CUDA kernel.
+    """
+
+    _check_backend(backend)
+    values = _izhikevich_params(params)
+    if inputs.ndim != 3:
+        raise ValueError(f"inputs must be shaped [T, B, N]; got {tuple(inputs.shape)}")
+    expected = inputs.shape[1:]
+    for name, t in (("voltage", initial_state.voltage), ("recovery", initial_state.recovery)):
+        if t.shape != expected:
+            raise ValueError(
+                f"initial_state.{name} must match inputs.shape[1:]; "
+                f"got {tuple(t.shape)} and {tuple(expected)}"
+            )
+    nat.require_cuda(inputs)
+    for name, t in (("voltage", initial_state.voltage), ("recovery", initial_state.recovery)):
+        if t.device != inputs.device or t.dtype != inputs.dtype:
+            raise ValueError(f"initial_state.{name} must have the same device and dtype as inputs")
+    if inputs.dtype not in nat.SCAN_DTYPES:
+        raise ValueError(
+            f"inputs must be float32, bfloat16 or float16 for the CUDA scan; got {inputs.dtype}"
+        )
+    with torch.no_grad():
+        vT, uT, spikes = cops.izhikevich_forward(
+            inputs.contiguous(), initial_state.voltage.contiguous(),
+            initial_state.recovery.contiguous(), values,
+        )
+    return IzhikevichState(voltage=vT, recovery=uT), spikes
+
+
+def izhikevich_step(
+    state: IzhikevichState, input_current: torch.Tensor, params: IzhikevichParams
+) -> tuple[IzhikevichState, torch.Tensor]:
+    """Advance one Izhikevich step (src/myelin/neurons.py:204-230), as a T=1 scan."""
+
+    params.validate()
+    for name, t in (("voltage", state.voltage), ("recovery", state.recovery)):
+        if t.shape != input_current.shape:
+            raise ValueError(
+                f"state.{name} and input_current must have the same shape; "
+                f"got {tuple(t.shape)} and {tuple(input_current.shape)}"
+            )
+    shape = input_current.shape
+    flat = (1, 1, input_current.numel())
+    new_state, spikes = izhikevich_forward(
+        input_current.reshape(flat),
+        IzhikevichState(state.voltage.reshape(flat[1:]), state.recovery.reshape(flat[1:])),
+        params,
+    )
+    return (IzhikevichState(new_state.voltage.reshape(shape), new_state.recovery.reshape(shape)),
+            spikes.reshape(shape))
 
 
 def two_layer_surrogate_lif_rate_packed_hidden_forward(

@@ -17,6 +17,7 @@ from torch import nn
 
 from myelin_b200.checkpointing import CheckpointSize
 from myelin_b200.kernels import (
+    izhikevich_step,
     Backend,
     alif_forward,
     linear_surrogate_lif_forward,
@@ -26,7 +27,14 @@ from myelin_b200.kernels import (
     surrogate_alif_forward,
     surrogate_lif_forward,
 )
-from myelin_b200.neurons import ALIFParams, ALIFState, LIFParams, LIFState
+from myelin_b200.neurons import (
+    ALIFParams,
+    ALIFState,
+    IzhikevichParams,
+    IzhikevichState,
+    LIFParams,
+    LIFState,
+)
 from myelin_b200.packing import PackedSpikes
 from myelin_b200.surrogates import (
     SurrogateFn,
@@ -93,6 +101,19 @@ class ALIFCell(nn.Module):
     ) -> tuple[ALIFState, torch.Tensor]:
         new_state, spikes = alif_forward(input_current.unsqueeze(0), state, self.params)
         return new_state, spikes[0]
+
+
+class IzhikevichCell(nn.Module):
+    """Single-step Izhikevich-style population (src/myelin/modules.py:175-208)."""
+
+    def __init__(self, params: IzhikevichParams | None = None) -> None:
+        super().__init__()
+        self.params = params or IzhikevichParams()
+
+    def forward(
+        self, state: IzhikevichState, input_current: torch.Tensor
+    ) -> tuple[IzhikevichState, torch.Tensor]:
+        return izhikevich_step(state, input_current, self.params)
 
 
 class SurrogateLIFCell(nn.Module):

@@ -66,3 +66,36 @@ class ALIFState:
 
     membrane: torch.Tensor
     adaptation: torch.Tensor
+
+
+@dataclass(frozen=True)
+class IzhikevichParams:
+    """Izhikevich-style neuron parameters (src/myelin/neurons.py:74-96).
+
+    Defaults are the regular-spiking configuration of the discrete model;
+    ``dt`` scales both the voltage and the recovery update.
+    """
+
+    recovery_decay: float = 0.02
+    recovery_coupling: float = 0.2
+    reset_voltage: float = -65.0
+    recovery_jump: float = 8.0
+    threshold: float = 30.0
+    dt: float = 1.0
+    voltage_square_coeff: float = 0.04
+    voltage_coeff: float = 5.0
+    voltage_bias: float = 140.0
+
+    def validate(self) -> None:
+        """Validate the scalar parameters (src/myelin/neurons.py:91-95)."""
+
+        if self.dt <= 0:
+            raise ValueError("dt must be positive")
+
+
+@dataclass(frozen=True)
+class IzhikevichState:
+    """Izhikevich state carried between steps (src/myelin/neurons.py:98-103)."""
+
+    voltage: torch.Tensor
+    recovery: torch.Tensor

@@ -180,3 +180,43 @@ def linear_backward(x, w, grad_currents):
     dw = x2.T @ g
     db = g.sum(axis=0)
     return dx.astype(np.float32), dw.astype(np.float32), db.astype(np.float32)
+
+
+IZHIKEVICH_FIELDS = ("recovery_decay", "recovery_coupling", "reset_voltage", "recovery_jump",
+                     "threshold", "dt", "voltage_square_coeff", "voltage_coeff", "voltage_bias")
+
+
+def izhikevich_forward(x, v0, u0, params: dict):
+    """Izhikevich forward, restated from src/myelin/neurons.py:131-156 /
+    functional.py:81-112 in float32 with one rounding per operation, in the
+    reference's evaluation order (Python scalars rounded to float32 first):
+
+        dv  = ((c2 * v) * v + c1 * v) + bias - u + I
+        p_v = v + dt * dv
+        p_u = u + dt * (a * (b * v - u))
+        s   = p_v >= threshold
+        v'  = s ? reset_voltage : p_v;   u' = s ? p_u + jump : p_u
+
+    Returns (spikes [T,B,N] 0/1 float32, vT, uT).
+    """
+
+    f = np.float32
+    x = _f32(x)
+    v = _f32(v0).copy()
+    u = _f32(u0).copy()
+    a, b, rv, jump, thr, dt, c2, c1, bias = (f(params[k]) for k in IZHIKEVICH_FIELDS)
+    spikes = np.empty_like(x)
+    with np.errstate(over="ignore", invalid="ignore"):
+        for t in range(x.shape[0]):
+            dv = (c2 * v) * v
+            dv = dv + c1 * v
+            dv = dv + bias
+            dv = dv - u
+            dv = dv + x[t]
+            pv = v + dt * dv
+            pu = u + dt * (a * (b * v - u))
+            s = pv >= thr
+            spikes[t] = s
+            v = np.where(s, rv, pv).astype(np.float32)
+            u = np.where(s, pu + jump, pu).astype(np.float32)
+    return spikes, v, u

@@ -23,6 +23,9 @@ the reference. Cases:
   (src/myelin/autograd.py:445-885);
 - packing.npz: ``pack_spikes`` / ``packed_spike_counts`` / ``packed_spike_count``
   (src/myelin/packing.py:45-216) on ragged widths;
+- izhikevich_*.npz: ``functional.izhikevich_unroll`` (functional.py:81-112)
+  spikes (packed words) and final voltage / recovery, default and custom
+  parameters;
 - c1_checksum.json: SHA-256 of the packed spikes and final membrane of
   ``lif_unroll`` at BASELINE config 1 (T=64, B=32, N=1024, x ~ N(0.3, 0.5),
   torch.Generator seed 0), for a full-size bit-exact check without storing it.
@@ -94,6 +97,35 @@ def lif_forward_cases() -> None:
             OUT / f"{name}.npz", x=x.numpy(), v0=v0.numpy(), a0=a0.numpy(),
             packed=_pack_np(spikes), vT=state.membrane.numpy(), aT=state.adaptation.numpy(),
             **{k: v for k, v in p.items()},
+        )
+
+
+def izhikevich_cases() -> None:
+    """``functional.izhikevich_unroll`` (src/myelin/functional.py:81-112) in float32."""
+
+    from myelin.functional import izhikevich_unroll
+    from myelin.neurons import IzhikevichParams, IzhikevichState
+
+    for name, (T, B, N), p, mean, std, seed in [
+        ("izhikevich_a", (60, 3, 67), {}, 10.0, 4.0, 5),
+        ("izhikevich_b", (50, 4, 64), dict(recovery_decay=0.1, recovery_coupling=0.25,
+                                           reset_voltage=-60.0, recovery_jump=2.0, threshold=25.0,
+                                           dt=0.5, voltage_square_coeff=0.05,
+                                           voltage_coeff=4.5, voltage_bias=130.0), 8.0, 6.0, 6),
+    ]:
+        g = _gen(seed)
+        x = torch.randn((T, B, N), generator=g) * std + mean
+        v0 = -65.0 + torch.rand((B, N), generator=g) * 10.0
+        u0 = 0.2 * v0 + torch.rand((B, N), generator=g)
+        params = IzhikevichParams(**p)
+        state, spikes = izhikevich_unroll(x, IzhikevichState(voltage=v0, recovery=u0), params)
+        fields = {k: getattr(params, k) for k in (
+            "recovery_decay", "recovery_coupling", "reset_voltage", "recovery_jump", "threshold",
+            "dt", "voltage_square_coeff", "voltage_coeff", "voltage_bias")}
+        np.savez_compressed(
+            OUT / f"{name}.npz", x=x.numpy(), v0=v0.numpy(), u0=u0.numpy(),
+            packed=_pack_np(spikes), vT=state.voltage.numpy(), uT=state.recovery.numpy(),
+            **fields,
         )
 
 
@@ -274,14 +306,15 @@ def c1_checksum() -> None:
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--reference-src", required=True, help="path to the reference's src/")
+    cases = {"lif": lif_forward_cases, "surrogate": surrogate_cases, "linear": linear_cases,
+             "packing": packing_cases, "c1": c1_checksum, "izhikevich": izhikevich_cases}
+    parser.add_argument("--cases", nargs="*", choices=sorted(cases), default=sorted(cases),
+                        help="which fixture groups to (re)write (default: all)")
     args = parser.parse_args()
     sys.path.insert(0, args.reference_src)
     torch.set_num_threads(1)
-    lif_forward_cases()
-    surrogate_cases()
-    linear_cases()
-    packing_cases()
-    c1_checksum()
+    for name in args.cases:
+        cases[name]()
     for f in sorted(OUT.glob("*.npz")) + sorted(OUT.glob("*.json")):
         print(f"{f.name:40s} {f.stat().st_size:8d} B")
 

@@ -20,7 +20,7 @@ from myelin_b200 import _native as nat
 from myelin_b200 import compile_ops as cops
 
 OP_NAMES = ("scan_forward", "scan_backward", "gemm_tn", "pack_spikes", "unpack_spikes",
-            "count_rows", "count_columns")
+            "count_rows", "count_columns", "pack_count_spikes", "izhikevich_forward")
 
 
 def _traced_ops(fn, *args):
@@ -139,3 +139,19 @@ def test_scan_forward_fake_placeholders():
     assert aT is None and spikes is None and packed is None and ckpt_a is None
     assert rates.shape == (2, 32) and ckpt_v.shape == (2, 2, 32)
     assert ckpt_v.dtype == torch.float32
+
+
+def test_izhikevich_and_fused_pack_trace_to_ops():
+    def f(x, v0, u0, s):
+        st, spikes = mb.izhikevich_forward(x, mb.IzhikevichState(v0, u0), mb.IzhikevichParams())
+        packed, counts = mb.pack_spikes_with_counts(s, dtype=torch.int32)
+        return st.voltage, st.recovery, spikes, packed.data, counts
+
+    x, v0, u0, s = _fake(((9, 2, 40), torch.float32), ((2, 40), torch.float32),
+                         ((2, 40), torch.float32), ((3, 4, 64), torch.bool))
+    gm, ops = _traced_ops(f, x, v0, u0, s)
+    assert ops == {"izhikevich_forward", "pack_count_spikes"}
+    with FakeTensorMode(allow_non_fake_inputs=True):
+        vT, uT, spikes, words, counts = gm(x, v0, u0, s)
+    assert vT.shape == (2, 40) and spikes.shape == (9, 2, 40)
+    assert words.shape == (3, 4, 2) and counts.shape == (64,) and counts.dtype == torch.int32

@@ -202,3 +202,13 @@ def test_oracle_chunk_size_does_not_change_gradients(oracle):
     a = oracle.scan_backward(x, v0, chunk=1, **kw)["grad_x"]
     b = oracle.scan_backward(x, v0, chunk=16, **kw)["grad_x"]
     assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("name", ["izhikevich_a", "izhikevich_b"])
+def test_izhikevich_oracle_matches_reference_golden(oracle, name):
+    g = load_golden(name)
+    params = {k: float(g[k]) for k in oracle.IZHIKEVICH_FIELDS}
+    spikes, vT, uT = oracle.izhikevich_forward(g["x"], g["v0"], g["u0"], params)
+    assert np.array_equal(oracle.pack(spikes), g["packed"])
+    assert np.array_equal(vT, g["vT"])
+    assert np.array_equal(uT, g["uT"])
