@@ -12,33 +12,16 @@
 //   v'  = s ? reset_voltage : p_v;   u' = s ? p_u + jump : p_u
 //
 // Forward only, like the reference's generated kernel
-// (src/myelin/triton/generated.py:1192-1227). HBM-streaming: 2 elements read
-// and written per neuron-step; each thread owns two neighbouring neurons and
-// keeps kIzhUnroll steps of loads in flight.
+// (src/myelin/triton/generated.py:1192-1227). Rows that are 16-byte aligned
+// run the warp-specialized scan forward (scan_fast.cu, TMA-streamed chunks);
+// the kernels here serve the other shapes: two neighbouring neurons per thread
+// with kIzhUnroll steps of loads in flight, or one neuron per thread.
 #include "common.cuh"
 #include "scan_common.cuh"
 
 namespace mb {
 
 namespace {
-
-struct IzhConsts {
-  float a, b, reset_v, jump, thr, dt, c2, c1, bias;
-};
-
-__device__ __forceinline__ bool izh_step(float& v, float& u, float x, const IzhConsts& c) {
-  float dv = __fmul_rn(__fmul_rn(c.c2, v), v);
-  dv = __fadd_rn(dv, __fmul_rn(c.c1, v));
-  dv = __fadd_rn(dv, c.bias);
-  dv = __fsub_rn(dv, u);
-  dv = __fadd_rn(dv, x);
-  const float pv = __fadd_rn(v, __fmul_rn(c.dt, dv));
-  const float pu = __fadd_rn(u, __fmul_rn(c.dt, __fmul_rn(c.a, __fsub_rn(__fmul_rn(c.b, v), u))));
-  const bool s = pv >= c.thr;
-  v = s ? c.reset_v : pv;
-  u = s ? __fadd_rn(pu, c.jump) : pu;
-  return s;
-}
 
 constexpr int kIzhUnroll = 8;
 
@@ -49,8 +32,9 @@ __global__ void __launch_bounds__(256) izh_fwd_pair_kernel(const T* __restrict__
                                                            const T* __restrict__ u0,
                                                            T* __restrict__ vT, T* __restrict__ uT,
                                                            T* __restrict__ spikes, int64_t steps,
-                                                           int64_t half, IzhConsts c) {
+                                                           int64_t half, IzhConsts cp) {
   using P = Pair<T>;
+  const IzhConsts c = cp;  // register copy (see izh_step's callers in scan_fast.cu)
   using V = typename P::V;
   const int64_t stride = int64_t(gridDim.x) * blockDim.x;
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < half; i += stride) {
@@ -87,8 +71,9 @@ __global__ void __launch_bounds__(256) izh_fwd_scalar_kernel(const T* __restrict
                                                              T* __restrict__ vT, T* __restrict__ uT,
                                                              T* __restrict__ spikes,
                                                              int64_t steps, int64_t BN,
-                                                             IzhConsts c) {
+                                                             IzhConsts cp) {
   using E = Elem<T>;
+  const IzhConsts c = cp;
   const int64_t stride = int64_t(gridDim.x) * blockDim.x;
   for (int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < BN; e += stride) {
     float v = E::to_f(v0[e]), u = E::to_f(u0[e]);
@@ -153,6 +138,18 @@ extern "C" int mb_izhikevich_forward(int dtype, const void* x, const void* v0, c
                     params->voltage_square_coeff, params->voltage_coeff, params->voltage_bias};
   cudaStream_t s = as_stream(stream);
   const int64_t BN = B * N;
+  if (T > 0) {
+    // 16-byte-aligned rows: the warp-specialized forward (TMA-streamed chunks)
+    ScanFwdArgs a{};
+    a.x = x; a.v0 = v0; a.a0 = u0; a.vT = vT; a.aT = uT; a.spikes = spikes;
+    a.T = T; a.B = B; a.N = N; a.BN = BN;
+    a.words_per_row = ceil_div(N, 32);
+    a.izh = c;
+    if (launch_scan_fwd_fast(dtype, kIzhikevich, MB_RESET_HARD, a, s)) {
+      MB_CHECK_LAUNCH("mb_izhikevich_forward");
+      return 0;
+    }
+  }
   switch (dtype) {
     case MB_F32: launch_izh<float>(x, v0, u0, vT, uT, spikes, T, BN, c, s); break;
     case MB_BF16: launch_izh<__nv_bfloat16>(x, v0, u0, vT, uT, spikes, T, BN, c, s); break;

@@ -9,6 +9,34 @@ namespace mb {
 constexpr int kChunk = MB_SCAN_CHUNK;
 constexpr int kBlock = 256;
 
+// Izhikevich constants (mb_izhikevich_params) and the internal neuron-kind id
+// the forward kernels use for it (the public mb_neuron enum covers the scans
+// with a backward; Izhikevich has its own entry point).
+constexpr int kIzhikevich = 2;
+
+struct IzhConsts {
+  float a, b, reset_v, jump, thr, dt, c2, c1, bias;
+};
+
+// One Izhikevich step (src/myelin/neurons.py:131-156) in the torch
+// expression's order, one fp32 rounding per operation, no FMA:
+//   dv = ((c2 * v) * v + c1 * v) + bias - u + x;  p_v = v + dt * dv
+//   p_u = u + dt * (a * (b * v - u));  s = p_v >= thr
+//   v = s ? reset_v : p_v;  u = s ? p_u + jump : p_u
+__device__ __forceinline__ bool izh_step(float& v, float& u, float x, const IzhConsts& c) {
+  float dv = __fmul_rn(__fmul_rn(c.c2, v), v);
+  dv = __fadd_rn(dv, __fmul_rn(c.c1, v));
+  dv = __fadd_rn(dv, c.bias);
+  dv = __fsub_rn(dv, u);
+  dv = __fadd_rn(dv, x);
+  const float pv = __fadd_rn(v, __fmul_rn(c.dt, dv));
+  const float pu = __fadd_rn(u, __fmul_rn(c.dt, __fmul_rn(c.a, __fsub_rn(__fmul_rn(c.b, v), u))));
+  const bool s = pv >= c.thr;
+  v = s ? c.reset_v : pv;
+  u = s ? __fadd_rn(pu, c.jump) : pu;
+  return s;
+}
+
 struct ScanFwdArgs {
   const void* x;
   const void* v0;
@@ -24,6 +52,7 @@ struct ScanFwdArgs {
   int64_t words_per_row;   // ceil(N / 32)
   int64_t groups_per_row;  // ceil(N / (32 * NPT))
   float decay, threshold, reset, adapt_decay, beta;
+  IzhConsts izh;  // kIzhikevich only
 };
 
 struct ScanBwdArgs {

@@ -56,12 +56,18 @@ enum FwdMode { kFwdDense = 0, kFwdPacked = 1, kFwdRates = 2, kFwdAny = 3 };
 // Backward inputs: spike gradients, rate gradients, or any combination.
 enum BwdMode { kBwdSpikes = 0, kBwdRates = 1, kBwdAny = 2 };
 
-// Resident CTAs per SM the backward is compiled for: ALIF keeps two state
-// adjoints and replays two state variables, and the exp-based surrogates
-// (sigmoid, multi-Gaussian) hold more temporaries; fewer CTAs give them
-// registers enough not to spill.
-constexpr int bwd_min_blocks(int kind, int surr) {
-  return kind == MB_LIF ? 4 : (surr == MB_SURR_SIGMOID || surr == MB_SURR_MULTI_GAUSSIAN ? 2 : 4);
+// Resident CTAs per SM the backward is compiled for (a register budget). LIF
+// fits 4 without spilling. ALIF (two state adjoints, two replayed states)
+// also runs at 4 for one gradient input: a small spill (24 bytes) costs less
+// than the occupancy lost at 3 (measured 0.155 vs 0.179 ms at config 3). With
+// both spike and rate gradients the spill grows past 100 bytes, so that mode
+// runs at 3; the exp-based surrogates (sigmoid, multi-Gaussian) hold more
+// temporaries and run at 2.
+constexpr int bwd_min_blocks(int kind, int surr, int mode) {
+  return kind == MB_LIF ? 4
+         : (surr == MB_SURR_SIGMOID || surr == MB_SURR_MULTI_GAUSSIAN) ? 2
+         : mode == kBwdAny ? 3
+                           : 4;
 }
 
 // Per-launch fp32 constants, each duplicated into both lanes of a float2 for
@@ -166,11 +172,12 @@ __global__ void __launch_bounds__(kThreads, 6) scan_fwd_fast_kernel(
   const int tid = threadIdx.x;  // 0 .. 32*kConsumerWarps-1
   const bool valid = 2 * tid < tile_n;  // tile_n is even
   const int64_t e = e0 + 2 * tid;
+  constexpr bool kTwoStates = KIND != MB_LIF;  // ALIF adaptation / Izhikevich recovery
   F2 m = f2(0.0f), ad = f2(0.0f);
   int c0 = 0, c1 = 0;
   if (valid) {
     m = f2(P::to_f2(reinterpret_cast<const V*>(a.v0)[e >> 1]));
-    if (KIND == MB_ALIF) ad = f2(P::to_f2(reinterpret_cast<const V*>(a.a0)[e >> 1]));
+    if (kTwoStates) ad = f2(P::to_f2(reinterpret_cast<const V*>(a.a0)[e >> 1]));
   }
   const F2 decay = c.decay, nthr = c.nthr, adapt_decay = c.adapt_decay, nbeta = c.nbeta;
   const float reset_v = a.reset;
@@ -191,9 +198,18 @@ __global__ void __launch_bounds__(kThreads, 6) scan_fwd_fast_kernel(
   const bool pk_lane = (lane & 15) == 0 && (q << 5) < a.BN;
   const int sh = lane & 16;  // lanes 0-15 -> word q, lanes 16-31 -> word q+1
 
+  // a register copy: referring to the parameter block itself would place it
+  // in local memory
+  const IzhConsts izc = a.izh;
   auto step = [&](V xv, V* slot) {
-    Step2<KIND, RESET> st;
-    st.run(m, ad, f2(P::to_f2(xv)), decay, nthr, reset_v, adapt_decay, nbeta);
+    Step2<KIND == kIzhikevich ? MB_LIF : KIND, RESET> st;
+    if constexpr (KIND == kIzhikevich) {
+      const float2 xf = P::to_f2(xv);
+      st.s0 = izh_step(m.x, ad.x, xf.x, izc);
+      st.s1 = izh_step(m.y, ad.y, xf.y, izc);
+    } else {
+      st.run(m, ad, f2(P::to_f2(xv)), decay, nthr, reset_v, adapt_decay, nbeta);
+    }
     if (kRates) {
       c0 += st.s0 ? 1 : 0;
       c1 += st.s1 ? 1 : 0;
@@ -216,7 +232,7 @@ __global__ void __launch_bounds__(kThreads, 6) scan_fwd_fast_kernel(
     }
     if (a.ckpt_v != nullptr && valid) {
       reinterpret_cast<float2*>(a.ckpt_v + k * a.BN)[e >> 1] = split(m);
-      if (KIND == MB_ALIF) reinterpret_cast<float2*>(a.ckpt_a + k * a.BN)[e >> 1] = split(ad);
+      if (kTwoStates) reinterpret_cast<float2*>(a.ckpt_a + k * a.BN)[e >> 1] = split(ad);
     }
     T* stage = ring + s * kChunk * kTileN;
     V* row = reinterpret_cast<V*>(stage) + tid;
@@ -245,7 +261,7 @@ __global__ void __launch_bounds__(kThreads, 6) scan_fwd_fast_kernel(
 
   if (!valid) return;
   if (a.vT) reinterpret_cast<V*>(a.vT)[e >> 1] = P::from_f2(split(m).x, split(m).y);
-  if (KIND == MB_ALIF && a.aT) reinterpret_cast<V*>(a.aT)[e >> 1] = P::from_f2(split(ad).x, split(ad).y);
+  if (kTwoStates && a.aT) reinterpret_cast<V*>(a.aT)[e >> 1] = P::from_f2(split(ad).x, split(ad).y);
   if (kRates && a.rates) {
     const float tf = static_cast<float>(a.T);
     reinterpret_cast<V*>(a.rates)[e >> 1] =
@@ -257,7 +273,7 @@ __global__ void __launch_bounds__(kThreads, 6) scan_fwd_fast_kernel(
 // Backward
 // ---------------------------------------------------------------------------
 template <typename T, int KIND, int RESET, int SURR, int MODE>
-__global__ void __launch_bounds__(kThreads, bwd_min_blocks(KIND, SURR)) scan_bwd_fast_kernel(
+__global__ void __launch_bounds__(kThreads, bwd_min_blocks(KIND, SURR, MODE)) scan_bwd_fast_kernel(
     const ScanBwdArgs a, const PairConsts c, const __grid_constant__ CUtensorMap out_map) {
   using P = Pair<T>;
   using V = typename P::V;
@@ -479,7 +495,9 @@ void fwd_fast(const ScanFwdArgs& a, const Map& om, cudaStream_t stream) {
 template <typename T>
 void fwd_fast_dispatch(int neuron, int reset_mode, const ScanFwdArgs& a, const Map& om,
                        cudaStream_t stream) {
-  if (neuron == MB_LIF) {
+  if (neuron == kIzhikevich) {
+    fwd_fast<T, kIzhikevich, MB_RESET_HARD>(a, om, stream);
+  } else if (neuron == MB_LIF) {
     if (reset_mode == MB_RESET_HARD) fwd_fast<T, MB_LIF, MB_RESET_HARD>(a, om, stream);
     else fwd_fast<T, MB_LIF, MB_RESET_SUBTRACT>(a, om, stream);
   } else {
