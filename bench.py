@@ -268,18 +268,32 @@ def run_gpu(args) -> None:
     pinned_g = gs.cpu().pin_memory()
     out_host = torch.empty(x.shape, dtype=x.dtype).pin_memory()
     e2e_steps = max(1, min(args.steps, 20))
-    for _ in range(2):
+    # The result read of step i runs on a second stream, ordered after the
+    # step's kernels by an event, so it overlaps the next step's host-to-device
+    # copies (PCIe is full duplex); everything else is the plain public API.
+    copy_stream = torch.cuda.Stream()
+
+    def e2e_step():
         xd = pinned_x.to("cuda", non_blocking=True).requires_grad_(True)
-        out_host.copy_(step(xd, pinned_g.to("cuda", non_blocking=True)), non_blocking=True)
+        gd = pinned_g.to("cuda", non_blocking=True)
+        gx = step(xd, gd)
+        done = torch.cuda.Event()
+        done.record(stream)
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(done)
+            out_host.copy_(gx, non_blocking=True)
+        gx.record_stream(copy_stream)
+
+    for _ in range(2):
+        e2e_step()
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     s2, t2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s2.record(stream)
     for _ in range(e2e_steps):
-        xd = pinned_x.to("cuda", non_blocking=True).requires_grad_(True)
-        gd = pinned_g.to("cuda", non_blocking=True)
-        out_host.copy_(step(xd, gd), non_blocking=True)
+        e2e_step()
+    stream.wait_stream(copy_stream)
     t2.record(stream)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(s2.elapsed_time(t2), world) / e2e_steps
