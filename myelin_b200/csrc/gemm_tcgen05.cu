@@ -16,7 +16,8 @@
 //   warps 2-5 epilogue: tcgen05.ld of the accumulator (each warp reads its own
 //             32-lane quarter of TMEM), bias add, conversion, global stores.
 // Two TMEM accumulators let the epilogue of one tile overlap the MMAs of the
-// next. Every mbarrier wait is bounded.
+// next. Every mbarrier wait is bounded. Large problems (M, N >= 256, enough
+// tiles for every SM pair) run the two-SM variant, gemm_tn_pair_kernel, below.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -198,12 +199,6 @@ __device__ __forceinline__ void load_bias32(const void* bias, int dtype, int64_t
   for (int j = 0; j < 32; ++j) bv[j] = j < valid ? cvt(p[j]) : 0.0f;
 }
 
-__device__ __forceinline__ float load_bias(const void* bias, int dtype, int64_t j) {
-  if (dtype == MB_F32) return __ldg(static_cast<const float*>(bias) + j);
-  if (dtype == MB_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(bias)[j]);
-  return __half2float(static_cast<const __half*>(bias)[j]);
-}
-
 template <typename TOut>
 __device__ __forceinline__ void store_row32(TOut* dst, const float (&v)[32], int valid,
                                             bool vec_ok) {
@@ -271,6 +266,60 @@ __device__ __forceinline__ void stage_row32(uint8_t* slot, int r, const float (&
       }
       const int pq = q ^ ((r >> 1) & 3);
       *reinterpret_cast<uint4*>(slot + r * 64 + pq * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
+// Epilogue of one tile for one warp: its 32 accumulator rows (TMEM lanes
+// taddr's quarter, columns b*BN ..) -> bias add in fp32 -> one rounding to TOut
+// -> global memory, either staged in swizzled shared memory and written with
+// bulk tensor stores (tma_store) or with direct row stores. TMEM loads are
+// double-buffered: chunk ci+1 loads while chunk ci is converted.
+template <typename TOut, int BN>
+__device__ __forceinline__ void drain_tile(uint32_t tbase, int64_t row0, int64_t col_tile0,
+                                           int lane, const GemmArgs& args,
+                                           const CUtensorMap* tma_c, uint8_t* slots,
+                                           uint32_t& nstore) {
+  constexpr int kSlotBytes = 32 * 32 * int(sizeof(TOut));
+  constexpr int kSlots = 2 * (32 * 32 * 4) / kSlotBytes;  // 2 (fp32) or 4 (16-bit)
+  const bool has_bias = args.bias != nullptr;
+  const bool vec_ok = args.vec_ok != 0;
+  const bool use_tma = args.tma_store != 0;
+  const int64_t row = row0 + lane;
+  TOut* crow = static_cast<TOut*>(args.C) + row * args.ldc;
+  uint32_t r[2][32];
+  tmem_ld32_issue(tbase, r[0]);
+#pragma unroll
+  for (int ci = 0; ci < BN / 32; ++ci) {
+    const int c = ci * 32;
+    tmem_wait_ld();  // chunk ci has landed
+    if (ci + 1 < BN / 32) tmem_ld32_issue(tbase + c + 32, r[(ci + 1) & 1]);  // overlap the next
+    const uint32_t(&rc)[32] = r[ci & 1];
+    const int64_t col0 = col_tile0 + c;
+    const int valid = static_cast<int>(imin64(32, args.N - col0));
+    if (valid <= 0 || row0 >= args.M) continue;  // warp-uniform
+    float v[32];
+    if (has_bias) {
+      float bv[32];
+      load_bias32(args.bias, args.bias_dtype, col0, valid, bv);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(rc[j]) + bv[j];
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(rc[j]);
+    }
+    if (use_tma) {
+      // the slot used kSlots stores ago must have been read out
+      if (lane == 0) tma_store_wait_read<kSlots - 1>();
+      __syncwarp();
+      uint8_t* slot = slots + (nstore % kSlots) * kSlotBytes;
+      stage_row32<TOut>(slot, lane, v);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) tma_store_2d(tma_c, slot, static_cast<int>(col0), static_cast<int>(row0));
+      ++nstore;
+    } else if (row < args.M) {
+      store_row32<TOut>(crow + col0, v, valid, vec_ok);
     }
   }
 }
@@ -382,12 +431,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     const int quarter = warp & 3;  // TMEM lanes this warp may access
-    const bool has_bias = args.bias != nullptr;
-    const bool vec_ok = args.vec_ok != 0;
     const bool use_tma = args.tma_store != 0;
     uint8_t* slots = sepi + (warp - 2) * 2 * L::kEpiSlotBytes;
-    constexpr int kSlotBytes = 32 * 32 * int(sizeof(TOut));
-    constexpr int kSlots = 2 * L::kEpiSlotBytes / kSlotBytes;  // 2 (fp32) or 4 (16-bit)
     uint32_t nstore = 0;
     uint32_t local = 0;
     for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
@@ -396,45 +441,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int64_t tm = tile / n_tiles;
       const int64_t tn = tile % n_tiles;
-      const int64_t row0 = tm * kBM + quarter * 32;
-      const int64_t row = row0 + lane;
-      TOut* crow = static_cast<TOut*>(args.C) + row * args.ldc;
-      const uint32_t tbase = tmem_base + (uint32_t(quarter * 32) << 16) + b * BN;
-      uint32_t r[2][32];
-      tmem_ld32_issue(tbase, r[0]);
-#pragma unroll
-      for (int ci = 0; ci < BN / 32; ++ci) {
-        const int c = ci * 32;
-        tmem_wait_ld();  // chunk ci has landed
-        if (ci + 1 < BN / 32) tmem_ld32_issue(tbase + c + 32, r[(ci + 1) & 1]);  // overlap the next
-        const uint32_t(&rc)[32] = r[ci & 1];
-        const int64_t col0 = tn * BN + c;
-        const int valid = static_cast<int>(imin64(32, args.N - col0));
-        if (valid <= 0 || row0 >= args.M) continue;  // warp-uniform
-        float v[32];
-        if (has_bias) {
-          float bv[32];
-          load_bias32(args.bias, args.bias_dtype, col0, valid, bv);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(rc[j]) + bv[j];
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(rc[j]);
-        }
-        if (use_tma) {
-          // the slot used kSlots stores ago must have been read out
-          if (lane == 0) tma_store_wait_read<kSlots - 1>();
-          __syncwarp();
-          uint8_t* slot = slots + (nstore % kSlots) * kSlotBytes;
-          stage_row32<TOut>(slot, lane, v);
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) tma_store_2d(&tma_c, slot, static_cast<int>(col0), static_cast<int>(row0));
-          ++nstore;
-        } else if (row < args.M) {
-          store_row32<TOut>(crow + col0, v, valid, vec_ok);
-        }
-      }
+      drain_tile<TOut, BN>(tmem_base + (uint32_t(quarter * 32) << 16) + b * BN,
+                           tm * kBM + quarter * 32, tn * BN, lane, args, &tma_c, slots,
+                           nstore);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
@@ -446,6 +455,255 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   if (warp == 1) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(L::kTmemCols));
+  }
+}
+
+
+// ---------------------------------------------------------------------------
+// Two-SM variant: a cluster of 2 CTAs (on 2 SMs) computes a 256 x 256 tile
+// with tcgen05.mma.cta_group::2 (M = 256, N = 256 per instruction). CTA r of
+// the pair loads rows [128 r, 128 r + 128) of the A tile and of the B tile
+// (32 KB per stage instead of 48 KB per 128 x 256 tile on one SM: half the
+// operand traffic per SM) and holds its 128 rows x 256 columns of the
+// accumulator in its own TMEM. The pair's leader (rank 0):
+//   - arms its "full" barrier with both CTAs' bytes; both CTAs' TMA loads
+//     (the .cta_group::2 form) complete on the leader's barrier;
+//   - issues the MMAs from one thread and commits stage release and tile
+//     completion to the barriers of both CTAs (one commit per CTA);
+//   - waits on its "acc_empty" barrier, which the epilogue warps of both
+//     CTAs arrive on through cluster addresses.
+// Each CTA drains its accumulator with 8 epilogue warps (two per TMEM lane
+// quarter, 128 columns each), so draining a tile keeps up with its MMAs even
+// at small K.
+// Every wait is bounded; no thread leaves early (failed waits fall through),
+// and a cluster barrier before TMEM release keeps both CTAs alive until
+// neither can touch the other's shared memory.
+// ---------------------------------------------------------------------------
+constexpr int k2Stages = 5;
+constexpr int k2EpiWarps = 8;  // two per TMEM lane quarter, 128 columns each
+constexpr int k2Threads = 64 + 32 * k2EpiWarps;
+constexpr int k2BM = 256;  // rows per pair tile (128 per CTA)
+constexpr int k2BN = 256;  // columns per pair tile (B rows: 128 per CTA)
+
+struct Layout2 {
+  static constexpr int kABytes = 128 * kBK * 2;  // this CTA's A rows
+  static constexpr int kBBytes = 128 * kBK * 2;  // this CTA's B rows
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kEpiSlotBytes = 32 * 32 * 4;
+  static constexpr int kEpiBytes = k2EpiWarps * 2 * kEpiSlotBytes;
+  static constexpr int kBarrierBytes = 256;
+  static constexpr size_t kSmem =
+      size_t(k2Stages) * kStageBytes + kEpiBytes + kBarrierBytes + 1024;
+  static constexpr uint32_t kTmemCols = 2 * k2BN;  // two accumulators
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address in the cluster's shared window of `local` (a shared::cta address)
+// as seen in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_addr(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
+// 2-D tiled load into this CTA's shared memory whose completion bytes are
+// counted on the barrier at cluster address `bar_cluster` (the leader's).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int c0, int c1,
+                                                 uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar_cluster)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// Arrive once on the barrier at cluster address `bar_cluster` when every
+// pair MMA issued so far by this thread has completed.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar_cluster) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar_cluster)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster)
+               : "memory");
+}
+
+template <typename TIn>
+__device__ __forceinline__ uint32_t mma_idesc_pair() {
+  constexpr uint32_t ab = std::is_same<TIn, __nv_bfloat16>::value ? 1u : 0u;
+  return (1u << 4) | (ab << 7) | (ab << 10) | (uint32_t(k2BN >> 3) << 17) |
+         (uint32_t(k2BM >> 4) << 24);
+}
+
+template <typename TIn, typename TOut>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
+    gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
+                        const __grid_constant__ CUtensorMap tma_b,
+                        const __grid_constant__ CUtensorMap tma_c, const GemmArgs args) {
+  using L = Layout2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + k2Stages * L::kABytes;
+  uint8_t* sepi = sb + k2Stages * L::kBBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sepi + L::kEpiBytes);
+  uint64_t* empty = full + k2Stages;
+  uint64_t* acc_full = empty + k2Stages;  // [2]
+  uint64_t* acc_empty = acc_full + 2;     // [2]
+  uint64_t* drained = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drained + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int64_t pair = blockIdx.x >> 1;
+  const int64_t pairs = gridDim.x >> 1;
+  const int64_t m_tiles = (args.M + k2BM - 1) / k2BM;
+  const int64_t n_tiles = (args.N + k2BN - 1) / k2BN;
+  const int64_t tiles = m_tiles * n_tiles;
+  const int kblocks = static_cast<int>((args.K + kBK - 1) / kBK);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < k2Stages; ++s) {
+      mbar_init(&full[s], 1);   // the leader's arm (its expect_tx); peer's unused
+      mbar_init(&empty[s], 1);  // one commit per use, from the leader's MMA thread
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);   // one commit per tile
+      mbar_init(&acc_empty[b], 2 * k2EpiWarps);  // epilogue warps of both CTAs (leader's used)
+    }
+    mbar_init(drained, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_addr(tmem_slot)),
+                 "r"(L::kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers initialised before any remote use
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int64_t tile = pair; tile < tiles && ok; tile += pairs) {
+        const int tm = static_cast<int>(tile / n_tiles);
+        const int tn = static_cast<int>(tile % n_tiles);
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = static_cast<int>(it % k2Stages);
+          const uint32_t use = it / k2Stages;
+          if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          const uint32_t bar = cluster_addr(smem_addr(&full[s]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * L::kStageBytes);
+          tma_load_2d_pair(sa + s * L::kABytes, &tma_a, kb * kBK, tm * k2BM + int(rank) * 128, bar);
+          tma_load_2d_pair(sb + s * L::kBBytes, &tma_b, kb * kBK, tn * k2BN + int(rank) * 128, bar);
+        }
+      }
+      if (leader) {
+        // both CTAs' copies complete on the leader's barriers: once the last
+        // phases have completed nothing is in flight into either CTA
+        const uint32_t issued = it;
+        for (uint32_t j = issued > k2Stages ? issued - k2Stages : 0; j < issued; ++j) {
+          mbar_wait_bounded(&full[j % k2Stages], (j / k2Stages) & 1);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      const uint32_t idesc = mma_idesc_pair<TIn>();
+      uint32_t it = 0, local = 0;
+      bool ok = true;
+      for (int64_t tile = pair; tile < tiles && ok; tile += pairs, ++local) {
+        const uint32_t b = local & 1;
+        const uint32_t use_b = local >> 1;
+        if (use_b > 0 && !mbar_wait_bounded(&acc_empty[b], (use_b - 1) & 1)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + b * k2BN;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = static_cast<int>(it % k2Stages);
+          if (!mbar_wait_bounded(&full[s], (it / k2Stages) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_addr(sa + s * L::kABytes);
+          const uint32_t b0 = smem_addr(sb + s * L::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / kUmmaK; ++k) {
+            mma_f16_pair(d_tmem, sw128_kmajor_desc(a0 + k * kUmmaK * 2),
+                         sw128_kmajor_desc(b0 + k * kUmmaK * 2), idesc, (kb | k) != 0);
+          }
+          // the stage is free in both CTAs once these MMAs finish
+          mma_commit_pair(cluster_addr(smem_addr(&empty[s]), 0));
+          mma_commit_pair(cluster_addr(smem_addr(&empty[s]), 1));
+        }
+        if (ok) {  // the tile's accumulator halves are complete in both CTAs
+          mma_commit_pair(cluster_addr(smem_addr(&acc_full[b]), 0));
+          mma_commit_pair(cluster_addr(smem_addr(&acc_full[b]), 1));
+        }
+      }
+      mma_commit_pair(cluster_addr(smem_addr(drained), 0));
+      mbar_wait_bounded(drained, 0);  // all MMAs done before TMEM is released
+    }
+  } else {
+    const int quarter = warp & 3;      // TMEM lanes this warp may access (warp id % 4)
+    const int half = (warp - 2) >> 2;  // which 128 of the 256 columns it drains
+    const bool use_tma = args.tma_store != 0;
+    uint8_t* slots = sepi + (warp - 2) * 2 * L::kEpiSlotBytes;
+    uint32_t nstore = 0;
+    uint32_t local = 0;
+    for (int64_t tile = pair; tile < tiles; tile += pairs, ++local) {
+      const uint32_t b = local & 1;
+      if (!mbar_wait_bounded(&acc_full[b], (local >> 1) & 1)) break;
+      tc_fence_after();
+      const int64_t tm = tile / n_tiles;
+      const int64_t tn = tile % n_tiles;
+      drain_tile<TOut, k2BN / 2>(
+          tmem_base + (uint32_t(quarter * 32) << 16) + b * k2BN + half * (k2BN / 2),
+          tm * k2BM + int64_t(rank) * 128 + quarter * 32, tn * k2BN + half * (k2BN / 2), lane,
+          args, &tma_c, slots, nstore);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(cluster_addr(smem_addr(&acc_empty[b]), 0));
+    }
+    if (use_tma && lane == 0) tma_store_wait_all();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // neither CTA touches the other's shared memory or TMEM after this
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
                  "r"(L::kTmemCols));
   }
 }
@@ -511,10 +769,51 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb_, const CUtensorMap& mc,
 }
 
 template <typename TIn, typename TOut>
+int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb_, const CUtensorMap& mc,
+                const GemmArgs& args, cudaStream_t s) {
+  auto kern = gemm_tn_pair_kernel<TIn, TOut>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       static_cast<int>(Layout2::kSmem));
+  const int64_t tiles = ((args.M + k2BM - 1) / k2BM) * ((args.N + k2BN - 1) / k2BN);
+  const int pairs = static_cast<int>(imin64(tiles, sm_count() / 2));
+  kern<<<2 * pairs, k2Threads, Layout2::kSmem, s>>>(ma, mb_, mc, args);
+  return 0;
+}
+
+// Kernel choice, from measurements on B200 (bf16, CUDA events):
+//  - the pair kernel halves operand traffic per SM and wins once the main
+//    loop dominates: K >= 2048 with 16-bit output (51200 x 4096 x 4096 with
+//    bias 1420 vs 1368 TFLOP/s; K = 2048 on par or better);
+//  - at smaller K, or with fp32 output, the accumulator drain is the larger
+//    part of a tile and the one-SM kernel, which waits only for its own
+//    epilogue, is faster (K = 1024: 1062 vs 937);
+//  - small problems (under two waves of one-SM tiles) go to the pair kernel
+//    (6400 x 1024 x 784: 440 vs 306).
+bool use_pair(const GemmArgs& args, bool out_f32) {
+  const int sms = sm_count();
+  const int64_t pair_tiles = ((args.M + k2BM - 1) / k2BM) * ((args.N + k2BN - 1) / k2BN);
+  const int64_t single_tiles = ((args.M + kBM - 1) / kBM) * ((args.N + 255) / 256);
+  if (args.M < k2BM || args.N < k2BN || pair_tiles < sms / 2) return false;
+  return (args.K >= 2048 && !out_f32) || single_tiles < 2 * sms;
+}
+
+template <typename TIn, typename TOut>
 int launch_bn(const void* A, int64_t lda, const void* B, int64_t ldb, GemmArgs args,
               int out_dtype, cudaStream_t s) {
   const bool bf16 = std::is_same<TIn, __nv_bfloat16>::value;
   CUtensorMap ma, mbm;
+  if (use_pair(args, out_dtype == MB_F32)) {
+    // both operand maps: 64 K-elements x 128 rows (each CTA's half of the pair tile)
+    if (!make_map(&ma, A, args.M, args.K, lda, 128, bf16) ||
+        !make_map(&mbm, B, args.N, args.K, ldb, 128, bf16)) {
+      set_error("mb_gemm_tn: cuTensorMapEncodeTiled failed (shape or alignment)");
+      return 1;
+    }
+    CUtensorMap mc;
+    memset(&mc, 0, sizeof(mc));
+    args.tma_store = make_c_map(&mc, args.C, args.M, args.N, args.ldc, out_dtype) ? 1 : 0;
+    return launch_pair<TIn, TOut>(ma, mbm, mc, args, s);
+  }
   const int bn = args.N >= 192 ? 256 : (args.N > 64 ? 128 : 64);
   if (!make_map(&ma, A, args.M, args.K, lda, kBM, bf16) ||
       !make_map(&mbm, B, args.N, args.K, ldb, bn, bf16)) {

@@ -1,6 +1,7 @@
 """The tcgen05 projection GEMM against a plain PyTorch fp32 reference.
 
-C = A @ B^T (+ bias) with bf16/f16 operands and fp32 accumulation. The fp32
+C = A @ B^T (+ bias) with bf16/f16 operands and fp32 accumulation, on the
+one-SM kernel (small problems) and the two-SM pair kernel. The fp32
 reference multiplies the same (upcast) operands; fp32 outputs agree to
 rtol 1e-4 scaled by max|C| (summation order), 16-bit outputs to one rounding
 of the output type.
@@ -30,7 +31,11 @@ def _case(M, N, K, dtype, seed, bias_dtype):
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 8, 8), (128, 256, 64), (129, 257, 72), (300, 10, 784),
-                                   (1000, 1000, 1024), (6400, 1024, 784), (2048, 4096, 2048)])
+                                   (1000, 1000, 1024), (6400, 1024, 784), (2048, 4096, 2048),
+                                   # two-SM pair tiles (>= 74 tiles of 256 x 256) with ragged
+                                   # M, N and K tails; the last pair tile's second half lies
+                                   # wholly past M in (562, 8192, 64)
+                                   (4999, 3001, 520), (562, 8192, 64)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("out_f32", [True, False])
 def test_gemm_matches_fp32_reference(M, N, K, dtype, out_f32):
