@@ -435,8 +435,28 @@ def run_network(args, world, rank, local) -> None:
         opt.step()
         return loss
 
-    for _ in range(args.warmup):
-        step()
+    # On one GPU the whole training step (forward, backward, SGD update) is
+    # captured once in a CUDA graph and replayed: the same kernels on the same
+    # buffers every step, without the per-launch host latency of a step made of
+    # many short kernels. With several ranks the step stays eager (its NCCL
+    # all-reduce is issued from the host each step).
+    graph = None
+    if world == 1:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(args.warmup):
+                step()
+        torch.cuda.current_stream().wait_stream(side)
+        opt.zero_grad(set_to_none=True)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            static_loss = step()
+        for _ in range(args.warmup):
+            graph.replay()
+    else:
+        for _ in range(args.warmup):
+            step()
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -445,7 +465,11 @@ def run_network(args, world, rank, local) -> None:
         torch.cuda.synchronize()
         start.record(stream)
         for _ in range(args.steps):
-            loss = step()
+            if graph is not None:
+                graph.replay()
+                loss = static_loss
+            else:
+                loss = step()
         stop.record(stream)
         torch.cuda.synchronize()
         barrier(world)
@@ -464,7 +488,8 @@ def run_network(args, world, rank, local) -> None:
         "config": {"workload": name + (" (BASELINE config 2)" if name == "mlp_fp32" else
                                        " (BASELINE config 5)"),
                    "T": T, "B_per_gpu": B, "global_batch": B * world, "F": F,
-                   "parallelism": f"dp{world} (gradient all-reduce, NCCL)" if world > 1 else "dp1"},
+                   "parallelism": f"dp{world} (gradient all-reduce, NCCL)" if world > 1 else "dp1",
+                   "cuda_graph": graph is not None},
         "tflops_per_gpu": round(flops / (ms / 1e3) / 1e12, 1),
         "loss": float(loss.item()),
         "device_status": nat.device_status(clear=True),
