@@ -45,7 +45,8 @@ FALLBACK_HBM_GBS = 6650.0
 # ---------------------------------------------------------------------------
 T_STEPS, BATCH, NEURONS = 256, 128, 4096
 
-# algorithmic bytes per neuron-step (from the API's I/O; DESIGN.md derives them)
+# algorithmic bytes per neuron-step, from the API's inputs and outputs plus the fp32
+# chunk checkpoints (4 B per state every 16 steps)
 #   forward : read x, write dense spikes, write fp32 checkpoints (s states / 16 steps)
 #   backward: read x, read grad_spikes, write grad_x, read checkpoints
 ALGO_BYTES = {

@@ -30,6 +30,7 @@ from myelin_b200.kernels import (
     linear_surrogate_lif_forward,
     linear_surrogate_lif_packed_forward,
     two_layer_surrogate_lif_rate_packed_hidden_forward,
+    two_layer_surrogate_lif_rate_recompute_forward,
     linear_surrogate_lif_rate_forward,
     surrogate_alif_forward,
     surrogate_lif_forward,

@@ -183,7 +183,10 @@ class LinearScanFunction(torch.autograd.Function):
 
 class TwoLayerPackedHiddenRateFunction(torch.autograd.Function):
     """Two stream-synapse LIF layers: hidden spikes, then output spike rates,
-    with the hidden spikes kept bit-packed between forward and backward.
+    with the hidden spikes kept bit-packed between forward and backward
+    (``save_hidden``) or not kept at all and regenerated in the backward by
+    re-running the layer-1 scan from its checkpoints (whole-model recompute,
+    src/myelin/autograd.py:926-1126).
 
     Forward: currents1 = X W1 + b1 -> scan writing packed hidden words (and
     checkpoints) -> hidden = unpack(words), transient -> currents2 = hidden W2
@@ -196,7 +199,8 @@ class TwoLayerPackedHiddenRateFunction(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx: Any, inputs, hidden_weight, hidden_bias, output_weight, output_bias,
-                decay: float, threshold: float, reset: float, surrogate: int, slope: float):
+                decay: float, threshold: float, reset: float, surrogate: int, slope: float,
+                save_hidden: bool = True):
         T, B, F = inputs.shape
         H = hidden_weight.shape[1]
         O = output_weight.shape[1]
@@ -218,13 +222,13 @@ class TwoLayerPackedHiddenRateFunction(torch.autograd.Function):
         )
         ctx.set_materialize_grads(False)
         ctx.save_for_backward(inputs, hidden_weight, hidden_bias, output_weight, output_bias,
-                              ckpt1, ckpt2, words)
+                              ckpt1, ckpt2, words if save_hidden else None)
         ctx.cfg = (decay, threshold, reset, surrogate, slope)
         return rates
 
     @staticmethod
     def backward(ctx: Any, g_rates):
-        tail = (None,) * 5
+        tail = (None,) * 6
         if g_rates is None:
             return (None,) * 5 + tail
         inputs, w1, b1, w2, b2, ckpt1, ckpt2, words = ctx.saved_tensors
@@ -236,6 +240,13 @@ class TwoLayerPackedHiddenRateFunction(torch.autograd.Function):
                        adapt_decay=0.0, beta=0.0, reset_mode=nat.MB_RESET_HARD,
                        surrogate=surrogate, slope=slope, need_v0=False, need_a0=False)
 
+        x2 = inputs.reshape(T * B, F)
+        cur1 = None
+        if words is None:  # whole-model recompute: regenerate the hidden spikes
+            cur1 = _project(x2, w1, b1).view(T, B, H)
+            v0 = torch.zeros((B, H), dtype=inputs.dtype, device=inputs.device)
+            words = cops.scan_forward(cur1, v0, None, nat.MB_LIF, decay, threshold, reset, 0.0,
+                                      0.0, nat.MB_RESET_HARD, packed=True)[3]
         hidden = cops.unpack(words, T * B, H, inputs.dtype)  # [T*B, H]
         cur2 = _project(hidden, w2, b2).view(T, B, O)
         g_cur2, _, _ = cops.scan_backward(cur2, ckpt2, None, grad_rates=g_rates, **scan_kw)
@@ -248,8 +259,8 @@ class TwoLayerPackedHiddenRateFunction(torch.autograd.Function):
         grad_x = grad_w1 = grad_b1 = None
         if need_x or need_w1 or need_b1:
             g_hidden = _input_grad(g2, w2).view(T, B, H)
-            x2 = inputs.reshape(T * B, F)
-            cur1 = _project(x2, w1, b1).view(T, B, H)
+            if cur1 is None:
+                cur1 = _project(x2, w1, b1).view(T, B, H)
             g_cur1, _, _ = cops.scan_backward(cur1, ckpt1, None, grad_spikes=g_hidden, **scan_kw)
             del cur1, g_hidden
             g1 = g_cur1.view(T * B, H)

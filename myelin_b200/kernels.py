@@ -456,6 +456,57 @@ def izhikevich_step(
             spikes.reshape(shape))
 
 
+def _two_layer_validate(inputs, hidden_weight, hidden_bias, output_weight, output_bias):
+    _validate_linear(inputs, hidden_weight, hidden_bias)
+    if output_weight.ndim != 2 or output_weight.shape[0] != hidden_weight.shape[1]:
+        raise ValueError("output_weight must be shaped [hidden_features, output_features]")
+    if output_bias is not None and tuple(output_bias.shape) != (output_weight.shape[1],):
+        raise ValueError("output_bias must be shaped [output_features]")
+    if output_weight.dtype != inputs.dtype or output_weight.device != inputs.device:
+        raise ValueError("output_weight must match the inputs' dtype and device")
+
+
+def two_layer_surrogate_lif_rate_recompute_forward(
+    inputs: torch.Tensor,
+    hidden_weight: torch.Tensor,
+    hidden_bias: torch.Tensor | None,
+    output_weight: torch.Tensor,
+    output_bias: torch.Tensor | None,
+    params: LIFParams,
+    *,
+    surrogate: SurrogateName = "fast_sigmoid",
+    surrogate_slope: float = 5.0,
+    hard_forward: bool = True,
+    checkpoint_size: CheckpointSize = 25,
+) -> torch.Tensor:
+    """Two-layer LIF rate model with whole-model backward recompute.
+
+    Same rates and gradients as the packed-hidden variant; between forward and
+    backward only the inputs, parameters and the layers' fp32 chunk
+    checkpoints are kept, and the backward regenerates the hidden spikes
+    (src/myelin/kernels.py:779-808, src/myelin/autograd.py:926-1126).
+    """
+
+    sid = surrogate_id(surrogate)
+    resolve_checkpoint_size(int(inputs.shape[0]), checkpoint_size)  # validates like the reference
+    if not hard_forward:
+        raise ValueError("two-layer recompute rate training supports only hard_forward=True")
+    _two_layer_validate(inputs, hidden_weight, hidden_bias, output_weight, output_bias)
+    return TwoLayerPackedHiddenRateFunction.apply(
+        inputs.contiguous(),
+        hidden_weight.contiguous(),
+        None if hidden_bias is None else hidden_bias.contiguous(),
+        output_weight.contiguous(),
+        None if output_bias is None else output_bias.contiguous(),
+        params.decay,
+        float(params.threshold),
+        float(params.reset),
+        sid,
+        float(surrogate_slope),
+        False,
+    )
+
+
 def two_layer_surrogate_lif_rate_packed_hidden_forward(
     inputs: torch.Tensor,
     hidden_weight: torch.Tensor,
@@ -484,13 +535,7 @@ def two_layer_surrogate_lif_rate_packed_hidden_forward(
     resolve_checkpoint_size(int(inputs.shape[0]), checkpoint_size)
     if not hard_forward:
         raise ValueError("packed-hidden two-layer rate training supports only hard_forward=True")
-    _validate_linear(inputs, hidden_weight, hidden_bias)
-    if output_weight.ndim != 2 or output_weight.shape[0] != hidden_weight.shape[1]:
-        raise ValueError("output_weight must be shaped [hidden_features, output_features]")
-    if output_bias is not None and tuple(output_bias.shape) != (output_weight.shape[1],):
-        raise ValueError("output_bias must be shaped [output_features]")
-    if output_weight.dtype != inputs.dtype or output_weight.device != inputs.device:
-        raise ValueError("output_weight must match the inputs' dtype and device")
+    _two_layer_validate(inputs, hidden_weight, hidden_bias, output_weight, output_bias)
     return TwoLayerPackedHiddenRateFunction.apply(
         inputs.contiguous(),
         hidden_weight.contiguous(),
@@ -502,6 +547,7 @@ def two_layer_surrogate_lif_rate_packed_hidden_forward(
         float(params.reset),
         sid,
         float(surrogate_slope),
+        True,
     )
 
 

@@ -1,4 +1,4 @@
-"""Izhikevich forward (SURVEY next row F4) on the GPU through the C ABI.
+"""Izhikevich forward on the GPU through the C ABI.
 
 Bit-exact against the reference's own golden vectors (functional.izhikevich_unroll,
 src/myelin/functional.py:81-112) and against the float32 oracle on seeded

@@ -1,4 +1,5 @@
-"""Two-layer rate model with bit-packed hidden spikes (SURVEY next row F1).
+"""Two-layer rate models: bit-packed hidden spikes and
+whole-model backward recompute.
 
 The reference checks its packed-hidden function against the composition of
 the dense layers (tests/test_triton_lif.py:2427-2505, same shapes and
@@ -57,16 +58,21 @@ def test_packed_hidden_matches_dense_composition(dtype, shape, with_bias):
         return mb.two_layer_surrogate_lif_rate_packed_hidden_forward(
             x, w1, b1 if with_bias else None, w2, b2 if with_bias else None, params, **kw)
 
+    def recompute(x, w1, b1, w2, b2):
+        return mb.two_layer_surrogate_lif_rate_recompute_forward(
+            x, w1, b1 if with_bias else None, w2, b2 if with_bias else None, params, **kw)
+
     leaves = _leaves(dtype, T, B, F, H, O, seed=151 + T)
     r_ref, g_ref = _run(composed, leaves, target)
-    leaves2 = [t.detach().clone().requires_grad_(True) for t in leaves]
-    r_act, g_act = _run(packed, leaves2, target)
-    assert torch.equal(r_act, r_ref)
     names = ("inputs", "hidden_weight", "hidden_bias", "output_weight", "output_bias")
-    for name, a, b in zip(names, g_act, g_ref):
-        if not with_bias and name.endswith("bias"):
-            continue
-        assert torch.equal(a, b), name
+    for fn in (packed, recompute):
+        leaves2 = [t.detach().clone().requires_grad_(True) for t in leaves]
+        r_act, g_act = _run(fn, leaves2, target)
+        assert torch.equal(r_act, r_ref), fn.__name__
+        for name, a, b in zip(names, g_act, g_ref):
+            if not with_bias and name.endswith("bias"):
+                continue
+            assert torch.equal(a, b), (fn.__name__, name)
 
 
 def test_packed_hidden_saves_bits_not_dense_hidden():
@@ -96,3 +102,14 @@ def test_packed_hidden_rejects_soft_forward_and_bad_shapes():
                                                               hard_forward=False)
     with pytest.raises(ValueError, match="output_weight"):
         mb.two_layer_surrogate_lif_rate_packed_hidden_forward(x, w1, b1, w2[:5], b2, params)
+
+
+def test_recompute_saves_no_hidden_spikes():
+    T, B, F, H, O = 32, 8, 64, 256, 10
+    params = mb.LIFParams(tau_mem=10.0, threshold=0.5)
+    leaves = _leaves(torch.float32, T, B, F, H, O, seed=9)
+    saved = []
+    with torch.autograd.graph.saved_tensors_hooks(lambda t: saved.append(tuple(t.shape)) or t,
+                                                  lambda t: t):
+        mb.two_layer_surrogate_lif_rate_recompute_forward(*leaves, params)
+    assert (T, B, H // 32) not in saved and (T, B, H) not in saved
