@@ -582,10 +582,17 @@ def run_pack_count(args, world, rank, local) -> None:
     spikes = torch.rand((T, B, N), generator=gen, device="cuda") < 0.05
     stream = torch.cuda.current_stream()
     gather_buf = torch.empty((world, T, B, N // 32), dtype=torch.int32, device="cuda")
+    fused = world > 1 and args.allgather == "fused"
+    exchange = mb.PackedSpikeExchange((T, B, N)) if fused else None
     if world > 1:
         import torch.distributed as dist
 
     def step():
+        if fused:
+            # one kernel packs, counts and stores the words into every rank's
+            # gather buffer over NVLink; the count all-reduce completes the step
+            _, counts = exchange.pack_count_all_gather(spikes, count_dtype=torch.int32)
+            return counts
         packed, counts = mb.pack_spikes_with_counts(spikes, dtype=torch.int32)
         if world > 1:
             mb.packed_spike_all_gather_into_tensor(packed, out=gather_buf)
@@ -620,7 +627,9 @@ def run_pack_count(args, world, rank, local) -> None:
         "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "u8", "data": "synthetic Bernoulli(0.05)",
         "config": {"workload": "pack_count (BASELINE config 4)", "T": T, "B_total": B * world,
-                   "B_per_gpu": B, "N": N, "parallelism": f"dp{world} (batch-sharded)"},
+                   "B_per_gpu": B, "N": N, "parallelism": f"dp{world} (batch-sharded)",
+                   "allgather": ("fused pack + peer stores over NVLink" if fused else
+                                 "NCCL all_gather_into_tensor" if world > 1 else None)},
         "allgather_busbw_gbs": (round(words_bytes * world * (world - 1) / world / (ms / 1e3) / 1e9, 1)
                                 if world > 1 else None),
         "roofline": {"bound": "hbm", "achieved": round(algo / (ms / 1e3) / 1e9, 1), "peak": peak,
@@ -633,6 +642,8 @@ def run_pack_count(args, world, rank, local) -> None:
     clk = clocks.summary()
     if clk is not None:
         result["clocks"] = clk
+    if exchange is not None:
+        exchange.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -733,6 +744,9 @@ def main() -> None:
                         default="alif_bf16")
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--allgather", choices=("fused", "nccl"), default="fused",
+                        help="pack_count at N > 1: fused pack + peer-store all-gather, or "
+                             "pack then NCCL all_gather_into_tensor")
     parser.add_argument("--batch", type=int, default=None,
                         help="per-GPU batch of the network workloads (default: the BASELINE "
                              "config's); smaller values are for profiling captures")

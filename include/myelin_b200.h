@@ -238,6 +238,40 @@ int mb_pack_count_spikes(int dtype, const void* spikes, int32_t* words, int64_t 
                          int64_t* counts64, int32_t* counts32, void* workspace,
                          int64_t workspace_bytes, void* stream);
 
+/*
+ * Pack + per-neuron count (as mb_pack_count_spikes) whose packed words are
+ * stored to `num_sinks` (1..8) destinations instead of one: `sinks` is a host
+ * array of device pointers, each the start of this rank's [rows,
+ * ceil(n/32)] slot in one rank's gather buffer — this GPU's own and peers'
+ * (mapped with mb_ipc_open; peer stores go over NVLink). The kernel reads the
+ * spikes once and writes every destination as it goes, so the all-gather's
+ * transfers overlap the packing. It does not wait for peers: the caller
+ * orders later reads of the gather buffers after every rank's call (the
+ * count all-reduce that follows does that). Fused for aligned 1-byte spikes
+ * with n % 32 == 0; other inputs pack into sinks[0] and copy to the rest.
+ * Replaces: packing.pack_spikes + distributed.packed_spike_all_gather
+ *   (src/myelin/distributed.py:63-80) + the local count of
+ *   packed_spike_count_all_reduce (distributed.py:83-98).
+ */
+int mb_pack_count_scatter(int dtype, const void* spikes, int64_t rows, int64_t n,
+                          void* const* sinks, int num_sinks, int64_t* counts64,
+                          int32_t* counts32, void* workspace, int64_t workspace_bytes,
+                          void* stream);
+
+/*
+ * Gather buffers shared between the processes of a job through CUDA IPC (no
+ * reference counterpart: the reference's all-gather is NCCL's). mb_ipc_alloc
+ * allocates `bytes` on the current device and writes its IPC handle
+ * (mb_ipc_handle_bytes() bytes) to `handle`; another process maps it with
+ * mb_ipc_open and unmaps it with mb_ipc_close; the owner frees it with
+ * mb_ipc_free.
+ */
+int mb_ipc_handle_bytes(void);
+int mb_ipc_alloc(int64_t bytes, void** ptr, void* handle);
+int mb_ipc_open(const void* handle, void** ptr);
+int mb_ipc_close(void* ptr);
+int mb_ipc_free(void* ptr);
+
 /* Largest scratch (bytes) mb_count_columns_noalloc can use: 4 MiB. */
 #define MB_COUNT_COLUMNS_NOALLOC_MAX_BYTES (4 << 20)
 

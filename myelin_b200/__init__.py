@@ -16,6 +16,7 @@ from myelin_b200.distributed import (
     distributed_available_and_initialized,
     packed_spike_all_gather,
     packed_spike_all_gather_into_tensor,
+    PackedSpikeExchange,
     packed_spike_count_all_reduce,
     packed_spike_rate_all_reduce,
 )

@@ -76,6 +76,14 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mb_izhikevich_forward": (
         _int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp]
     ),
+    "mb_pack_count_scatter": (
+        _int, [_int, _vp, _i64, _i64, _vp, _int, _vp, _vp, _vp, _i64, _vp]
+    ),
+    "mb_ipc_handle_bytes": (_int, []),
+    "mb_ipc_alloc": (_int, [_i64, _vp, _vp]),
+    "mb_ipc_open": (_int, [_vp, _vp]),
+    "mb_ipc_close": (_int, [_vp]),
+    "mb_ipc_free": (_int, [_vp]),
 }
 
 EXPORTED_SYMBOLS = tuple(_SIGNATURES)
@@ -326,3 +334,49 @@ def izhikevich_forward(
             T, B, N, ctypes.addressof(params), stream_handle(x.device),
         )
     check(status, "mb_izhikevich_forward")
+
+
+def pack_count_scatter(
+    spikes: torch.Tensor,
+    rows: int,
+    n: int,
+    sinks: list[int],
+    counts64: torch.Tensor | None,
+    counts32: torch.Tensor | None,
+) -> None:
+    """Pack + count ``spikes[rows, n]``, storing the words to every address in
+    ``sinks`` (this rank's slot in each rank's gather buffer)."""
+
+    need = int(lib().mb_pack_count_workspace_bytes(rows, n))
+    workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=spikes.device)
+    arr = (ctypes.c_void_p * len(sinks))(*sinks)
+    with torch.cuda.device(spikes.device):
+        status = lib().mb_pack_count_scatter(
+            dtype_code(spikes.dtype), ptr(spikes), rows, n, arr, len(sinks), ptr(counts64),
+            ptr(counts32), ptr(workspace), need, stream_handle(spikes.device),
+        )
+    check(status, "mb_pack_count_scatter")
+
+
+def ipc_alloc(nbytes: int) -> tuple[int, bytes]:
+    """cudaMalloc + IPC handle on the current device: (device pointer, handle bytes)."""
+
+    size = int(lib().mb_ipc_handle_bytes())
+    handle = ctypes.create_string_buffer(size)
+    out = ctypes.c_void_p()
+    check(lib().mb_ipc_alloc(nbytes, ctypes.byref(out), handle), "mb_ipc_alloc")
+    return int(out.value), handle.raw
+
+
+def ipc_open(handle: bytes) -> int:
+    out = ctypes.c_void_p()
+    check(lib().mb_ipc_open(handle, ctypes.byref(out)), "mb_ipc_open")
+    return int(out.value)
+
+
+def ipc_close(address: int) -> None:
+    check(lib().mb_ipc_close(address), "mb_ipc_close")
+
+
+def ipc_free(address: int) -> None:
+    check(lib().mb_ipc_free(address), "mb_ipc_free")

@@ -137,3 +137,132 @@ def packed_spike_rate_all_reduce(
     counts = packed_spike_count_all_reduce(packed, dim=dim, group=group)
     world_size = dist.get_world_size(group=group)
     return counts.to(dtype) / (_count_denominator(packed, dim) * world_size)
+
+
+class _DeviceArray:
+    """A raw device allocation seen by torch through ``__cuda_array_interface__``."""
+
+    def __init__(self, address: int, shape: tuple[int, ...]) -> None:
+        self.__cuda_array_interface__ = {
+            "shape": tuple(shape), "typestr": "<i4", "data": (address, False),
+            "strides": None, "version": 3,
+        }
+
+
+class PackedSpikeExchange:
+    """One step of packed-spike exchange fused over NVLink peer memory.
+
+    ``pack_count_all_gather(spikes)`` packs this rank's spikes, counts spikes
+    per neuron, and writes the packed words straight into this rank's slot of
+    every rank's gather buffer (peer stores over NVLink / NVSwitch, inside the
+    packing kernel: the transfers overlap the packing), then all-reduces the
+    counts. Returns the gathered words ``[world, *leading, ceil(N/32)]`` (the
+    result of ``packed_spike_all_gather_into_tensor`` of every rank's
+    ``pack_spikes``) and the summed per-neuron counts (the result of
+    ``packed_spike_count_all_reduce(packed, dim=leading dims)``), the step of
+    src/myelin/distributed.py:63-98 in one kernel plus one small all-reduce.
+
+    The count all-reduce is also the completion barrier: a rank's all-reduce
+    finishes only after every rank has entered it, i.e. after every rank's
+    packing kernel (and all its peer stores) has finished. Gather buffers are
+    allocated once per object (CUDA IPC, plain peer memory, no multicast) and
+    used alternately, so reads of a returned buffer that the caller enqueues
+    on the current stream before its next call are ordered before any rank
+    overwrites it (a rank writes that buffer again only after the next call's
+    all-reduce, which waits for this rank's stream). Collective: every rank constructs the
+    object with the same local spike shape and calls each method in the same
+    order. ``close()`` releases the buffers (collective as well).
+    """
+
+    def __init__(self, local_shape: tuple[int, ...], *, device: torch.device | int | None = None,
+                 group: Any = None, buffers: int = 2, native: Any = None) -> None:
+        _require_distributed_initialized()
+        from myelin_b200 import _native
+
+        self._nat = native if native is not None else _native
+        if len(local_shape) < 1 or local_shape[-1] <= 0:
+            raise ValueError("local_shape must have a non-empty last dimension")
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("PackedSpikeExchange supports up to 8 ranks (one NVLink domain)")
+        self.local_shape = tuple(int(d) for d in local_shape)
+        self.n = self.local_shape[-1]
+        self.rows = 1
+        for d in self.local_shape[:-1]:
+            self.rows *= d
+        self.words = (self.n + 31) // 32
+        self.slot_bytes = self.rows * self.words * 4
+        if device is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        self.device = torch.device(device) if not isinstance(device, int) else \
+            torch.device("cuda", device)
+        # the native layer may supply its own device context and raw-memory view
+        # (tests run the host logic on CPU ranks with a stand-in)
+        self._ctx = getattr(self._nat, "device_context", torch.cuda.device)
+        view = getattr(self._nat, "device_view", None)
+        self._view = view if view is not None else (
+            lambda address, shape, dev: torch.as_tensor(_DeviceArray(address, shape), device=dev))
+        self._own: list[int] = []
+        self._opened: list[int] = []
+        self._sinks: list[list[int]] = []
+        self._views: list[torch.Tensor] = []
+        handles = []
+        with self._ctx(self.device):
+            for _ in range(buffers):
+                address, handle = self._nat.ipc_alloc(self.world * self.slot_bytes)
+                self._own.append(address)
+                handles.append(handle)
+        gathered: list[Any] = [None] * self.world
+        dist.all_gather_object(gathered, (self.rank, self.local_shape, handles), group=group)
+        for r, (rr, shape, _) in enumerate(gathered):
+            if rr != r or tuple(shape) != self.local_shape:
+                raise ValueError("every rank must build PackedSpikeExchange with the same shape")
+        with self._ctx(self.device):
+            for i in range(buffers):
+                sinks = []
+                for r in range(self.world):
+                    if r == self.rank:
+                        base = self._own[i]
+                    else:
+                        base = self._nat.ipc_open(gathered[r][2][i])
+                        self._opened.append(base)
+                    sinks.append(base + self.rank * self.slot_bytes)
+                self._sinks.append(sinks)
+                shape = (self.world, *self.local_shape[:-1], self.words)
+                self._views.append(self._view(self._own[i], shape, self.device))
+        self._step = 0
+
+    def pack_count_all_gather(
+        self, spikes: torch.Tensor, *, count_dtype: torch.dtype = torch.int64
+    ) -> tuple[torch.Tensor, torch.Tensor]:
+        if tuple(spikes.shape) != self.local_shape:
+            raise ValueError(f"spikes must be shaped {self.local_shape}; got {tuple(spikes.shape)}")
+        if spikes.device != self.device:
+            raise ValueError(f"spikes must be on {self.device}")
+        if count_dtype not in (torch.int64, torch.int32):
+            raise ValueError("count_dtype must be torch.int64 or torch.int32")
+        i = self._step % len(self._sinks)
+        self._step += 1
+        wide = self.rows * self.world > _INT32_MAX  # int32 on the wire when the sum fits
+        counts = torch.empty((self.n,), dtype=torch.int64 if wide else torch.int32,
+                             device=self.device)
+        self._nat.pack_count_scatter(spikes.contiguous(), self.rows, self.n, self._sinks[i],
+                                     counts if wide else None, None if wide else counts)
+        dist.all_reduce(counts, op=dist.ReduceOp.SUM, group=self.group)
+        return self._views[i], counts.to(count_dtype)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers, wait for every rank, free this rank's."""
+
+        if not self._own:
+            return
+        for address in self._opened:
+            self._nat.ipc_close(address)
+        self._opened = []
+        self._views = []
+        dist.barrier(group=self.group)
+        for address in self._own:
+            self._nat.ipc_free(address)
+        self._own = []

@@ -182,3 +182,103 @@ def test_collectives_on_two_gloo_ranks(tmp_path: Path):
     if len(results) != world:
         failures.append(f"expected {world} results, got {len(results)}")
     assert not failures, failures
+
+
+class _FakeIpc:
+    """Stand-in for the CUDA IPC / scatter-kernel layer of PackedSpikeExchange
+    on CPU ranks: addresses encode (owner rank, buffer); 'opening' a peer's
+    handle yields a distinct importer address; the scatter records its sinks
+    and counts spikes with numpy."""
+
+    IMPORT = 1 << 50
+
+    def __init__(self, rank: int) -> None:
+        self.rank = rank
+        self.calls: list[tuple] = []
+        self.n_alloc = 0
+
+    def device_context(self, device):
+        import contextlib
+
+        return contextlib.nullcontext()
+
+    def device_view(self, address, shape, device):
+        return torch.zeros(shape, dtype=torch.int32)
+
+    def ipc_alloc(self, nbytes):
+        address = ((self.rank + 1) << 40) | (self.n_alloc << 32)
+        self.n_alloc += 1
+        self.calls.append(("alloc", address, nbytes))
+        return address, repr((address, nbytes)).encode()
+
+    def ipc_open(self, handle):
+        address, _ = eval(handle.decode())  # noqa: S307 - test-local repr round trip
+        self.calls.append(("open", address))
+        return address | self.IMPORT
+
+    def pack_count_scatter(self, spikes, rows, n, sinks, c64, c32):
+        self.calls.append(("scatter", tuple(sinks)))
+        out = c64 if c64 is not None else c32
+        out.copy_((spikes.reshape(rows, n) != 0).sum(0).to(out.dtype))
+
+    def ipc_close(self, address):
+        self.calls.append(("close", address))
+
+    def ipc_free(self, address):
+        self.calls.append(("free", address))
+
+
+def _exchange_worker(rank: int, world: int, init: str, queue) -> None:
+    torch_dist.init_process_group("gloo", init_method=init, rank=rank, world_size=world)
+    try:
+        shape = (4, 3, 70)
+        fake = _FakeIpc(rank)
+        ex = mbd.PackedSpikeExchange(shape, device=torch.device("cpu"), native=fake)
+        slot = 4 * 3 * 3 * 4  # rows x words x 4 bytes
+        ok = ex.slot_bytes == slot
+        own = [c[1] for c in fake.calls if c[0] == "alloc"]
+        ok = ok and all(c[2] == world * slot for c in fake.calls if c[0] == "alloc")
+
+        def expected_sinks(i):
+            bases = [own[i] if d == rank else ((((d + 1) << 40) | (i << 32)) | _FakeIpc.IMPORT)
+                     for d in range(world)]
+            return tuple(b + rank * slot for b in bases)
+
+        totals = []
+        for step in range(3):
+            spikes = torch.rand(shape, generator=torch.Generator().manual_seed(10 * step + rank)) < 0.3
+            view, counts = ex.pack_count_all_gather(spikes)
+            ok = ok and view.shape == (world, 4, 3, 3) and counts.dtype == torch.int64
+            totals.append(counts)
+            scatter = [c for c in fake.calls if c[0] == "scatter"][-1]
+            ok = ok and scatter[1] == expected_sinks(step % 2)  # two buffers, used alternately
+        expect = [sum((torch.rand(shape, generator=torch.Generator().manual_seed(10 * s + r)) < 0.3)
+                      .sum((0, 1)).to(torch.int64) for r in range(world)) for s in range(3)]
+        ok = ok and all(torch.equal(a, b) for a, b in zip(totals, expect))
+        ex.close()
+        kinds = [c[0] for c in fake.calls]
+        # peers' mappings are closed before this rank's buffers are freed
+        ok = ok and kinds.count("close") == 2 * (world - 1) and kinds.count("free") == 2
+        ok = ok and max(i for i, k in enumerate(kinds) if k == "close") < kinds.index("free")
+        queue.put((rank, bool(ok), ""))
+    except Exception as exc:  # pragma: no cover - reported through the queue
+        queue.put((rank, False, f"{type(exc).__name__}: {exc}"))
+    finally:
+        torch_dist.destroy_process_group()
+
+
+def test_packed_spike_exchange_host_logic_on_two_gloo_ranks(tmp_path: Path):
+    world = 2
+    ctx = multiprocessing.get_context("spawn")
+    queue = ctx.Queue()
+    init = f"file://{tmp_path / 'rendezvous_exchange'}"
+    procs = [ctx.Process(target=_exchange_worker, args=(r, world, init, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    results = [queue.get(timeout=1) for _ in range(world)]
+    assert all(ok for _, ok, _ in results), results

@@ -78,3 +78,72 @@ def test_packed_collectives_over_nccl(tmp_path: Path):
     if len(results) != world:
         failures.append(f"expected {world} results, got {len(results)}")
     assert not failures, failures
+
+
+def _exchange_spikes(rank: int, step: int, shape) -> torch.Tensor:
+    gen = torch.Generator().manual_seed(1000 * step + 7 * rank + shape[-1])
+    return torch.rand(shape, generator=gen) < 0.1
+
+
+def _exchange_worker(rank: int, world: int, init: str, queue) -> None:
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=init, rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    try:
+        import myelin_b200 as mb
+
+        ok, msg = True, ""
+        # (16, 8, 256): fused kernel with peer stores; (6, 5, 70): pack then copy
+        for shape in ((16, 8, 256), (6, 5, 70)):
+            ex = mb.PackedSpikeExchange(shape)
+            for step in range(3):  # both buffers, then the first again
+                view, counts = ex.pack_count_all_gather(_exchange_spikes(rank, step, shape).cuda())
+                torch.cuda.synchronize()
+                for r in range(world):
+                    ref = mb.pack_spikes(_exchange_spikes(r, step, shape).cuda()).data
+                    if not torch.equal(view[r], ref):
+                        ok, msg = False, f"words of rank {r}, shape {shape}, step {step}"
+                expected = sum(_exchange_spikes(r, step, shape).sum(dim=(0, 1)).to(torch.int64)
+                               for r in range(world)).cuda()
+                if counts.dtype != torch.int64 or not torch.equal(counts, expected):
+                    ok, msg = False, f"counts, shape {shape}, step {step}"
+            ex.close()
+        torch.cuda.synchronize()
+        queue.put((rank, bool(ok), msg))
+    except Exception as exc:
+        queue.put((rank, False, f"{type(exc).__name__}: {exc}"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_packed_spike_exchange_over_nvlink(tmp_path: Path):
+    """Fused pack + peer-store all-gather + count all-reduce on 2 GPUs equals
+    every rank's pack_spikes and the summed counts, bit for bit."""
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    world = 2
+    ctx = multiprocessing.get_context("spawn")
+    queue = ctx.Queue()
+    init = f"file://{tmp_path / 'rdzv_exchange'}"
+    procs = [ctx.Process(target=_exchange_worker, args=(r, world, init, queue))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    failures = []
+    for p in procs:
+        p.join(timeout=180)
+        if p.is_alive():
+            p.terminate()
+            failures.append(f"rank {p.pid} timed out")
+    results = []
+    while not queue.empty():
+        results.append(queue.get(timeout=1))
+    failures += [m for _, ok, m in results if not ok]
+    if len(results) != world:
+        failures.append(f"expected {world} results, got {len(results)}")
+    assert not failures, failures
