@@ -240,21 +240,22 @@ int mb_pack_count_spikes(int dtype, const void* spikes, int32_t* words, int64_t 
 
 /*
  * Pack + per-neuron count (as mb_pack_count_spikes) whose packed words are
- * stored to `num_sinks` (1..8) destinations instead of one: `sinks` is a host
- * array of device pointers, each the start of this rank's [rows,
- * ceil(n/32)] slot in one rank's gather buffer — this GPU's own and peers'
- * (mapped with mb_ipc_open; peer stores go over NVLink). The kernel reads the
- * spikes once and writes every destination as it goes, so the all-gather's
- * transfers overlap the packing. It does not wait for peers: the caller
- * orders later reads of the gather buffers after every rank's call (the
- * count all-reduce that follows does that). Fused for aligned 1-byte spikes
- * with n % 32 == 0; other inputs pack into sinks[0] and copy to the rest.
+ * stored to `words` (this rank's [rows, ceil(n/32)] slot of its own gather
+ * buffer) and to `num_peers` (0..7) more places: `peers` is a host array of
+ * device pointers, each the start of this rank's slot in another rank's
+ * gather buffer (mapped with mb_ipc_open; the stores go over NVLink). The
+ * kernel reads the spikes once and writes every destination as it goes, so
+ * the all-gather's transfers overlap the packing. It does not wait for
+ * peers: the caller orders later reads of the gather buffers after every
+ * rank's call (the count all-reduce that follows does that). Fused for
+ * aligned 1-byte spikes with n % 32 == 0; other inputs pack into `words` and
+ * copy it to each peer slot.
  * Replaces: packing.pack_spikes + distributed.packed_spike_all_gather
  *   (src/myelin/distributed.py:63-80) + the local count of
  *   packed_spike_count_all_reduce (distributed.py:83-98).
  */
-int mb_pack_count_scatter(int dtype, const void* spikes, int64_t rows, int64_t n,
-                          void* const* sinks, int num_sinks, int64_t* counts64,
+int mb_pack_count_scatter(int dtype, const void* spikes, int32_t* words, int64_t rows,
+                          int64_t n, void* const* peers, int num_peers, int64_t* counts64,
                           int32_t* counts32, void* workspace, int64_t workspace_bytes,
                           void* stream);
 

@@ -77,7 +77,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp]
     ),
     "mb_pack_count_scatter": (
-        _int, [_int, _vp, _i64, _i64, _vp, _int, _vp, _vp, _vp, _i64, _vp]
+        _int, [_int, _vp, _vp, _i64, _i64, _vp, _int, _vp, _vp, _vp, _i64, _vp]
     ),
     "mb_ipc_handle_bytes": (_int, []),
     "mb_ipc_alloc": (_int, [_i64, _vp, _vp]),
@@ -338,22 +338,24 @@ def izhikevich_forward(
 
 def pack_count_scatter(
     spikes: torch.Tensor,
+    words: int,
     rows: int,
     n: int,
-    sinks: list[int],
+    peers: list[int],
     counts64: torch.Tensor | None,
     counts32: torch.Tensor | None,
 ) -> None:
-    """Pack + count ``spikes[rows, n]``, storing the words to every address in
-    ``sinks`` (this rank's slot in each rank's gather buffer)."""
+    """Pack + count ``spikes[rows, n]``, storing the words at device address
+    ``words`` (this rank's slot of its own gather buffer) and at every address
+    in ``peers`` (this rank's slot in the other ranks' gather buffers)."""
 
     need = int(lib().mb_pack_count_workspace_bytes(rows, n))
     workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=spikes.device)
-    arr = (ctypes.c_void_p * len(sinks))(*sinks)
+    arr = (ctypes.c_void_p * max(len(peers), 1))(*peers)
     with torch.cuda.device(spikes.device):
         status = lib().mb_pack_count_scatter(
-            dtype_code(spikes.dtype), ptr(spikes), rows, n, arr, len(sinks), ptr(counts64),
-            ptr(counts32), ptr(workspace), need, stream_handle(spikes.device),
+            dtype_code(spikes.dtype), ptr(spikes), words, rows, n, arr, len(peers),
+            ptr(counts64), ptr(counts32), ptr(workspace), need, stream_handle(spikes.device),
         )
     check(status, "mb_pack_count_scatter")
 

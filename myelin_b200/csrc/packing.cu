@@ -284,21 +284,21 @@ __device__ __forceinline__ uint32_t nonzero_bytes(uint32_t w) {
   return ((((w & 0x7f7f7f7fu) + 0x7f7f7f7fu) | w) & 0x80808080u) >> 7;
 }
 
-// Destinations of the packed words: `n` word arrays [rows, W] (this rank's
-// slot of the gather buffer on every rank, local and peers over NVLink).
-constexpr int kMaxWordSinks = 8;
-struct WordSinks {
-  uint32_t* p[kMaxWordSinks];
-  int n;
+// Further destinations of the packed words: this rank's [rows, W] slot in
+// the other ranks' gather buffers (peer memory over NVLink).
+constexpr int kMaxPeerSlots = 7;
+struct PeerSlots {
+  uint32_t* p[kMaxPeerSlots];
 };
 
 // COUNT = false packs only (the plain pack of 1-byte spikes: no counters, no
-// partials). SCATTER stores each word to every sink instead of `words`
-// (plain stores; sinks on other GPUs are peer memory).
-template <bool COUNT, bool SCATTER>
+// partials). NPEER > 0 also stores each word to the first NPEER peer slots
+// (plain stores; a compile-time count, so a word costs exactly 1 + NPEER
+// stores and no predicates).
+template <bool COUNT, int NPEER>
 __global__ void __launch_bounds__(kPackCountThreads) pack_count_u8_kernel(
     const uint4* __restrict__ in, uint32_t* __restrict__ words, int32_t* __restrict__ partial,
-    int64_t rows, int64_t W, int64_t rows_per_slice, const WordSinks sinks) {
+    int64_t rows, int64_t W, int64_t rows_per_slice, const PeerSlots peers) {
   __shared__ int32_t cnt[32][kPackCountThreads];  // [neuron in word][thread]: conflict-free
   const int tid = threadIdx.x;
   const int64_t wc = int64_t(blockIdx.x) * kPackCountThreads + tid;  // word column
@@ -335,14 +335,9 @@ __global__ void __launch_bounds__(kPackCountThreads) pack_count_u8_kernel(
       word |= ((b * 0x01020408u) >> 24) << (4 * q);
       if (COUNT) acc[q] += b;
     }
-    if constexpr (SCATTER) {
+    words[r * W + wc] = word;
 #pragma unroll
-      for (int d = 0; d < kMaxWordSinks; ++d) {
-        if (d < sinks.n) sinks.p[d][r * W + wc] = word;
-      }
-    } else {
-      words[r * W + wc] = word;
-    }
+    for (int d = 0; d < NPEER; ++d) peers.p[d][r * W + wc] = word;
   };
 
   const uint4* src = in + wc * 2;  // 2 x 16 bytes per row
@@ -364,7 +359,7 @@ __global__ void __launch_bounds__(kPackCountThreads) pack_count_u8_kernel(
     consume(src[r * row_vec], src[r * row_vec + 1], r);
     if (++pending == 255) flush();
   }
-  if (SCATTER) __threadfence_system();  // peer stores ordered before the kernel's end
+  if (NPEER > 0) __threadfence_system();  // peer stores ordered before the kernel's end
   if (!COUNT) return;
   flush();
   int4* dst = reinterpret_cast<int4*>(partial + int64_t(blockIdx.y) * W * 32 + wc * 32);
@@ -397,9 +392,9 @@ static void launch_pack(const void* spikes, int32_t* words, int64_t rows, int64_
     const int64_t slices = pack_count_slices(rows, n);
     dim3 grid(static_cast<unsigned>(ceil_div(W, kPackCountThreads)),
               static_cast<unsigned>(slices));
-    pack_count_u8_kernel<false, false><<<grid, kPackCountThreads, 0, s>>>(
+    pack_count_u8_kernel<false, 0><<<grid, kPackCountThreads, 0, s>>>(
         static_cast<const uint4*>(spikes), reinterpret_cast<uint32_t*>(words), nullptr, rows, W,
-        ceil_div(rows, slices), WordSinks{});
+        ceil_div(rows, slices), PeerSlots{});
   } else if (n % 32 == 0 && aligned_to(spikes, 16)) {
     const int64_t n_vec = rows * n * int64_t(sizeof(U)) / 16;
     pack_vec_kernel<DT><<<grid_for(n_vec), 256, 0, s>>>(static_cast<const uint4*>(spikes), words,
@@ -490,21 +485,46 @@ int64_t pack_count_workspace_bytes(int64_t rows, int64_t n) {
 
 // Pack + per-neuron count: one fused pass for aligned 1-byte spikes with
 // n % 32 == 0, else the pack kernel followed by the column count of the words.
+// The fused pack + count of aligned 1-byte spikes (n % 32 == 0): packing
+// kernel (words to `words` and to `npeer` peer slots) + slice-sum kernel.
+static void launch_pack_count_u8(const void* spikes, int32_t* words, const PeerSlots& peers,
+                                 int npeer, int64_t rows, int64_t n, int64_t* counts64,
+                                 int32_t* counts32, void* workspace, cudaStream_t s) {
+  const int64_t W = n / 32;
+  const int64_t slices = pack_count_slices(rows, n);
+  const dim3 grid(static_cast<unsigned>(ceil_div(W, kPackCountThreads)),
+                  static_cast<unsigned>(slices));
+  const auto* in = static_cast<const uint4*>(spikes);
+  auto* out = reinterpret_cast<uint32_t*>(words);
+  auto* partial = static_cast<int32_t*>(workspace);
+  const int64_t per_slice = ceil_div(rows, slices);
+  switch (npeer) {
+#define MB_PACK_PEERS(K)                                                                   \
+  case K:                                                                                  \
+    pack_count_u8_kernel<true, K>                                                          \
+        <<<grid, kPackCountThreads, 0, s>>>(in, out, partial, rows, W, per_slice, peers); \
+    break;
+    MB_PACK_PEERS(0)
+    MB_PACK_PEERS(1)
+    MB_PACK_PEERS(2)
+    MB_PACK_PEERS(3)
+    MB_PACK_PEERS(4)
+    MB_PACK_PEERS(5)
+    MB_PACK_PEERS(6)
+    MB_PACK_PEERS(7)
+#undef MB_PACK_PEERS
+    default: break;
+  }
+  count_columns_final_kernel<<<static_cast<unsigned>(ceil_div(n, 32)), 256, 0, s>>>(
+      partial, slices, n, counts64, counts32);
+}
+
 template <int DT>
 static void launch_pack_count(const void* spikes, int32_t* words, int64_t rows, int64_t n,
                               int64_t* counts64, int32_t* counts32, void* workspace,
                               cudaStream_t s) {
   if (pack_count_fused_ok(DT, spikes, n, workspace)) {
-    const int64_t W = n / 32;
-    const int64_t slices = pack_count_slices(rows, n);
-    dim3 grid(static_cast<unsigned>(ceil_div(W, kPackCountThreads)),
-              static_cast<unsigned>(slices));
-    pack_count_u8_kernel<true, false><<<grid, kPackCountThreads, 0, s>>>(static_cast<const uint4*>(spikes),
-                                              reinterpret_cast<uint32_t*>(words),
-                                              static_cast<int32_t*>(workspace), rows, W,
-                                              ceil_div(rows, slices), WordSinks{});
-    count_columns_final_kernel<<<static_cast<unsigned>(ceil_div(n, 32)), 256, 0, s>>>(static_cast<int32_t*>(workspace),
-                                                           slices, n, counts64, counts32);
+    launch_pack_count_u8(spikes, words, PeerSlots{}, 0, rows, n, counts64, counts32, workspace, s);
     return;
   }
   launch_pack<DT>(spikes, words, rows, n, s);
@@ -615,19 +635,21 @@ extern "C" int mb_pack_count_spikes(int dtype, const void* spikes, int32_t* word
   return 0;
 }
 
-extern "C" int mb_pack_count_scatter(int dtype, const void* spikes, int64_t rows, int64_t n,
-                                     void* const* sinks, int num_sinks, int64_t* counts64,
-                                     int32_t* counts32, void* workspace,
+extern "C" int mb_pack_count_scatter(int dtype, const void* spikes, int32_t* words,
+                                     int64_t rows, int64_t n, void* const* peers, int num_peers,
+                                     int64_t* counts64, int32_t* counts32, void* workspace,
                                      int64_t workspace_bytes, void* stream) {
   clear_error();
   MB_CHECK_ARG(valid_io_dtype(dtype), "mb_pack_count_scatter: unknown dtype %d", dtype);
   MB_CHECK_ARG(rows >= 0 && n > 0, "mb_pack_count_scatter: cannot pack an empty last dimension");
   MB_CHECK_ARG(counts64 != nullptr || counts32 != nullptr, "mb_pack_count_scatter: no output");
-  MB_CHECK_ARG(sinks != nullptr && num_sinks >= 1 && num_sinks <= kMaxWordSinks,
-               "mb_pack_count_scatter: 1 to %d word destinations required", kMaxWordSinks);
-  for (int d = 0; d < num_sinks; ++d) {
-    MB_CHECK_ARG(sinks[d] != nullptr && aligned_to(sinks[d], 4),
-                 "mb_pack_count_scatter: destination %d null or misaligned", d);
+  MB_CHECK_ARG(words != nullptr && aligned_to(words, 4),
+               "mb_pack_count_scatter: words null or misaligned");
+  MB_CHECK_ARG(num_peers >= 0 && num_peers <= kMaxPeerSlots && (num_peers == 0 || peers),
+               "mb_pack_count_scatter: 0 to %d peer slots required", kMaxPeerSlots);
+  for (int d = 0; d < num_peers; ++d) {
+    MB_CHECK_ARG(peers[d] != nullptr && aligned_to(peers[d], 4),
+                 "mb_pack_count_scatter: peer slot %d null or misaligned", d);
   }
   cudaStream_t s = as_stream(stream);
   if (rows == 0) {
@@ -642,28 +664,19 @@ extern "C" int mb_pack_count_scatter(int dtype, const void* spikes, int64_t rows
                "mb_pack_count_scatter: workspace of %lld bytes required, got %lld",
                (long long)need, (long long)workspace_bytes);
   MB_CHECK_ARG(aligned_to(workspace, 4), "mb_pack_count_scatter: workspace misaligned");
-  int32_t* first = static_cast<int32_t*>(sinks[0]);
   if (pack_count_fused_ok(dtype, spikes, n, workspace)) {
-    WordSinks ws{};
-    ws.n = num_sinks;
-    for (int d = 0; d < num_sinks; ++d) ws.p[d] = static_cast<uint32_t*>(sinks[d]);
-    const int64_t W = n / 32;
-    const int64_t slices = pack_count_slices(rows, n);
-    dim3 grid(static_cast<unsigned>(ceil_div(W, kPackCountThreads)),
-              static_cast<unsigned>(slices));
-    pack_count_u8_kernel<true, true><<<grid, kPackCountThreads, 0, s>>>(
-        static_cast<const uint4*>(spikes), nullptr, static_cast<int32_t*>(workspace), rows, W,
-        ceil_div(rows, slices), ws);
-    count_columns_final_kernel<<<static_cast<unsigned>(ceil_div(n, 32)), 256, 0, s>>>(
-        static_cast<int32_t*>(workspace), slices, n, counts64, counts32);
+    PeerSlots slots{};
+    for (int d = 0; d < num_peers; ++d) slots.p[d] = static_cast<uint32_t*>(peers[d]);
+    launch_pack_count_u8(spikes, words, slots, num_peers, rows, n, counts64, counts32, workspace,
+                         s);
   } else {
-    // other shapes: pack + count into the first destination, then one copy
-    // per further destination (peer copies over NVLink)
-    MB_DISPATCH_DTYPE(dtype, launch_pack_count, spikes, first, rows, n, counts64, counts32,
+    // other shapes: pack + count into `words`, then one copy per peer slot
+    // (over NVLink)
+    MB_DISPATCH_DTYPE(dtype, launch_pack_count, spikes, words, rows, n, counts64, counts32,
                       workspace, s);
     const size_t bytes = size_t(rows) * size_t(ceil_div(n, 32)) * sizeof(int32_t);
-    for (int d = 1; d < num_sinks; ++d) {
-      cudaMemcpyAsync(sinks[d], first, bytes, cudaMemcpyDefault, s);
+    for (int d = 0; d < num_peers; ++d) {
+      cudaMemcpyAsync(peers[d], words, bytes, cudaMemcpyDefault, s);
     }
   }
   MB_CHECK_LAUNCH("mb_pack_count_scatter");

@@ -206,7 +206,7 @@ class PackedSpikeExchange:
             lambda address, shape, dev: torch.as_tensor(_DeviceArray(address, shape), device=dev))
         self._own: list[int] = []
         self._opened: list[int] = []
-        self._sinks: list[list[int]] = []
+        self._slots: list[tuple[int, list[int]]] = []  # (own slot, peer slots) per buffer
         self._views: list[torch.Tensor] = []
         handles = []
         with self._ctx(self.device):
@@ -221,15 +221,13 @@ class PackedSpikeExchange:
                 raise ValueError("every rank must build PackedSpikeExchange with the same shape")
         with self._ctx(self.device):
             for i in range(buffers):
-                sinks = []
+                peers = []
                 for r in range(self.world):
-                    if r == self.rank:
-                        base = self._own[i]
-                    else:
+                    if r != self.rank:
                         base = self._nat.ipc_open(gathered[r][2][i])
                         self._opened.append(base)
-                    sinks.append(base + self.rank * self.slot_bytes)
-                self._sinks.append(sinks)
+                        peers.append(base + self.rank * self.slot_bytes)
+                self._slots.append((self._own[i] + self.rank * self.slot_bytes, peers))
                 shape = (self.world, *self.local_shape[:-1], self.words)
                 self._views.append(self._view(self._own[i], shape, self.device))
         self._step = 0
@@ -243,12 +241,13 @@ class PackedSpikeExchange:
             raise ValueError(f"spikes must be on {self.device}")
         if count_dtype not in (torch.int64, torch.int32):
             raise ValueError("count_dtype must be torch.int64 or torch.int32")
-        i = self._step % len(self._sinks)
+        i = self._step % len(self._slots)
         self._step += 1
         wide = self.rows * self.world > _INT32_MAX  # int32 on the wire when the sum fits
         counts = torch.empty((self.n,), dtype=torch.int64 if wide else torch.int32,
                              device=self.device)
-        self._nat.pack_count_scatter(spikes.contiguous(), self.rows, self.n, self._sinks[i],
+        own, peers = self._slots[i]
+        self._nat.pack_count_scatter(spikes.contiguous(), own, self.rows, self.n, peers,
                                      counts if wide else None, None if wide else counts)
         dist.all_reduce(counts, op=dist.ReduceOp.SUM, group=self.group)
         return self._views[i], counts.to(count_dtype)

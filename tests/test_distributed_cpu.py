@@ -187,8 +187,8 @@ def test_collectives_on_two_gloo_ranks(tmp_path: Path):
 class _FakeIpc:
     """Stand-in for the CUDA IPC / scatter-kernel layer of PackedSpikeExchange
     on CPU ranks: addresses encode (owner rank, buffer); 'opening' a peer's
-    handle yields a distinct importer address; the scatter records its sinks
-    and counts spikes with numpy."""
+    handle yields a distinct importer address; the scatter records its
+    destinations and counts spikes with torch."""
 
     IMPORT = 1 << 50
 
@@ -216,8 +216,8 @@ class _FakeIpc:
         self.calls.append(("open", address))
         return address | self.IMPORT
 
-    def pack_count_scatter(self, spikes, rows, n, sinks, c64, c32):
-        self.calls.append(("scatter", tuple(sinks)))
+    def pack_count_scatter(self, spikes, words, rows, n, peers, c64, c32):
+        self.calls.append(("scatter", words, tuple(peers)))
         out = c64 if c64 is not None else c32
         out.copy_((spikes.reshape(rows, n) != 0).sum(0).to(out.dtype))
 
@@ -239,10 +239,10 @@ def _exchange_worker(rank: int, world: int, init: str, queue) -> None:
         own = [c[1] for c in fake.calls if c[0] == "alloc"]
         ok = ok and all(c[2] == world * slot for c in fake.calls if c[0] == "alloc")
 
-        def expected_sinks(i):
-            bases = [own[i] if d == rank else ((((d + 1) << 40) | (i << 32)) | _FakeIpc.IMPORT)
-                     for d in range(world)]
-            return tuple(b + rank * slot for b in bases)
+        def expected_slots(i):
+            peers = [((((d + 1) << 40) | (i << 32)) | _FakeIpc.IMPORT) + rank * slot
+                     for d in range(world) if d != rank]
+            return own[i] + rank * slot, tuple(peers)
 
         totals = []
         for step in range(3):
@@ -251,7 +251,7 @@ def _exchange_worker(rank: int, world: int, init: str, queue) -> None:
             ok = ok and view.shape == (world, 4, 3, 3) and counts.dtype == torch.int64
             totals.append(counts)
             scatter = [c for c in fake.calls if c[0] == "scatter"][-1]
-            ok = ok and scatter[1] == expected_sinks(step % 2)  # two buffers, used alternately
+            ok = ok and scatter[1:] == expected_slots(step % 2)  # two buffers, used alternately
         expect = [sum((torch.rand(shape, generator=torch.Generator().manual_seed(10 * s + r)) < 0.3)
                       .sum((0, 1)).to(torch.int64) for r in range(world)) for s in range(3)]
         ok = ok and all(torch.equal(a, b) for a, b in zip(totals, expect))
