@@ -221,6 +221,8 @@ def run_gpu(args) -> None:
         return run_network(args, world, rank, local)
     if name == "izhikevich_fp32":
         return run_izhikevich(args, world, rank, local)
+    if name == "lif_packed":
+        return run_lif_packed(args, world, rank, local)
     x, gs, forward = scan_workload(name, rank)
     x.requires_grad_(True)
     stream = torch.cuda.current_stream()
@@ -566,6 +568,85 @@ def run_izhikevich(args, world, rank, local) -> None:
         print(json.dumps(result), flush=True)
 
 
+def run_lif_packed(args, world, rank, local) -> None:
+    """LIF forward with packed spike output at the north-star shape (T=256,
+    B=128 per GPU, N=4096, fp32, x ~ N(0.3, 0.5)), followed at N > 1 by the
+    packed all-gather of every rank's words: the forward-only communication
+    path of the packed modules. ``--allgather fused`` writes the words into
+    this rank's slot of a peer-mapped gather buffer and copies the slot to
+    the peers (``PackedSpikeExchange.lif_forward_packed_spikes``); ``nccl``
+    runs ``lif_forward_packed_spikes`` then ``all_gather_into_tensor``."""
+
+    import myelin_b200 as mb
+    from myelin_b200 import _native as nat
+
+    T, B, N = T_STEPS, BATCH, NEURONS
+    gen = torch.Generator(device="cuda").manual_seed(41 + rank)
+    x = torch.randn((T, B, N), generator=gen, device="cuda") * 0.5 + 0.3
+    state0 = mb.LIFState(torch.zeros((B, N), device="cuda"))
+    params = mb.LIFParams(tau_mem=10.0)
+    stream = torch.cuda.current_stream()
+    fused = world > 1 and args.allgather == "fused"
+    exchange = mb.PackedSpikeExchange((T, B, N)) if fused else None
+    gather_buf = torch.empty((world, T, B, N // 32), dtype=torch.int32, device="cuda")
+
+    def step():
+        if fused:
+            return exchange.lif_forward_packed_spikes(x, state0, params)[1]
+        _, packed = mb.lif_forward_packed_spikes(x, state0, params)
+        if world > 1:
+            mb.packed_spike_all_gather_into_tensor(packed, out=gather_buf)
+        return packed.data
+
+    for _ in range(args.warmup):
+        words = step()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(args.steps):
+            words = step()
+        stop.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+    ms = max_over_ranks(start.elapsed_time(stop), world) / args.steps
+    units = T * B * N
+    algo = units * (4 + 0.125)  # read x (4 B) + write packed words (1/8 B) per neuron-step
+    peak, peak_kind = load_peak_hbm()
+    achieved = algo / (ms / 1e3) / 1e9
+    result = {
+        "metric": "LIF packed forward neuron-timesteps/s (+ packed all-gather at N > 1)",
+        "value": units * world / (ms / 1e3), "unit": "neuron-steps/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic currents ~ N(0.3, 0.5)",
+        "config": {"workload": "lif_packed (north-star shape, forward only)", "T": T,
+                   "B_per_gpu": B, "N": N,
+                   "allgather": ("peer-mapped slot + copies over NVLink" if fused else
+                                 "NCCL all_gather_into_tensor" if world > 1 else None),
+                   "l2": "x is 537 MB (larger than L2), no flush"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None,
+                     "note": "scan bytes over the whole step (all-gather included at N > 1)"},
+        "words_checksum": int(words.sum().item()),
+        "gpu_launches": args.steps, "device_status": nat.device_status(clear=True),
+    }
+    clk = clocks.summary()
+    if clk is not None:
+        result["clocks"] = clk
+    if exchange is not None:
+        exchange.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
 def run_pack_count(args, world, rank, local) -> None:
     """Bernoulli(0.05) spikes [128, 1024, 8192], batch sharded over ranks.
 
@@ -740,13 +821,13 @@ def main() -> None:
     parser.add_argument("--impl", choices=("mine", "reference"), default="mine")
     parser.add_argument("--workload",
                         choices=("alif_bf16", "lif_fp32", "pack_count", "mlp_fp32", "rate_net",
-                                 "izhikevich_fp32"),
+                                 "izhikevich_fp32", "lif_packed"),
                         default="alif_bf16")
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--allgather", choices=("fused", "nccl"), default="fused",
-                        help="pack_count at N > 1: fused pack + peer-store all-gather, or "
-                             "pack then NCCL all_gather_into_tensor")
+                        help="pack_count / lif_packed at N > 1: the peer-mapped exchange "
+                             "(PackedSpikeExchange), or NCCL all_gather_into_tensor")
     parser.add_argument("--batch", type=int, default=None,
                         help="per-GPU batch of the network workloads (default: the BASELINE "
                              "config's); smaller values are for profiling captures")

@@ -122,6 +122,26 @@ int mb_scan_forward(int neuron, int dtype, const void* x, const void* v0, const 
                     float beta, int reset_mode, void* stream);
 
 /*
+ * Packed-only LIF/ALIF forward (as mb_scan_forward with only `packed`) whose
+ * words also go to `num_peers` (0..7) peer slots: `peers` is a host array of
+ * device pointers, each the start of this rank's [T, B, ceil(N/32)] slot in
+ * another rank's gather buffer (mapped with mb_ipc_open). The scan writes
+ * `packed` (this rank's slot of its own buffer); one copy per peer on the
+ * same stream then moves the slot over NVLink. Like mb_pack_count_scatter it
+ * does not wait for peers: the caller orders later reads of the gather
+ * buffers after every rank's call.
+ * Replaces: kernels.lif_forward_packed_spikes (src/myelin/kernels.py:96-156)
+ *   followed by distributed.packed_spike_all_gather (distributed.py:63-80),
+ *   the forward-only communication path of the packed linear module
+ *   (kernels.py:705-776, modules.py:906-943).
+ */
+int mb_scan_forward_packed_scatter(int neuron, int dtype, const void* x, const void* v0,
+                                   const void* a0, void* vT, void* aT, int32_t* packed,
+                                   void* const* peers, int num_peers, int64_t T, int64_t B,
+                                   int64_t N, float decay, float threshold, float reset,
+                                   float adapt_decay, float beta, int reset_mode, void* stream);
+
+/*
  * Reverse-time surrogate backward of mb_scan_forward. Replays each chunk from
  * its checkpoint in registers (bit-identical to the forward), then walks it in
  * reverse:

@@ -76,6 +76,10 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mb_izhikevich_forward": (
         _int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp]
     ),
+    "mb_scan_forward_packed_scatter": (
+        _int, [_int, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _i64, _i64, _i64, _f, _f, _f,
+               _f, _f, _int, _vp]
+    ),
     "mb_pack_count_scatter": (
         _int, [_int, _vp, _vp, _i64, _i64, _vp, _int, _vp, _vp, _vp, _i64, _vp]
     ),
@@ -334,6 +338,37 @@ def izhikevich_forward(
             T, B, N, ctypes.addressof(params), stream_handle(x.device),
         )
     check(status, "mb_izhikevich_forward")
+
+
+def scan_forward_packed_scatter(
+    *,
+    neuron: int,
+    x: torch.Tensor,
+    v0: torch.Tensor,
+    a0: torch.Tensor | None,
+    vT: torch.Tensor | None,
+    aT: torch.Tensor | None,
+    packed: int,
+    peers: list[int],
+    decay: float,
+    threshold: float,
+    reset: float,
+    adapt_decay: float,
+    beta: float,
+    reset_mode: int,
+) -> None:
+    """Packed-only forward whose words go to device address ``packed`` and to
+    every address in ``peers`` (this rank's slot in the other ranks' buffers)."""
+
+    T, B, N = x.shape
+    arr = (ctypes.c_void_p * max(len(peers), 1))(*peers)
+    with torch.cuda.device(x.device):
+        status = lib().mb_scan_forward_packed_scatter(
+            neuron, dtype_code(x.dtype), ptr(x), ptr(v0), ptr(a0), ptr(vT), ptr(aT), packed, arr,
+            len(peers), T, B, N, decay, threshold, reset, adapt_decay, beta, reset_mode,
+            stream_handle(x.device),
+        )
+    check(status, "mb_scan_forward_packed_scatter")
 
 
 def pack_count_scatter(

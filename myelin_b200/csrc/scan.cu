@@ -575,6 +575,38 @@ extern "C" int mb_scan_forward(int neuron, int dtype, const void* x, const void*
   return 0;
 }
 
+extern "C" int mb_scan_forward_packed_scatter(int neuron, int dtype, const void* x,
+                                              const void* v0, const void* a0, void* vT, void* aT,
+                                              int32_t* packed, void* const* peers, int num_peers,
+                                              int64_t T, int64_t B, int64_t N, float decay,
+                                              float threshold, float reset, float adapt_decay,
+                                              float beta, int reset_mode, void* stream) {
+  clear_error();
+  MB_CHECK_ARG(neuron == MB_LIF || neuron == MB_ALIF,
+               "mb_scan_forward_packed_scatter: LIF or ALIF only");
+  MB_CHECK_ARG(num_peers >= 0 && num_peers <= 7 && (num_peers == 0 || peers),
+               "mb_scan_forward_packed_scatter: 0 to 7 peer slots required");
+  MB_CHECK_ARG(packed != nullptr || T * B * N == 0,
+               "mb_scan_forward_packed_scatter: packed is required");
+  for (int d = 0; d < num_peers; ++d) {
+    MB_CHECK_ARG(peers[d] != nullptr, "mb_scan_forward_packed_scatter: peer slot %d is null", d);
+  }
+  // The scan writes the words into this GPU's slot at full speed; the copy
+  // engines then move the whole slot to each peer in one transfer. (Stores
+  // of the words from the scan itself reach NVLink as 4- to 32-byte pieces
+  // — one step of one 256-neuron tile — which made the step slower than this.)
+  const int rc = mb_scan_forward(neuron, dtype, x, v0, a0, vT, aT, nullptr, packed, nullptr,
+                                 nullptr, nullptr, T, B, N, decay, threshold, reset, adapt_decay,
+                                 beta, reset_mode, stream);
+  if (rc != 0) return rc;
+  const size_t bytes = size_t(T) * size_t(B) * size_t(ceil_div(N, 32)) * sizeof(int32_t);
+  if (bytes == 0) return 0;
+  cudaStream_t s = as_stream(stream);
+  for (int d = 0; d < num_peers; ++d) cudaMemcpyAsync(peers[d], packed, bytes, cudaMemcpyDefault, s);
+  MB_CHECK_LAUNCH("mb_scan_forward_packed_scatter");
+  return 0;
+}
+
 extern "C" int mb_scan_backward(int neuron, int dtype, const void* x, const float* ckpt_v,
                                 const float* ckpt_a, const void* grad_spikes,
                                 const void* grad_rates, const void* grad_vT, const void* grad_aT,

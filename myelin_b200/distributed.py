@@ -252,6 +252,90 @@ class PackedSpikeExchange:
         dist.all_reduce(counts, op=dist.ReduceOp.SUM, group=self.group)
         return self._views[i], counts.to(count_dtype)
 
+    def lif_forward_packed_spikes(
+        self, inputs: torch.Tensor, initial_state: Any, params: Any, *, reset_mode: str = "hard"
+    ) -> tuple[Any, torch.Tensor]:
+        """``kernels.lif_forward_packed_spikes`` feeding the all-gather directly.
+
+        The scan writes its packed words straight into this rank's slot of
+        its own gather buffer and the copy engines move that slot into every
+        peer's buffer over NVLink (src/myelin/kernels.py:96-156 followed by
+        distributed.py:63-80, with no staging buffer and no NCCL all-gather).
+        Returns the final ``LIFState`` and the gathered words ``[world, T, B,
+        ceil(N/32)]``, which equal ``packed_spike_all_gather_into_tensor`` of
+        every rank's packed output. A one-word all-reduce after the copies
+        completes the step (the same ordering argument as
+        ``pack_count_all_gather``).
+        """
+
+        from myelin_b200 import _native as nat
+        from myelin_b200 import kernels as K
+        from myelin_b200.neurons import LIFState
+
+        rc = K._reset_code(reset_mode)
+        K._validate_scan(inputs, [("membrane", initial_state.membrane)])
+        vT = self._scan_scatter(inputs.contiguous(), initial_state.membrane.contiguous(), params,
+                                rc, nat.MB_LIF)
+        return LIFState(membrane=vT), self._views[(self._step - 1) % len(self._slots)]
+
+    def linear_surrogate_lif_packed_forward(
+        self,
+        inputs: torch.Tensor,
+        weight: torch.Tensor,
+        bias: torch.Tensor | None,
+        params: Any,
+        *,
+        surrogate: str = "atan",
+        surrogate_slope: float = 10.0,
+        hard_forward: bool = True,
+        checkpoint_size: Any = 25,
+    ) -> tuple[Any, torch.Tensor]:
+        """``kernels.linear_surrogate_lif_packed_forward`` feeding the all-gather
+        directly: the projection, then the packed scan into this rank's slot
+        and the copies to every peer (src/myelin/kernels.py:705-776 followed
+        by distributed.py:63-80). Forward only, like the reference's packed
+        path. Returns the final ``LIFState`` and the gathered words."""
+
+        from myelin_b200 import _native as nat
+        from myelin_b200 import kernels as K
+        from myelin_b200.autograd import _project
+        from myelin_b200.checkpointing import resolve_checkpoint_size
+        from myelin_b200.neurons import LIFState
+        from myelin_b200.surrogates import surrogate_id
+
+        surrogate_id(surrogate)
+        resolve_checkpoint_size(int(inputs.shape[0]), checkpoint_size)
+        K._hard_forward_only(hard_forward, "packed surrogate LIF")
+        K._validate_linear(inputs, weight, bias)
+        with torch.no_grad():
+            T, B, F = inputs.shape
+            N = weight.shape[1]
+            x2 = inputs.contiguous().reshape(T * B, F)
+            currents = _project(x2, weight.contiguous(), bias).view(T, B, N)
+            v0 = torch.zeros((B, N), dtype=inputs.dtype, device=inputs.device)
+            vT = self._scan_scatter(currents, v0, params, nat.MB_RESET_HARD, nat.MB_LIF)
+        return LIFState(membrane=vT), self._views[(self._step - 1) % len(self._slots)]
+
+    def _scan_scatter(self, x: torch.Tensor, v0: torch.Tensor, params: Any, reset_mode: int,
+                      neuron: int) -> torch.Tensor:
+        if tuple(x.shape) != self.local_shape:
+            raise ValueError(f"spikes must be shaped {self.local_shape}; got {tuple(x.shape)}")
+        if x.device != self.device:
+            raise ValueError(f"inputs must be on {self.device}")
+        i = self._step % len(self._slots)
+        self._step += 1
+        own, peers = self._slots[i]
+        vT = torch.empty_like(v0)
+        self._nat.scan_forward_packed_scatter(
+            neuron=neuron, x=x, v0=v0, a0=None, vT=vT, aT=None, packed=own, peers=peers,
+            decay=params.decay, threshold=float(params.threshold), reset=float(params.reset),
+            adapt_decay=0.0, beta=0.0, reset_mode=reset_mode,
+        )
+        # completion: no rank's all-reduce ends before every rank's kernel has
+        flag = torch.zeros((1,), dtype=torch.int32, device=self.device)
+        dist.all_reduce(flag, group=self.group)
+        return vT
+
     def close(self) -> None:
         """Unmap the peers' buffers, wait for every rank, free this rank's."""
 

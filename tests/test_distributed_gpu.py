@@ -85,6 +85,11 @@ def _exchange_spikes(rank: int, step: int, shape) -> torch.Tensor:
     return torch.rand(shape, generator=gen) < 0.1
 
 
+def _exchange_currents(rank: int, step: int, shape) -> torch.Tensor:
+    gen = torch.Generator(device="cuda").manual_seed(500 * step + 11 * rank + shape[-1])
+    return 0.3 + 0.5 * torch.randn(shape, generator=gen, device="cuda")
+
+
 def _exchange_worker(rank: int, world: int, init: str, queue) -> None:
     from datetime import timedelta
 
@@ -111,7 +116,40 @@ def _exchange_worker(rank: int, world: int, init: str, queue) -> None:
                                for r in range(world)).cuda()
                 if counts.dtype != torch.int64 or not torch.equal(counts, expected):
                     ok, msg = False, f"counts, shape {shape}, step {step}"
+            # the packed scan feeding the same buffers (fused forward / fallback)
+            params = mb.LIFParams(tau_mem=8.0)
+            for step in range(2):
+                xs = [_exchange_currents(r, step, shape) for r in range(world)]
+                v0 = torch.full(shape[1:], 0.25, device="cuda")
+                st, view = ex.lif_forward_packed_spikes(xs[rank], mb.LIFState(v0), params,
+                                                        reset_mode="subtract")
+                torch.cuda.synchronize()
+                for r in range(world):
+                    ref_st, ref = mb.lif_forward_packed_spikes(xs[r], mb.LIFState(v0), params,
+                                                               reset_mode="subtract")
+                    if not torch.equal(view[r], ref.data):
+                        ok, msg = False, f"scan words of rank {r}, shape {shape}, step {step}"
+                    if r == rank and not torch.equal(st.membrane, ref_st.membrane):
+                        ok, msg = False, f"scan state, shape {shape}, step {step}"
             ex.close()
+        # projection + packed scan (bf16, tcgen05 GEMM) feeding the buffers
+        T, B, F, N = 12, 8, 64, 256
+        ex = mb.PackedSpikeExchange((T, B, N))
+        g = torch.Generator(device="cuda").manual_seed(5)
+        w = (0.2 * torch.randn((F, N), generator=g, device="cuda")).to(torch.bfloat16)
+        b = (0.1 * torch.randn((N,), generator=g, device="cuda")).to(torch.bfloat16)
+        xs = [(torch.rand((T, B, F), generator=torch.Generator(device="cuda").manual_seed(40 + r),
+                          device="cuda") < 0.3).to(torch.bfloat16) for r in range(world)]
+        params = mb.LIFParams(tau_mem=20.0)
+        st, view = ex.linear_surrogate_lif_packed_forward(xs[rank], w, b, params)
+        torch.cuda.synchronize()
+        for r in range(world):
+            ref_st, ref = mb.linear_surrogate_lif_packed_forward(xs[r], w, b, params)
+            if not torch.equal(view[r], ref.data):
+                ok, msg = False, f"linear packed words of rank {r}"
+            if r == rank and not torch.equal(st.membrane, ref_st.membrane):
+                ok, msg = False, "linear packed state"
+        ex.close()
         torch.cuda.synchronize()
         queue.put((rank, bool(ok), msg))
     except Exception as exc:
@@ -120,13 +158,14 @@ def _exchange_worker(rank: int, world: int, init: str, queue) -> None:
         dist.destroy_process_group()
 
 
-def test_packed_spike_exchange_over_nvlink(tmp_path: Path):
-    """Fused pack + peer-store all-gather + count all-reduce on 2 GPUs equals
-    every rank's pack_spikes and the summed counts, bit for bit."""
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_packed_spike_exchange_over_nvlink(tmp_path: Path, world: int):
+    """Fused pack + peer-store all-gather + count all-reduce on 2-8 GPUs equals
+    every rank's pack_spikes and the summed counts, bit for bit; the packed
+    scans feeding the same buffers equal every rank's packed forward."""
 
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    world = 2
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = multiprocessing.get_context("spawn")
     queue = ctx.Queue()
     init = f"file://{tmp_path / 'rdzv_exchange'}"
