@@ -239,15 +239,17 @@ int mb_count_columns(const int32_t* words, int64_t rows, int64_t n, int64_t* cou
                      int32_t* counts32, void* workspace, int64_t workspace_bytes,
                      void* stream);
 
-/* Workspace (bytes, device memory) that mb_pack_count_spikes needs. */
+/* Workspace (bytes, device memory) that mb_pack_count_spikes needs (used by
+ * the pack-then-count path; the one-pass path adds each row slice's counts
+ * straight into the totals with integer atomics). */
 int64_t mb_pack_count_workspace_bytes(int64_t rows, int64_t n);
 
 /*
  * Pack spikes[rows, n] into words (as mb_pack_spikes) and count spikes per
  * neuron over all rows (as mb_count_columns on the words) in one call. For
- * aligned 1-byte spikes (bool / uint8 / int8) with n % 32 == 0 and a 16-byte
- * aligned workspace this is one pass over the spikes; other inputs run the
- * pack and the count kernels in sequence. Same results either way.
+ * aligned 1-byte spikes (bool / uint8 / int8) with n % 32 == 0 this is one
+ * pass over the spikes; other inputs run the pack and the count kernels in
+ * sequence. Same results either way (integer sums: exact in any order).
  * `workspace` must hold mb_pack_count_workspace_bytes(rows, n) bytes.
  * Replaces: the pair packing.pack_spikes (src/myelin/packing.py:45-71) +
  *   _packed_spike_counts_over_leading_dims (packing.py:209-216) that one

@@ -297,14 +297,19 @@ struct PeerSlots {
 // stores and no predicates).
 template <bool COUNT, int NPEER>
 __global__ void __launch_bounds__(kPackCountThreads) pack_count_u8_kernel(
-    const uint4* __restrict__ in, uint32_t* __restrict__ words, int32_t* __restrict__ partial,
-    int64_t rows, int64_t W, int64_t rows_per_slice, const PeerSlots peers) {
-  __shared__ int32_t cnt[32][kPackCountThreads];  // [neuron in word][thread]: conflict-free
+    const uint4* __restrict__ in, uint32_t* __restrict__ words,
+    unsigned long long* __restrict__ counts64, unsigned int* __restrict__ counts32, int64_t rows,
+    int64_t W, int64_t rows_per_slice, const PeerSlots peers) {
+  // [neuron in word][thread], one pad column: conflict-free both for a thread
+  // walking its own 32 counters and for a warp reading one thread's 32
+  __shared__ int32_t cnt[32][kPackCountThreads + 1];
   const int tid = threadIdx.x;
   const int64_t wc = int64_t(blockIdx.x) * kPackCountThreads + tid;  // word column
   const int64_t r_begin = int64_t(blockIdx.y) * rows_per_slice;
-  const int64_t r_end = imin64(rows, r_begin + rows_per_slice);
-  if (wc >= W) return;  // no block-wide barrier below: early exit is safe
+  // with counters, columns past W take no rows (they still meet the block
+  // barrier below); without, they leave at once
+  if (!COUNT && wc >= W) return;
+  const int64_t r_end = COUNT && wc >= W ? r_begin : imin64(rows, r_begin + rows_per_slice);
 
   if (COUNT) {
 #pragma unroll
@@ -362,10 +367,22 @@ __global__ void __launch_bounds__(kPackCountThreads) pack_count_u8_kernel(
   if (NPEER > 0) __threadfence_system();  // peer stores ordered before the kernel's end
   if (!COUNT) return;
   flush();
-  int4* dst = reinterpret_cast<int4*>(partial + int64_t(blockIdx.y) * W * 32 + wc * 32);
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    dst[k] = make_int4(cnt[4 * k][tid], cnt[4 * k + 1][tid], cnt[4 * k + 2][tid], cnt[4 * k + 3][tid]);
+  __syncthreads();
+  // The slice's counts go straight into the per-neuron totals: warp w reads
+  // the 32 counters of each of its threads' word columns in turn, so each
+  // reduction instruction covers 32 consecutive neurons (one 128-byte line of
+  // int32 totals). Integer adds: the totals do not depend on their order.
+  const int w = tid >> 5, lane = tid & 31;
+  for (int j = 0; j < 32; ++j) {
+    const int t = 32 * w + j;
+    const int64_t col = int64_t(blockIdx.x) * kPackCountThreads + t;
+    if (col >= W) break;  // uniform over the warp
+    const unsigned int v = static_cast<unsigned int>(cnt[lane][t]);
+    const int64_t neuron = col * 32 + lane;
+    if (v != 0) {
+      if (counts64) atomicAdd(counts64 + neuron, static_cast<unsigned long long>(v));
+      if (counts32) atomicAdd(counts32 + neuron, v);
+    }
   }
 }
 
@@ -393,8 +410,8 @@ static void launch_pack(const void* spikes, int32_t* words, int64_t rows, int64_
     dim3 grid(static_cast<unsigned>(ceil_div(W, kPackCountThreads)),
               static_cast<unsigned>(slices));
     pack_count_u8_kernel<false, 0><<<grid, kPackCountThreads, 0, s>>>(
-        static_cast<const uint4*>(spikes), reinterpret_cast<uint32_t*>(words), nullptr, rows, W,
-        ceil_div(rows, slices), PeerSlots{});
+        static_cast<const uint4*>(spikes), reinterpret_cast<uint32_t*>(words), nullptr, nullptr,
+        rows, W, ceil_div(rows, slices), PeerSlots{});
   } else if (n % 32 == 0 && aligned_to(spikes, 16)) {
     const int64_t n_vec = rows * n * int64_t(sizeof(U)) / 16;
     pack_vec_kernel<DT><<<grid_for(n_vec), 256, 0, s>>>(static_cast<const uint4*>(spikes), words,
@@ -472,37 +489,41 @@ static int64_t pack_count_slices(int64_t rows, int64_t n) {
   return slices;
 }
 
-static bool pack_count_fused_ok(int dtype, const void* spikes, int64_t n, const void* workspace) {
-  return dtype == MB_U8 && n % 32 == 0 && aligned_to(spikes, 16) && aligned_to(workspace, 16);
+static bool pack_count_fused_ok(int dtype, const void* spikes, int64_t n) {
+  return dtype == MB_U8 && n % 32 == 0 && aligned_to(spikes, 16);
 }
 
+// The fused kernel needs no scratch; the pack-then-count path (other dtypes,
+// ragged or unaligned spikes) needs the column count's.
 int64_t pack_count_workspace_bytes(int64_t rows, int64_t n) {
   if (rows <= 0 || n <= 0) return 0;
-  const int64_t fused = n % 32 == 0 ? pack_count_slices(rows, n) * n * int64_t(sizeof(int32_t)) : 0;
-  const int64_t split = count_columns_workspace_bytes(rows, n);
-  return fused > split ? fused : split;
+  return count_columns_workspace_bytes(rows, n);
 }
 
 // Pack + per-neuron count: one fused pass for aligned 1-byte spikes with
 // n % 32 == 0, else the pack kernel followed by the column count of the words.
-// The fused pack + count of aligned 1-byte spikes (n % 32 == 0): packing
-// kernel (words to `words` and to `npeer` peer slots) + slice-sum kernel.
+// The fused pack + count of aligned 1-byte spikes (n % 32 == 0): the totals
+// are zeroed, then one kernel packs (words to `words` and to `npeer` peer
+// slots) and adds each row slice's counts into them.
 static void launch_pack_count_u8(const void* spikes, int32_t* words, const PeerSlots& peers,
                                  int npeer, int64_t rows, int64_t n, int64_t* counts64,
-                                 int32_t* counts32, void* workspace, cudaStream_t s) {
+                                 int32_t* counts32, cudaStream_t s) {
   const int64_t W = n / 32;
   const int64_t slices = pack_count_slices(rows, n);
   const dim3 grid(static_cast<unsigned>(ceil_div(W, kPackCountThreads)),
                   static_cast<unsigned>(slices));
   const auto* in = static_cast<const uint4*>(spikes);
   auto* out = reinterpret_cast<uint32_t*>(words);
-  auto* partial = static_cast<int32_t*>(workspace);
+  auto* c64 = reinterpret_cast<unsigned long long*>(counts64);
+  auto* c32 = reinterpret_cast<unsigned int*>(counts32);
+  if (c64) cudaMemsetAsync(c64, 0, size_t(n) * sizeof(int64_t), s);
+  if (c32) cudaMemsetAsync(c32, 0, size_t(n) * sizeof(int32_t), s);
   const int64_t per_slice = ceil_div(rows, slices);
   switch (npeer) {
-#define MB_PACK_PEERS(K)                                                                   \
-  case K:                                                                                  \
-    pack_count_u8_kernel<true, K>                                                          \
-        <<<grid, kPackCountThreads, 0, s>>>(in, out, partial, rows, W, per_slice, peers); \
+#define MB_PACK_PEERS(K)                                                                     \
+  case K:                                                                                    \
+    pack_count_u8_kernel<true, K>                                                            \
+        <<<grid, kPackCountThreads, 0, s>>>(in, out, c64, c32, rows, W, per_slice, peers);  \
     break;
     MB_PACK_PEERS(0)
     MB_PACK_PEERS(1)
@@ -515,16 +536,14 @@ static void launch_pack_count_u8(const void* spikes, int32_t* words, const PeerS
 #undef MB_PACK_PEERS
     default: break;
   }
-  count_columns_final_kernel<<<static_cast<unsigned>(ceil_div(n, 32)), 256, 0, s>>>(
-      partial, slices, n, counts64, counts32);
 }
 
 template <int DT>
 static void launch_pack_count(const void* spikes, int32_t* words, int64_t rows, int64_t n,
                               int64_t* counts64, int32_t* counts32, void* workspace,
                               cudaStream_t s) {
-  if (pack_count_fused_ok(DT, spikes, n, workspace)) {
-    launch_pack_count_u8(spikes, words, PeerSlots{}, 0, rows, n, counts64, counts32, workspace, s);
+  if (pack_count_fused_ok(DT, spikes, n)) {
+    launch_pack_count_u8(spikes, words, PeerSlots{}, 0, rows, n, counts64, counts32, s);
     return;
   }
   launch_pack<DT>(spikes, words, rows, n, s);
@@ -587,6 +606,8 @@ extern "C" int mb_count_columns(const int32_t* words, int64_t rows, int64_t n, i
   clear_error();
   MB_CHECK_ARG(rows >= 0 && n > 0, "mb_count_columns: packed.original_shape must have non-empty last dimension");
   MB_CHECK_ARG(counts64 != nullptr || counts32 != nullptr, "mb_count_columns: no output");
+  MB_CHECK_ARG(aligned_to(counts64, 8) && aligned_to(counts32, 4),
+               "mb_count_columns: counts misaligned");
   cudaStream_t s = as_stream(stream);
   if (rows == 0) {
     if (counts64) cudaMemsetAsync(counts64, 0, n * sizeof(int64_t), s);
@@ -616,6 +637,8 @@ extern "C" int mb_pack_count_spikes(int dtype, const void* spikes, int32_t* word
   MB_CHECK_ARG(valid_io_dtype(dtype), "mb_pack_count_spikes: unknown dtype %d", dtype);
   MB_CHECK_ARG(rows >= 0 && n > 0, "mb_pack_count_spikes: cannot pack an empty last dimension");
   MB_CHECK_ARG(counts64 != nullptr || counts32 != nullptr, "mb_pack_count_spikes: no output");
+  MB_CHECK_ARG(aligned_to(counts64, 8) && aligned_to(counts32, 4),
+               "mb_pack_count_spikes: counts misaligned");
   cudaStream_t s = as_stream(stream);
   if (rows == 0) {
     if (counts64) cudaMemsetAsync(counts64, 0, n * sizeof(int64_t), s);
@@ -643,6 +666,8 @@ extern "C" int mb_pack_count_scatter(int dtype, const void* spikes, int32_t* wor
   MB_CHECK_ARG(valid_io_dtype(dtype), "mb_pack_count_scatter: unknown dtype %d", dtype);
   MB_CHECK_ARG(rows >= 0 && n > 0, "mb_pack_count_scatter: cannot pack an empty last dimension");
   MB_CHECK_ARG(counts64 != nullptr || counts32 != nullptr, "mb_pack_count_scatter: no output");
+  MB_CHECK_ARG(aligned_to(counts64, 8) && aligned_to(counts32, 4),
+               "mb_pack_count_scatter: counts misaligned");
   MB_CHECK_ARG(words != nullptr && aligned_to(words, 4),
                "mb_pack_count_scatter: words null or misaligned");
   MB_CHECK_ARG(num_peers >= 0 && num_peers <= kMaxPeerSlots && (num_peers == 0 || peers),
@@ -664,11 +689,10 @@ extern "C" int mb_pack_count_scatter(int dtype, const void* spikes, int32_t* wor
                "mb_pack_count_scatter: workspace of %lld bytes required, got %lld",
                (long long)need, (long long)workspace_bytes);
   MB_CHECK_ARG(aligned_to(workspace, 4), "mb_pack_count_scatter: workspace misaligned");
-  if (pack_count_fused_ok(dtype, spikes, n, workspace)) {
+  if (pack_count_fused_ok(dtype, spikes, n)) {
     PeerSlots slots{};
     for (int d = 0; d < num_peers; ++d) slots.p[d] = static_cast<uint32_t*>(peers[d]);
-    launch_pack_count_u8(spikes, words, slots, num_peers, rows, n, counts64, counts32, workspace,
-                         s);
+    launch_pack_count_u8(spikes, words, slots, num_peers, rows, n, counts64, counts32, s);
   } else {
     // other shapes: pack + count into `words`, then one copy per peer slot
     // (over NVLink)
