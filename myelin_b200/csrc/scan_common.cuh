@@ -173,6 +173,7 @@ struct Pair;
 template <>
 struct Pair<float> {
   using V = float2;
+  static __device__ __forceinline__ float2 join(float a, float b) { return make_float2(a, b); }
   static __device__ __forceinline__ float2 to_f2(float2 v) { return v; }
   static __device__ __forceinline__ float2 from_f2(float a, float b) { return make_float2(a, b); }
   static __device__ __forceinline__ float2 spikes(bool s0, bool s1) {
@@ -183,6 +184,9 @@ struct Pair<float> {
 template <>
 struct Pair<__nv_bfloat16> {
   using V = uint32_t;  // bf16x2, low half = first neuron
+  static __device__ __forceinline__ uint32_t join(__nv_bfloat16 a, __nv_bfloat16 b) {
+    return uint32_t(__bfloat16_as_ushort(a)) | (uint32_t(__bfloat16_as_ushort(b)) << 16);
+  }
   static __device__ __forceinline__ float2 to_f2(uint32_t v) {
     return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
   }
@@ -198,6 +202,9 @@ struct Pair<__nv_bfloat16> {
 template <>
 struct Pair<__half> {
   using V = uint32_t;  // f16x2, low half = first neuron
+  static __device__ __forceinline__ uint32_t join(__half a, __half b) {
+    return uint32_t(__half_as_ushort(a)) | (uint32_t(__half_as_ushort(b)) << 16);
+  }
   static __device__ __forceinline__ float2 to_f2(uint32_t v) {
     return __half22float2(*reinterpret_cast<const __half2*>(&v));
   }

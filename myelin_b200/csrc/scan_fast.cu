@@ -170,12 +170,30 @@ __global__ void __launch_bounds__(kThreads, 6) scan_fwd_fast_kernel(
   }
 
   const int tid = threadIdx.x;  // 0 .. 32*kConsumerWarps-1
-  const bool valid = 2 * tid < tile_n;  // tile_n is even
+  // Neurons of a thread: the adjacent pair e, e + 1 (e = e0 + 2 tid), so that
+  // one vector access moves both; or, for packed output only (kSplit), lane l
+  // of warp w owns neurons l and l + 32 of the warp's 64 (ea = e0 + 64 w + l,
+  // eb = ea + 32), so that each ballot over the warp is already a finished
+  // 32-neuron word (no bit interleaving per step). Packed output needs
+  // N % 32 == 0, so tile_n is a multiple of 32 and both halves of a warp are
+  // wholly inside or outside the tile.
+  constexpr bool kSplit = MODE == kFwdPacked;
+  using E = Elem<T>;
+  const bool valid = kSplit ? 64 * warp < tile_n : 2 * tid < tile_n;  // tile_n is even
+  const bool valid_b = kSplit ? 64 * warp + 32 < tile_n : valid;
   const int64_t e = e0 + 2 * tid;
+  const int64_t ea = e0 + 64 * warp + lane, eb = ea + 32;
   constexpr bool kTwoStates = KIND != MB_LIF;  // ALIF adaptation / Izhikevich recovery
   F2 m = f2(0.0f), ad = f2(0.0f);
   int c0 = 0, c1 = 0;
-  if (valid) {
+  if constexpr (kSplit) {
+    const T* v0 = static_cast<const T*>(a.v0);
+    const T* a0 = static_cast<const T*>(a.a0);
+    m = f2(make_float2(valid ? E::to_f(v0[ea]) : 0.0f, valid_b ? E::to_f(v0[eb]) : 0.0f));
+    if (kTwoStates) {
+      ad = f2(make_float2(valid ? E::to_f(a0[ea]) : 0.0f, valid_b ? E::to_f(a0[eb]) : 0.0f));
+    }
+  } else if (valid) {
     m = f2(P::to_f2(reinterpret_cast<const V*>(a.v0)[e >> 1]));
     if (kTwoStates) ad = f2(P::to_f2(reinterpret_cast<const V*>(a.a0)[e >> 1]));
   }
@@ -193,22 +211,24 @@ __global__ void __launch_bounds__(kThreads, 6) scan_fwd_fast_kernel(
   // packed words: this warp's 64 neurons are flat words q and q+1; with
   // N % 32 == 0 every word lies wholly inside or wholly outside the tile
   const int64_t words_per_t = a.BN >> 5;
-  const int64_t q = (e0 >> 5) + 2 * warp + (lane >> 4);
+  const int64_t q = (e0 >> 5) + 2 * warp + (kSplit ? lane : lane >> 4);
   int32_t* pk = do_packed ? a.packed + q : nullptr;
-  const bool pk_lane = (lane & 15) == 0 && (q << 5) < a.BN;
-  const int sh = lane & 16;  // lanes 0-15 -> word q, lanes 16-31 -> word q+1
+  // pair layout: lanes 0 and 16 store words q and q + 1 (built from the even
+  // and odd ballots); split layout: lanes 0 and 1 store the two ballots
+  const bool pk_lane = kSplit ? (lane == 0 && valid) || (lane == 1 && valid_b)
+                              : (lane & 15) == 0 && (q << 5) < a.BN;
+  const int sh = lane & 16;  // pair layout: lanes 0-15 -> word q, lanes 16-31 -> word q+1
 
   // a register copy: referring to the parameter block itself would place it
   // in local memory
   const IzhConsts izc = a.izh;
-  auto step = [&](V xv, V* slot) {
+  auto step = [&](float2 xf, V* slot) {
     Step2<KIND == kIzhikevich ? MB_LIF : KIND, RESET> st;
     if constexpr (KIND == kIzhikevich) {
-      const float2 xf = P::to_f2(xv);
       st.s0 = izh_step(m.x, ad.x, xf.x, izc);
       st.s1 = izh_step(m.y, ad.y, xf.y, izc);
     } else {
-      st.run(m, ad, f2(P::to_f2(xv)), decay, nthr, reset_v, adapt_decay, nbeta);
+      st.run(m, ad, f2(xf), decay, nthr, reset_v, adapt_decay, nbeta);
     }
     if (kRates) {
       c0 += st.s0 ? 1 : 0;
@@ -218,7 +238,9 @@ __global__ void __launch_bounds__(kThreads, 6) scan_fwd_fast_kernel(
     if (kPacked && (MODE != kFwdAny || pk != nullptr)) {
       const uint32_t even = __ballot_sync(0xffffffffu, st.s0);
       const uint32_t odd = __ballot_sync(0xffffffffu, st.s1);
-      const uint32_t word = spread_even_bits(even >> sh) | (spread_even_bits(odd >> sh) << 1);
+      const uint32_t word =
+          kSplit ? (lane == 0 ? even : odd)
+                 : spread_even_bits(even >> sh) | (spread_even_bits(odd >> sh) << 1);
       if (pk_lane) *pk = static_cast<int32_t>(word);
       pk += words_per_t;
     }
@@ -230,22 +252,44 @@ __global__ void __launch_bounds__(kThreads, 6) scan_fwd_fast_kernel(
       bulk_wait_all();  // stores of earlier chunks finish before the early exit
       return;
     }
-    if (a.ckpt_v != nullptr && valid) {
+    if constexpr (kSplit) {
+      if (a.ckpt_v != nullptr) {
+        if (valid) a.ckpt_v[k * a.BN + ea] = split(m).x;
+        if (valid_b) a.ckpt_v[k * a.BN + eb] = split(m).y;
+        if (kTwoStates) {
+          if (valid) a.ckpt_a[k * a.BN + ea] = split(ad).x;
+          if (valid_b) a.ckpt_a[k * a.BN + eb] = split(ad).y;
+        }
+      }
+    } else if (a.ckpt_v != nullptr && valid) {
       reinterpret_cast<float2*>(a.ckpt_v + k * a.BN)[e >> 1] = split(m);
       if (kTwoStates) reinterpret_cast<float2*>(a.ckpt_a + k * a.BN)[e >> 1] = split(ad);
     }
     T* stage = ring + s * kChunk * kTileN;
     V* row = reinterpret_cast<V*>(stage) + tid;
+    const T* srow = stage + 64 * warp + lane;  // split layout: neurons l and l + 32
     const int len = static_cast<int>(imin64(kChunk, a.T - k * kChunk));
-    if (len == kChunk) {
+    if constexpr (kSplit) {
+      if (len == kChunk) {
+        V xv[kChunk];  // the two neurons' inputs joined as one pair value
+#pragma unroll
+        for (int j = 0; j < kChunk; ++j) xv[j] = P::join(srow[j * kTileN], srow[j * kTileN + 32]);
+#pragma unroll
+        for (int j = 0; j < kChunk; ++j) step(P::to_f2(xv[j]), nullptr);
+      } else {
+        for (int j = 0; j < len; ++j) {
+          step(P::to_f2(P::join(srow[j * kTileN], srow[j * kTileN + 32])), nullptr);
+        }
+      }
+    } else if (len == kChunk) {
       // all loads first: the spike stores below alias the same stage
       V xv[kChunk];
 #pragma unroll
       for (int j = 0; j < kChunk; ++j) xv[j] = row[j * (kTileN / 2)];
 #pragma unroll
-      for (int j = 0; j < kChunk; ++j) step(xv[j], row + j * (kTileN / 2));
+      for (int j = 0; j < kChunk; ++j) step(P::to_f2(xv[j]), row + j * (kTileN / 2));
     } else {
-      for (int j = 0; j < len; ++j) step(row[j * (kTileN / 2)], row + j * (kTileN / 2));
+      for (int j = 0; j < len; ++j) step(P::to_f2(row[j * (kTileN / 2)]), row + j * (kTileN / 2));
     }
     if (kDense && (MODE != kFwdAny || do_dense)) {
       if (!store_stage(stage, &done[s], &empty[s], k, kFwdRing, &out_map, e0, k * kChunk)) {
@@ -259,6 +303,15 @@ __global__ void __launch_bounds__(kThreads, 6) scan_fwd_fast_kernel(
   }
   if (kDense && (MODE != kFwdAny || do_dense)) bulk_wait_all();
 
+  if constexpr (kSplit) {
+    T* vT = static_cast<T*>(a.vT);
+    T* aT = static_cast<T*>(a.aT);
+    if (vT && valid) vT[ea] = E::from_f(split(m).x);
+    if (vT && valid_b) vT[eb] = E::from_f(split(m).y);
+    if (kTwoStates && aT && valid) aT[ea] = E::from_f(split(ad).x);
+    if (kTwoStates && aT && valid_b) aT[eb] = E::from_f(split(ad).y);
+    return;
+  }
   if (!valid) return;
   if (a.vT) reinterpret_cast<V*>(a.vT)[e >> 1] = P::from_f2(split(m).x, split(m).y);
   if (kTwoStates && a.aT) reinterpret_cast<V*>(a.aT)[e >> 1] = P::from_f2(split(ad).x, split(ad).y);
