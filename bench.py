@@ -573,8 +573,8 @@ def run_lif_packed(args, world, rank, local) -> None:
     B=128 per GPU, N=4096, fp32, x ~ N(0.3, 0.5)), followed at N > 1 by the
     packed all-gather of every rank's words: the forward-only communication
     path of the packed modules. ``--allgather fused`` writes the words into
-    this rank's slot of a peer-mapped gather buffer and copies the slot to
-    the peers (``PackedSpikeExchange.lif_forward_packed_spikes``); ``nccl``
+    this rank's slot of a peer-mapped gather buffer and a push kernel stores
+    the slot into every peer's (``PackedSpikeExchange.lif_forward_packed_spikes``); ``nccl``
     runs ``lif_forward_packed_spikes`` then ``all_gather_into_tensor``."""
 
     import myelin_b200 as mb
@@ -624,7 +624,7 @@ def run_lif_packed(args, world, rank, local) -> None:
         "data": "synthetic currents ~ N(0.3, 0.5)",
         "config": {"workload": "lif_packed (north-star shape, forward only)", "T": T,
                    "B_per_gpu": B, "N": N,
-                   "allgather": ("peer-mapped slot + copies over NVLink" if fused else
+                   "allgather": ("peer-mapped slot + push kernel over NVLink" if fused else
                                  "NCCL all_gather_into_tensor" if world > 1 else None),
                    "l2": "x is 537 MB (larger than L2), no flush"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",

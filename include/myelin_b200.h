@@ -126,8 +126,8 @@ int mb_scan_forward(int neuron, int dtype, const void* x, const void* v0, const 
  * words also go to `num_peers` (0..7) peer slots: `peers` is a host array of
  * device pointers, each the start of this rank's [T, B, ceil(N/32)] slot in
  * another rank's gather buffer (mapped with mb_ipc_open). The scan writes
- * `packed` (this rank's slot of its own buffer); one copy per peer on the
- * same stream then moves the slot over NVLink. Like mb_pack_count_scatter it
+ * `packed` (this rank's slot of its own buffer); one kernel on the same
+ * stream then stores the slot into every peer slot at once over NVLink. Like mb_pack_count_scatter it
  * does not wait for peers: the caller orders later reads of the gather
  * buffers after every rank's call.
  * Replaces: kernels.lif_forward_packed_spikes (src/myelin/kernels.py:96-156)
@@ -271,7 +271,7 @@ int mb_pack_count_spikes(int dtype, const void* spikes, int32_t* words, int64_t 
  * peers: the caller orders later reads of the gather buffers after every
  * rank's call (the count all-reduce that follows does that). Fused for
  * aligned 1-byte spikes with n % 32 == 0; other inputs pack into `words` and
- * copy it to each peer slot.
+ * a second kernel stores it into every peer slot.
  * Replaces: packing.pack_spikes + distributed.packed_spike_all_gather
  *   (src/myelin/distributed.py:63-80) + the local count of
  *   packed_spike_count_all_reduce (distributed.py:83-98).

@@ -8,6 +8,82 @@
 #include <cstring>
 
 #include "common.cuh"
+#include "exchange.cuh"
+
+namespace mb {
+
+namespace {
+
+template <typename W>
+struct PushPeers {
+  W* p[kMaxPushPeers];
+};
+
+constexpr int kPushUnroll = 4;
+
+// Grid-stride copy of n units (16 or 4 bytes) from src to NPEER peers: each
+// thread keeps kPushUnroll loads in flight, then stores every unit to every
+// peer (a warp stores 512 contiguous bytes per peer per instruction with
+// 16-byte units).
+template <typename W, int NPEER>
+__global__ void __launch_bounds__(256) push_kernel(const W* __restrict__ src,
+                                                   const PushPeers<W> peers, int64_t n) {
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (; i + (kPushUnroll - 1) * stride < n; i += kPushUnroll * stride) {
+    W v[kPushUnroll];
+#pragma unroll
+    for (int u = 0; u < kPushUnroll; ++u) v[u] = src[i + u * stride];
+#pragma unroll
+    for (int u = 0; u < kPushUnroll; ++u) {
+#pragma unroll
+      for (int d = 0; d < NPEER; ++d) peers.p[d][i + u * stride] = v[u];
+    }
+  }
+  for (; i < n; i += stride) {
+    const W v = src[i];
+#pragma unroll
+    for (int d = 0; d < NPEER; ++d) peers.p[d][i] = v;
+  }
+  __threadfence_system();  // peer stores ordered before the kernel's end
+}
+
+template <typename W>
+void launch_push(const void* src, void* const* peers, int num_peers, int64_t n, cudaStream_t s) {
+  PushPeers<W> pp{};
+  for (int d = 0; d < num_peers; ++d) pp.p[d] = static_cast<W*>(peers[d]);
+  int64_t blocks = ceil_div(n, 256 * kPushUnroll);
+  if (blocks > 148 * 4) blocks = 148 * 4;
+  if (blocks < 1) blocks = 1;
+  const auto* in = static_cast<const W*>(src);
+  const unsigned g = static_cast<unsigned>(blocks);
+  switch (num_peers) {
+    case 1: push_kernel<W, 1><<<g, 256, 0, s>>>(in, pp, n); break;
+    case 2: push_kernel<W, 2><<<g, 256, 0, s>>>(in, pp, n); break;
+    case 3: push_kernel<W, 3><<<g, 256, 0, s>>>(in, pp, n); break;
+    case 4: push_kernel<W, 4><<<g, 256, 0, s>>>(in, pp, n); break;
+    case 5: push_kernel<W, 5><<<g, 256, 0, s>>>(in, pp, n); break;
+    case 6: push_kernel<W, 6><<<g, 256, 0, s>>>(in, pp, n); break;
+    case 7: push_kernel<W, 7><<<g, 256, 0, s>>>(in, pp, n); break;
+    default: break;
+  }
+}
+
+}  // namespace
+
+void push_to_peers(const void* src, void* const* peers, int num_peers, size_t bytes,
+                   cudaStream_t s) {
+  if (num_peers <= 0 || bytes == 0) return;
+  bool vec = bytes % 16 == 0 && aligned_to(src, 16);
+  for (int d = 0; d < num_peers; ++d) vec = vec && aligned_to(peers[d], 16);
+  if (vec) {
+    launch_push<uint4>(src, peers, num_peers, static_cast<int64_t>(bytes / 16), s);
+  } else {
+    launch_push<uint32_t>(src, peers, num_peers, static_cast<int64_t>(bytes / 4), s);
+  }
+}
+
+}  // namespace mb
 
 using namespace mb;
 

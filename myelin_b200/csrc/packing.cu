@@ -11,6 +11,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "exchange.cuh"
 
 namespace mb {
 
@@ -694,14 +695,12 @@ extern "C" int mb_pack_count_scatter(int dtype, const void* spikes, int32_t* wor
     for (int d = 0; d < num_peers; ++d) slots.p[d] = static_cast<uint32_t*>(peers[d]);
     launch_pack_count_u8(spikes, words, slots, num_peers, rows, n, counts64, counts32, s);
   } else {
-    // other shapes: pack + count into `words`, then one copy per peer slot
-    // (over NVLink)
+    // other shapes: pack + count into `words`, then one kernel stores them
+    // into every peer slot (over NVLink)
     MB_DISPATCH_DTYPE(dtype, launch_pack_count, spikes, words, rows, n, counts64, counts32,
                       workspace, s);
-    const size_t bytes = size_t(rows) * size_t(ceil_div(n, 32)) * sizeof(int32_t);
-    for (int d = 0; d < num_peers; ++d) {
-      cudaMemcpyAsync(peers[d], words, bytes, cudaMemcpyDefault, s);
-    }
+    push_to_peers(words, peers, num_peers,
+                  size_t(rows) * size_t(ceil_div(n, 32)) * sizeof(int32_t), s);
   }
   MB_CHECK_LAUNCH("mb_pack_count_scatter");
   return 0;

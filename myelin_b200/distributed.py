@@ -258,12 +258,12 @@ class PackedSpikeExchange:
         """``kernels.lif_forward_packed_spikes`` feeding the all-gather directly.
 
         The scan writes its packed words straight into this rank's slot of
-        its own gather buffer and the copy engines move that slot into every
-        peer's buffer over NVLink (src/myelin/kernels.py:96-156 followed by
+        its own gather buffer and a push kernel stores that slot into every
+        peer's buffer over NVLink, all peers at once (src/myelin/kernels.py:96-156 followed by
         distributed.py:63-80, with no staging buffer and no NCCL all-gather).
         Returns the final ``LIFState`` and the gathered words ``[world, T, B,
         ceil(N/32)]``, which equal ``packed_spike_all_gather_into_tensor`` of
-        every rank's packed output. A one-word all-reduce after the copies
+        every rank's packed output. A one-word all-reduce after the push
         completes the step (the same ordering argument as
         ``pack_count_all_gather``).
         """
