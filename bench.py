@@ -552,7 +552,8 @@ def run_izhikevich(args, world, rank, local) -> None:
                    "B_per_gpu": BATCH, "N": NEURONS,
                    "l2": "x and spikes are 537 MB each (larger than L2), no flush"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None},
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "traffic": profile_traffic("scan_fwd_izhikevich_fp32")},
         "spike_rate": float(spikes.mean()),
         "gpu_launches": args.steps, "device_status": nat.device_status(clear=True),
     }
@@ -628,7 +629,8 @@ def run_lif_packed(args, world, rank, local) -> None:
                                  "NCCL all_gather_into_tensor" if world > 1 else None),
                    "l2": "x is 537 MB (larger than L2), no flush"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None,
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "traffic": profile_traffic("scan_fwd_lif_packed_fp32") if world == 1 else None,
                      "note": "scan bytes over the whole step (all-gather included at N > 1)"},
         "words_checksum": int(words.sum().item()),
         "gpu_launches": args.steps, "device_status": nat.device_status(clear=True),
@@ -715,7 +717,8 @@ def run_pack_count(args, world, rank, local) -> None:
                                 if world > 1 else None),
         "roofline": {"bound": "hbm", "achieved": round(algo / (ms / 1e3) / 1e9, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(algo / (ms / 1e3) / 1e9 / peak, 4),
-                     "peak_kind": peak_kind, "traffic": None,
+                     "peak_kind": peak_kind,
+                     "traffic": profile_traffic("pack_count_u8_config4") if world == 1 else None,
                      "note": "fused pack+count bytes over the whole step (collectives included)"},
         "spike_count_check": total,
         "gpu_launches": 2 * args.steps, "device_status": nat.device_status(clear=True),
