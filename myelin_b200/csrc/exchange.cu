@@ -4,7 +4,7 @@
 // mb_ipc_alloc, the handles travel between processes on the host (any
 // channel: torch.distributed in the Python layer), and each process maps the
 // others' buffers with mb_ipc_open. Plain peer-to-peer memory over
-// NVLink / NVSwitch: no multicast object is created.
+// NVLink / NVSwitch: no switch-replicated (NVLS) mapping is created.
 #include <cstring>
 
 #include "common.cuh"

@@ -165,7 +165,7 @@ class PackedSpikeExchange:
     The count all-reduce is also the completion barrier: a rank's all-reduce
     finishes only after every rank has entered it, i.e. after every rank's
     packing kernel (and all its peer stores) has finished. Gather buffers are
-    allocated once per object (CUDA IPC, plain peer memory, no multicast) and
+    allocated once per object (CUDA IPC, plain peer-to-peer memory, no switch-replicated mapping) and
     used alternately, so reads of a returned buffer that the caller enqueues
     on the current stream before its next call are ordered before any rank
     overwrites it (a rank writes that buffer again only after the next call's
