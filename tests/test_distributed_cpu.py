@@ -19,6 +19,7 @@ import torch
 import torch.distributed as torch_dist
 
 import myelin_b200.distributed as mbd
+import myelin_b200.neurons as mbd_neurons
 from myelin_b200.packing import PackedSpikes, _normalize_count_dims
 
 
@@ -221,6 +222,11 @@ class _FakeIpc:
         out = c64 if c64 is not None else c32
         out.copy_((spikes.reshape(rows, n) != 0).sum(0).to(out.dtype))
 
+    def scan_forward_packed_scatter(self, *, x, v0, vT, packed, peers, decay, threshold,
+                                    reset_mode, **_):
+        self.calls.append(("scan", packed, tuple(peers), decay, threshold, reset_mode))
+        vT.copy_(v0)
+
     def ipc_close(self, address):
         self.calls.append(("close", address))
 
@@ -255,6 +261,20 @@ def _exchange_worker(rank: int, world: int, init: str, queue) -> None:
         expect = [sum((torch.rand(shape, generator=torch.Generator().manual_seed(10 * s + r)) < 0.3)
                       .sum((0, 1)).to(torch.int64) for r in range(world)) for s in range(3)]
         ok = ok and all(torch.equal(a, b) for a, b in zip(totals, expect))
+        # the packed scan path shares the buffer rotation (step 3 uses buffer 1)
+        # and completes with a one-word all-reduce that every rank joins
+        params = mbd_neurons.LIFParams(tau_mem=4.0)
+        x = torch.zeros(shape)
+        v0 = torch.full(shape[1:], 0.5)
+        vT = ex._scan_scatter(x, v0, params, 1, 0)
+        scan = [c for c in fake.calls if c[0] == "scan"][-1]
+        ok = ok and scan[1:3] == expected_slots(1) and scan[3] == params.decay and scan[5] == 1
+        ok = ok and torch.equal(vT, v0)
+        try:
+            ex._scan_scatter(torch.zeros((4, 3, 71)), v0, params, 0, 0)
+            ok = False  # a shape other than the exchange's must be refused
+        except ValueError:
+            pass
         ex.close()
         kinds = [c[0] for c in fake.calls]
         # peers' mappings are closed before this rank's buffers are freed
