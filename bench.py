@@ -12,11 +12,17 @@ packed words + per-neuron int32 counts), ``mlp_fp32`` (config 2: one training
 step of the 784 -> 1024 -> 10 stream-synapse LIF MLP, fp32) and ``rate_net``
 (config 5: one training step of 4 x 4096 hidden stream-synapse LIF layers and
 a 4096 -> 10 rate readout, bf16, T=100, B=512 per GPU, with the gradient
-all-reduce across ranks).
+all-reduce across ranks), ``izhikevich_fp32`` (Izhikevich forward at the
+north-star shape) and ``lif_packed`` (LIF forward with packed words only at
+the north-star shape, plus the packed all-gather at N > 1).
 
-Multi-GPU (torchrun, one process per GPU): every rank runs its own batch shard
-of the same size (weak scaling, no collective on the data path); the value is
-all ranks' neuron-steps divided by the max-over-ranks device time.
+Multi-GPU (torchrun, one process per GPU): the scan workloads run one batch
+shard of the same size per rank (weak scaling, no collective on the data
+path); ``pack_count`` splits config 4's batch of 1024 over the ranks (strong
+scaling) and all-gathers the packed words and all-reduces the counts, through
+the peer-mapped exchange by default (``--allgather fused``) or NCCL
+(``--allgather nccl``). The value is all ranks' units divided by the
+max-over-ranks device time.
 
 ``--impl reference`` times the reference algorithm's CPU restatement (the
 oracle, all host threads) on a bounded sample of the same workload.
@@ -721,7 +727,8 @@ def run_pack_count(args, world, rank, local) -> None:
                      "traffic": profile_traffic("pack_count_u8_config4") if world == 1 else None,
                      "note": "fused pack+count bytes over the whole step (collectives included)"},
         "spike_count_check": total,
-        "gpu_launches": 2 * args.steps, "device_status": nat.device_status(clear=True),
+        # one packing kernel per step (the totals are zeroed by a memset)
+        "gpu_launches": args.steps, "device_status": nat.device_status(clear=True),
     }
     clk = clocks.summary()
     if clk is not None:
