@@ -83,12 +83,24 @@ const char* mb_last_error(void);
 /* Library version string. */
 const char* mb_version(void);
 
-/* Device status of the scan kernels on the current device: 0 = ok, 1 = a
- * bounded wait for an asynchronous copy ran out (the kernel stopped early and
- * its outputs are incomplete). Synchronises the device. `clear` != 0 resets
- * the status to 0 after reading it. Returns -1 if the status can't be read.
+/* Device status of every kernel with bounded waits (scan forward/backward, both
+ * tensor-core GEMMs) on the current device: 0 = ok, 1 = a bounded wait for an
+ * asynchronous copy or an MMA ran out (the kernel stopped early and its
+ * outputs are incomplete). Synchronises the device. `clear` != 0 resets the
+ * status to 0 after reading it. Returns -1 if the status can't be read.
  * No reference counterpart (the reference's Triton kernels never wait). */
 int mb_device_status(int clear);
+
+/* Code units whose status words mb_device_status combines. */
+enum mb_unit { MB_UNIT_SCAN = 0, MB_UNIT_SCAN_FAST = 1, MB_UNIT_GEMM = 2 };
+
+/* Diagnostic: launch one tiny kernel in `unit` whose single bounded wait
+ * (budget `polls`, 1..65536) is on a barrier nothing arrives at, so it runs
+ * out the way a stalled copy would: the kernel records status 1 (visible
+ * through mb_device_status) and returns. It touches no memory but the status
+ * word. Used by tests to show that a timeout is reported; no reference
+ * counterpart. */
+int mb_debug_wait_timeout(int unit, int polls, void* stream);
 
 /* Number of chunk checkpoints for T steps: ceil(T / MB_SCAN_CHUNK). */
 int64_t mb_scan_num_checkpoints(int64_t T);

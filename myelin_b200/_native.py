@@ -51,6 +51,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mb_last_error": (ctypes.c_char_p, []),
     "mb_version": (ctypes.c_char_p, []),
     "mb_device_status": (_int, [_int]),
+    "mb_debug_wait_timeout": (_int, [_int, _int, _vp]),
     "mb_scan_num_checkpoints": (_i64, [_i64]),
     "mb_scan_forward": (
         _int,
@@ -149,9 +150,25 @@ def require_cuda(tensor: torch.Tensor, what: str = "inputs") -> None:
 
 
 def device_status(clear: bool = True) -> int:
-    """Return (and by default clear) the scan kernels' device status word."""
+    """Return (and by default clear) the device status of every kernel with
+    bounded waits (scan forward/backward, both tensor-core GEMMs)."""
 
     return int(lib().mb_device_status(1 if clear else 0))
+
+
+# enum mb_unit: the code units whose status words mb_device_status combines
+MB_UNIT_SCAN, MB_UNIT_SCAN_FAST, MB_UNIT_GEMM = 0, 1, 2
+
+
+def debug_wait_timeout(unit: int, polls: int = 256, device: torch.device | None = None) -> None:
+    """Launch a kernel in ``unit`` whose one bounded wait is on a barrier that
+    nothing arrives at: the wait runs out, the unit records status 1 and the
+    kernel returns (diagnostic for tests of the timeout path)."""
+
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    with torch.cuda.device(device):
+        status = lib().mb_debug_wait_timeout(unit, polls, stream_handle(device))
+    check(status, "mb_debug_wait_timeout")
 
 
 def scan_forward(

@@ -9,9 +9,22 @@
 namespace mb {
 
 // Device status word of this translation unit: 0 = ok. Set (first error
-// wins) by kernels whose bounded waits ran out; read and cleared by the host
-// through mb_device_status().
+// wins) by kernels whose bounded waits ran out. The library is built without
+// relocatable device code, so every .cu file that includes this header has
+// its own copy of the word; each such file defines one host accessor (below)
+// and mb_device_status() combines all of them.
 static __device__ int g_device_status = 0;
+
+// Host accessors, one per translation unit that includes this header: read
+// (and with `clear`, reset) that unit's status word; -1 if it can't be read.
+int scan_unit_status(bool clear);       // scan.cu
+int scan_fast_unit_status(bool clear);  // scan_fast.cu
+int gemm_unit_status(bool clear);       // gemm_tcgen05.cu
+
+// Launchers of each unit's wait-timeout probe (wait_timeout_probe_kernel).
+cudaError_t scan_unit_wait_probe(uint32_t polls, cudaStream_t stream);
+cudaError_t scan_fast_unit_wait_probe(uint32_t polls, cudaStream_t stream);
+cudaError_t gemm_unit_wait_probe(uint32_t polls, cudaStream_t stream);
 
 enum DeviceStatus : int {
   kStatusOk = 0,
@@ -107,13 +120,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // copy is tens of kilobytes.
 constexpr uint32_t kMaxWaitPolls = 1u << 22;
 
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kMaxWaitPolls; ++i) {
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  uint32_t max_polls = kMaxWaitPolls) {
+  for (uint32_t i = 0; i < max_polls; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
   }
   record_status(kStatusWaitTimeout);
   return false;
 }
+
+namespace {
+
+// Diagnostic: one thread waits, with a poll budget of `polls`, for phase 0 of
+// a freshly initialised barrier that nothing ever arrives at, so the wait runs
+// out through the same path as the kernels' own waits (the unit's status word
+// becomes kStatusWaitTimeout) and the kernel returns. Nothing faults and
+// nothing spins without bound.
+__global__ void wait_timeout_probe_kernel(uint32_t polls) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+    mbar_wait_bounded(&bar, 0, polls);
+  }
+}
+
+}  // namespace
 
 // Host side: read (and optionally clear) this translation unit's status word.
 // Synchronises with the device.

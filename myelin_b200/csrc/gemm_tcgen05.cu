@@ -390,10 +390,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_2d(sb + s * L::kBBytes, &tma_b, kb * kBK, tn * BN, &full[s]);
         }
       }
-      // every issued copy has landed before the CTA can retire
+      // every issued copy has landed before the CTA can retire; a wait that
+      // runs out is already recorded in the status word, and the remaining
+      // waits still run (each bounded) so that no copy is left in flight
       const uint32_t issued = it;
       for (uint32_t j = issued > kStages ? issued - kStages : 0; j < issued; ++j) {
-        mbar_wait_bounded(&full[j % kStages], (j / kStages) & 1);
+        (void)mbar_wait_bounded(&full[j % kStages], (j / kStages) & 1);
       }
     }
   } else if (warp == 1) {
@@ -425,9 +427,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (ok) mma_commit(&acc_full[b]);  // the tile's accumulator is complete
       }
-      // all issued MMAs have finished before TMEM is released
+      // all issued MMAs have finished before TMEM is released (a timeout is
+      // recorded in the status word; the exit path is the same either way)
       mma_commit(drained);
-      mbar_wait_bounded(drained, 0);
+      (void)mbar_wait_bounded(drained, 0);
     }
   } else {
     const int quarter = warp & 3;  // TMEM lanes this warp may access
@@ -632,9 +635,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
       if (leader) {
         // both CTAs' copies complete on the leader's barriers: once the last
         // phases have completed nothing is in flight into either CTA
+        // (a wait that runs out is recorded; the rest still run, each bounded)
         const uint32_t issued = it;
         for (uint32_t j = issued > k2Stages ? issued - k2Stages : 0; j < issued; ++j) {
-          mbar_wait_bounded(&full[j % k2Stages], (j / k2Stages) & 1);
+          (void)mbar_wait_bounded(&full[j % k2Stages], (j / k2Stages) & 1);
         }
       }
     }
@@ -673,7 +677,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
         }
       }
       mma_commit_pair(cluster_addr(smem_addr(drained), 0));
-      mbar_wait_bounded(drained, 0);  // all MMAs done before TMEM is released
+      // all MMAs done before TMEM is released (a timeout is recorded in the
+      // status word; the exit path is the same either way)
+      (void)mbar_wait_bounded(drained, 0);
     }
   } else {
     const int quarter = warp & 3;      // TMEM lanes this warp may access (warp id % 4)
@@ -868,3 +874,14 @@ extern "C" int mb_gemm_tn(int in_dtype, const void* A, int64_t lda, const void* 
   MB_CHECK_LAUNCH("mb_gemm_tn");
   return 0;
 }
+
+namespace mb {
+
+int gemm_unit_status(bool clear) { return read_device_status(clear); }
+
+cudaError_t gemm_unit_wait_probe(uint32_t polls, cudaStream_t stream) {
+  wait_timeout_probe_kernel<<<1, 32, 0, stream>>>(polls);
+  return cudaGetLastError();
+}
+
+}  // namespace mb

@@ -768,6 +768,14 @@ extern "C" int mb_count_columns_noalloc(const int32_t* words, int64_t rows, int6
                "mb_count_columns_noalloc: packed.original_shape must have non-empty last dimension");
   MB_CHECK_ARG(counts64 != nullptr || counts32 != nullptr, "mb_count_columns_noalloc: no output");
   MB_CHECK_ARG(rows == 0 || words != nullptr, "mb_count_columns_noalloc: null words");
+  MB_CHECK_ARG(aligned_to(counts64, 8) && aligned_to(counts32, 4),
+               "mb_count_columns_noalloc: counts misaligned");
+  // every row slice holds n partial sums of 4 bytes: reject an n whose single
+  // slice already exceeds the scratch before the size product can overflow
+  MB_CHECK_ARG(rows == 0 || n <= kNoAllocScratchBytes / 4,
+               "mb_count_columns_noalloc: n = %lld needs more scratch than the built-in %lld "
+               "bytes; use mb_count_columns with a caller-provided workspace",
+               (long long)n, (long long)kNoAllocScratchBytes);
   const int64_t need = count_columns_workspace_bytes(rows, n);
   MB_CHECK_ARG(need <= kNoAllocScratchBytes,
                "mb_count_columns_noalloc: this shape needs %lld bytes of scratch, more than the "

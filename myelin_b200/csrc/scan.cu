@@ -649,4 +649,13 @@ extern "C" int mb_scan_backward(int neuron, int dtype, const void* x, const floa
   return 0;
 }
 
-extern "C" int mb_device_status(int clear) { return read_device_status(clear != 0); }
+namespace mb {
+
+int scan_unit_status(bool clear) { return read_device_status(clear); }
+
+cudaError_t scan_unit_wait_probe(uint32_t polls, cudaStream_t stream) {
+  wait_timeout_probe_kernel<<<1, 32, 0, stream>>>(polls);
+  return cudaGetLastError();
+}
+
+}  // namespace mb

@@ -666,4 +666,11 @@ bool launch_scan_bwd_fast(int dtype, int neuron, int reset_mode, int surrogate,
   return true;
 }
 
+int scan_fast_unit_status(bool clear) { return read_device_status(clear); }
+
+cudaError_t scan_fast_unit_wait_probe(uint32_t polls, cudaStream_t stream) {
+  wait_timeout_probe_kernel<<<1, 32, 0, stream>>>(polls);
+  return cudaGetLastError();
+}
+
 }  // namespace mb

@@ -341,6 +341,13 @@ class PackedSpikeExchange:
 
         if not self._own:
             return
+        # kernels still queued on this device may be storing into the peer
+        # mappings: let them finish before the mappings go away
+        sync = getattr(self._nat, "device_synchronize", None)
+        if sync is not None:
+            sync(self.device)
+        else:
+            torch.cuda.synchronize(self.device)
         for address in self._opened:
             self._nat.ipc_close(address)
         self._opened = []

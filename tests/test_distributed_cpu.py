@@ -227,6 +227,9 @@ class _FakeIpc:
         self.calls.append(("scan", packed, tuple(peers), decay, threshold, reset_mode))
         vT.copy_(v0)
 
+    def device_synchronize(self, device):
+        self.calls.append(("sync",))
+
     def ipc_close(self, address):
         self.calls.append(("close", address))
 
@@ -280,6 +283,8 @@ def _exchange_worker(rank: int, world: int, init: str, queue) -> None:
         # peers' mappings are closed before this rank's buffers are freed
         ok = ok and kinds.count("close") == 2 * (world - 1) and kinds.count("free") == 2
         ok = ok and max(i for i, k in enumerate(kinds) if k == "close") < kinds.index("free")
+        # the device is synchronised before any peer mapping goes away
+        ok = ok and "sync" in kinds and kinds.index("sync") < kinds.index("close")
         queue.put((rank, bool(ok), ""))
     except Exception as exc:  # pragma: no cover - reported through the queue
         queue.put((rank, False, f"{type(exc).__name__}: {exc}"))

@@ -53,6 +53,9 @@ def _count_noalloc(words, rows, n):
     [
         [((128, 128, 8192), 0.05, 1), ((64, 96, 8192), 0.3, 2)],  # config-4 shard, then a denser one
         [((7, 3, 45), 0.4, 3), ((300, 5, 70), 0.1, 4)],            # ragged widths, many rows
+        # 74 row slices, then 2: the second call must not read the partial
+        # sums the first call left in slices 2..73
+        [((128, 128, 8192), 0.05, 5), ((2, 64, 8192), 0.2, 6)],
     ],
 )
 def test_noalloc_counts_match_workspace_counts_on_consecutive_calls(shapes):
