@@ -17,7 +17,14 @@ the reference. Cases:
   ``surrogate_alif_unroll`` (functional.py:115-189) for every surrogate;
 - alif_subtract_atan.npz: the same for the subtractive-reset extension, from a
   torch restatement of ``surrogate_alif_unroll`` with ``m = p - theta * s``
-  (no reference counterpart: parity of this case is unpinned);
+  (the gradient of this case has no reference counterpart and stays unpinned);
+- alif_subtract_dsl_*.npz: the subtractive-reset ALIF forward evaluated by the
+  reference's own custom-neuron oracle, ``dsl.evaluate_neuron_unroll``
+  (src/myelin/dsl.py:457-511), on an ALIF ``NeuronIR`` built like ``alif_ir``
+  (dsl.py:1064-1089) whose membrane update is
+  ``where(spike, pre_reset - adaptive_threshold, pre_reset)``: spikes (packed
+  words) and final membrane / adaptation. Case ``b`` uses bf16-representable
+  inputs and states so the bf16-I/O kernel can be checked against it too;
 - linear_stream.npz / linear_checkpoint_rate.npz: the torch autograd functions
   ``LinearSurrogateLIFStreamFunction`` / ``LinearSurrogateLIFCheckpointRateFunction``
   (src/myelin/autograd.py:445-885);
@@ -214,6 +221,65 @@ def surrogate_cases() -> None:
     )
 
 
+def alif_subtract_ir():
+    """ALIF NeuronIR with subtractive reset, from the reference DSL's own
+    builders (dsl.py:1064-1089 shows the hard-reset original)."""
+
+    from myelin.dsl import NeuronIR, input_, param, state, where
+
+    membrane = state("membrane")
+    adaptation = state("adaptation")
+    current = input_("input_current")
+    decay = param("decay")
+    adaptation_decay = param("adaptation_decay")
+    threshold = param("threshold")
+    beta = param("beta")
+    pre_reset = membrane * decay + current
+    adaptive_threshold = threshold + beta * adaptation
+    spike = pre_reset.ge(adaptive_threshold)
+    spike_float = where(spike, 1.0, 0.0)
+    return NeuronIR(
+        name="alif_subtract",
+        state=("membrane", "adaptation"),
+        params=("decay", "adaptation_decay", "threshold", "beta"),
+        inputs=("input_current",),
+        next_state={
+            "membrane": where(spike, pre_reset - adaptive_threshold, pre_reset),
+            "adaptation": adaptation * adaptation_decay + spike_float,
+        },
+        outputs={"spike": spike_float},
+    )
+
+
+def alif_subtract_dsl_cases() -> None:
+    from myelin.dsl import evaluate_neuron_unroll
+    from myelin.neurons import ALIFParams
+
+    ir = alif_subtract_ir()
+    for name, (T, B, N), seed, bf16 in [
+        ("alif_subtract_dsl_a", (24, 3, 37), 600, False),
+        ("alif_subtract_dsl_b", (96, 4, 160), 601, True),  # T >= 64, bf16-representable
+    ]:
+        g = _gen(seed)
+        x = torch.randn((T, B, N), generator=g) * 0.6 + 0.2
+        v0 = torch.rand((B, N), generator=g) * 0.4
+        a0 = torch.rand((B, N), generator=g) * 0.3
+        if bf16:
+            x, v0, a0 = (t.to(torch.bfloat16).to(torch.float32) for t in (x, v0, a0))
+        p = dict(tau_mem=10.0, tau_adaptation=50.0, threshold=1.0, reset=0.0, beta=1.8)
+        params = ALIFParams(**p)
+        values = {"decay": params.decay, "adaptation_decay": params.adaptation_decay,
+                  "threshold": params.threshold, "beta": params.beta}
+        final, spikes = evaluate_neuron_unroll(
+            ir, x, {"membrane": v0, "adaptation": a0}, values)
+        np.savez_compressed(
+            OUT / f"{name}.npz", x=x.numpy(), v0=v0.numpy(), a0=a0.numpy(),
+            packed=_pack_np(spikes), vT=final["membrane"].numpy(),
+            aT=final["adaptation"].numpy(), spike_count=np.asarray(int(spikes.sum().item())),
+            **p,
+        )
+
+
 def linear_cases() -> None:
     from myelin.autograd import (
         linear_surrogate_lif_checkpoint_rate_function,
@@ -307,7 +373,8 @@ def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--reference-src", required=True, help="path to the reference's src/")
     cases = {"lif": lif_forward_cases, "surrogate": surrogate_cases, "linear": linear_cases,
-             "packing": packing_cases, "c1": c1_checksum, "izhikevich": izhikevich_cases}
+             "packing": packing_cases, "c1": c1_checksum, "izhikevich": izhikevich_cases,
+             "subtract_dsl": alif_subtract_dsl_cases}
     parser.add_argument("--cases", nargs="*", choices=sorted(cases), default=sorted(cases),
                         help="which fixture groups to (re)write (default: all)")
     args = parser.parse_args()

@@ -50,6 +50,25 @@ def test_alif_forward_bit_exact(oracle, name):
     assert np.array_equal(out["aT"], g["aT"])
 
 
+@pytest.mark.parametrize("name", ["alif_subtract_dsl_a", "alif_subtract_dsl_b"])
+def test_alif_subtract_forward_bit_exact_with_reference_dsl(oracle, name):
+    """The subtractive-reset forward (the headline workload's reset rule)
+    against the reference's own custom-neuron evaluator
+    (src/myelin/dsl.py:457-511) on an ALIF IR with
+    ``where(spike, pre_reset - adaptive_threshold, pre_reset)``."""
+
+    g = load_golden(name)
+    out = oracle.scan_forward(
+        g["x"], g["v0"], g["a0"], neuron=oracle.ALIF, reset_mode=oracle.SUBTRACT,
+        decay=lif_decay(g["tau_mem"]), threshold=f32(g["threshold"]), reset=f32(g["reset"]),
+        adapt_decay=lif_decay(g["tau_adaptation"]), beta=f32(g["beta"]),
+    )
+    assert int(out["spikes"].sum()) == int(g["spike_count"]) > 0
+    assert np.array_equal(oracle.pack(out["spikes"]), g["packed"])
+    assert np.array_equal(out["vT"], g["vT"])
+    assert np.array_equal(out["aT"], g["aT"])
+
+
 @pytest.mark.parametrize("surrogate", SURROGATES)
 @pytest.mark.parametrize("chunk", [1, 5, 16])
 def test_surrogate_lif_backward_matches_reference_autograd(oracle, surrogate, chunk):

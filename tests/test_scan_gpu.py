@@ -70,6 +70,40 @@ def test_alif_forward_matches_reference_golden(oracle, name):
     assert np.array_equal(host(state.adaptation), g["aT"])
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("name", ["alif_subtract_dsl_a", "alif_subtract_dsl_b"])
+def test_alif_subtract_forward_matches_reference_dsl(oracle, name, dtype):
+    """Subtractive reset (the headline workload's reset rule) against the
+    reference's own custom-neuron evaluator (src/myelin/dsl.py:457-511) on an
+    ALIF IR with ``where(spike, pre_reset - adaptive_threshold, pre_reset)``.
+    Spikes bit-exact; final states bit-exact in fp32 and equal to the rounded
+    fp32 result in bf16 (fp32 carry). Case ``b`` (T=96) holds bf16-representable
+    inputs; case ``a`` runs in fp32 only."""
+
+    g = load_golden(name)
+    if dtype == torch.bfloat16 and not name.endswith("_b"):
+        pytest.skip("inputs of this case are not bf16-representable")
+    params = mb.ALIFParams(tau_mem=float(g["tau_mem"]), tau_adaptation=float(g["tau_adaptation"]),
+                           threshold=float(g["threshold"]), reset=float(g["reset"]),
+                           beta=float(g["beta"]))
+    n = g["x"].shape[-1]
+    state0 = mb.ALIFState(dev(g["v0"], dtype), dev(g["a0"], dtype))
+    runs = {
+        "alif_forward": lambda: mb.alif_forward(dev(g["x"], dtype), state0, params,
+                                                reset_mode="subtract"),
+        "surrogate_alif_forward": lambda: mb.surrogate_alif_forward(
+            dev(g["x"], dtype), state0, params, surrogate="atan", checkpoint_size="memory",
+            reset_mode="subtract"),
+    }
+    for what, run in runs.items():
+        state, spikes = run()
+        assert np.array_equal(host(spikes).astype(np.uint8), oracle.unpack(g["packed"], n)), what
+        want_v = torch.from_numpy(g["vT"]).to(dtype).float().numpy()
+        want_a = torch.from_numpy(g["aT"]).to(dtype).float().numpy()
+        assert np.array_equal(host(state.membrane), want_v), what
+        assert np.array_equal(host(state.adaptation), want_a), what
+
+
 @pytest.mark.parametrize("surrogate", SURROGATES)
 def test_surrogate_lif_gradients_match_reference_golden(oracle, surrogate):
     g = load_golden(f"surrogate_lif_{surrogate}")
