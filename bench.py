@@ -22,10 +22,17 @@ path); ``pack_count`` splits config 4's batch of 1024 over the ranks (strong
 scaling) and all-gathers the packed words and all-reduces the counts, through
 the peer-mapped exchange by default (``--allgather fused``) or NCCL
 (``--allgather nccl``). The value is all ranks' units divided by the
-max-over-ranks device time.
+max-over-ranks device time. At N > 1 the default run also times BASELINE
+config 4's packed reductions on the same ranks (the ``collective`` key: the
+fused peer-store exchange and pack + NCCL, each with an in-run bit-exact
+parity check against every rank's regenerated shard).
 
-``--impl reference`` times the reference algorithm's CPU restatement (the
-oracle, all host threads) on a bounded sample of the same workload.
+CPU figures: ``--impl reference`` (and the GPU arm's ``cpu_baseline`` at N = 1)
+time myelin's own CPU implementation of the path, its torch per-timestep loop
++ autograd (restated in ``oracle/torch_path.py``), at the full config-3 step
+on all host threads, next to the C restatement of the same scan
+(``oracle/scan_oracle.c``, OpenMP) on a 32-row sample, both by the same
+per-step timing method.
 """
 
 from __future__ import annotations
@@ -271,6 +278,7 @@ def run_gpu(args) -> None:
     ms_per_step = total_ms / args.steps
     value = units * world / (ms_per_step / 1e3)
     status = nat.device_status(clear=True)
+    graph = graph_replay_diagnostic(forward, x, gs, stream, args.steps, world)
 
     # end to end through the public API with host buffers
     pinned_x = x.detach().cpu().pin_memory()
@@ -348,6 +356,7 @@ def run_gpu(args) -> None:
                 "ms_per_step": e2e_ms},
         "gpu_launches": 2 * args.steps,
         "device_status": status,
+        "graph_replay": graph,
     }
     clk = clocks.summary()
     if clk is not None:
@@ -357,10 +366,164 @@ def run_gpu(args) -> None:
     if world > 1:
         import torch.distributed as dist
 
+        # the packed reductions on the same ranks, after the
+        # scan's own numbers are final: every rank takes part
+        result["collective"] = collective_leg(world, rank, local, args.steps, args.warmup)
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(result), flush=True)
+
+
+def graph_replay_diagnostic(forward, x, gs, stream, steps: int, world: int) -> dict:
+    """The same forward + backward captured as two CUDA graphs and replayed,
+    with events between the replays: the kernels' device time without the
+    host's per-launch work (Python, autograd) in between. A gap between this
+    and the eager step says how much of the eager time is the host's."""
+
+    side = torch.cuda.Stream()
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            spikes = forward(x)
+            torch.autograd.grad(spikes, x, gs)
+    stream.wait_stream(side)
+    torch.cuda.synchronize()
+    g_fwd, g_bwd = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_fwd):
+        spikes_g = forward(x)
+    with torch.cuda.graph(g_bwd, pool=g_fwd.pool()):
+        torch.autograd.grad(spikes_g, x, gs)
+    for _ in range(3):
+        g_fwd.replay()
+        g_bwd.replay()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    for e0, e1, e2 in ev:
+        e0.record(stream)
+        g_fwd.replay()
+        e1.record(stream)
+        g_bwd.replay()
+        e2.record(stream)
+    torch.cuda.synchronize()
+    total = max_over_ranks(ev[0][0].elapsed_time(ev[-1][2]), world) / steps
+    fwd = statistics.mean(a.elapsed_time(b) for a, b, _ in ev)
+    bwd = statistics.mean(b.elapsed_time(c) for _, b, c in ev)
+    del g_fwd, g_bwd
+    return {"ms_per_step": round(total, 4), "fwd_launch_ms": round(fwd, 4),
+            "bwd_launch_ms": round(bwd, 4),
+            "note": "forward and backward each captured once in a CUDA graph and replayed "
+                    "(same kernels and buffers); diagnostic, not the headline"}
+
+
+PEER_GBS = 770.0  # measured NVLink peer-copy bandwidth per direction on this pool's B200s
+
+
+def collective_leg(world: int, rank: int, local: int, steps: int, warmup: int) -> dict:
+    """BASELINE config 4's packed reductions on ``world`` ranks, with a parity check.
+
+    Spikes: Bernoulli(0.05) bool [T=128, B=1024, N=8192], the batch split over
+    the ranks (rank r holds rows r*B/w .. (r+1)*B/w, seeded 77 + r). A step
+    packs this rank's shard into int32 words, counts spikes per neuron over T
+    and the local batch, all-gathers every rank's words and all-reduces the
+    counts (src/myelin/distributed.py:63-109). Timed two ways on the same
+    shards: ``fused`` (PackedSpikeExchange: one kernel packs, counts and
+    stores every word into each rank's gather buffer over NVLink, then an
+    int32 NCCL all-reduce) and ``nccl`` (pack + count kernel, NCCL
+    all_gather_into_tensor, NCCL all-reduce). CUDA events on the launching
+    stream, max over ranks.
+
+    Parity (bit-exact, checked inside this run after each timing): every rank
+    regenerates every rank's seeded shard, packs it with ``pack_spikes`` and
+    compares the words with that rank's slot of the gathered buffer, and
+    compares the all-reduced counts with the per-neuron sum of all shards'
+    spikes (torch, int64). A MIN all-reduce of the per-rank results gives one
+    verdict for the job.
+    """
+
+    import torch.distributed as dist
+
+    import myelin_b200 as mb
+
+    T, B_TOTAL, N = 128, 1024, 8192
+    B = B_TOTAL // world
+    stream = torch.cuda.current_stream()
+
+    def shard(r: int) -> torch.Tensor:
+        gen = torch.Generator(device="cuda").manual_seed(77 + r)
+        return torch.rand((T, B, N), generator=gen, device="cuda") < 0.05
+
+    spikes = shard(rank)
+    exchange = mb.PackedSpikeExchange((T, B, N))
+    gather_buf = torch.empty((world, T, B, N // 32), dtype=torch.int32, device="cuda")
+
+    def fused_step():
+        return exchange.pack_count_all_gather(spikes, count_dtype=torch.int32)
+
+    def nccl_step():
+        packed, counts = mb.pack_spikes_with_counts(spikes, dtype=torch.int32)
+        mb.packed_spike_all_gather_into_tensor(packed, out=gather_buf)
+        dist.all_reduce(counts, op=dist.ReduceOp.SUM)
+        return gather_buf, counts
+
+    def timed(step_fn):
+        for _ in range(warmup):
+            step_fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(steps):
+            out = step_fn()
+        stop.record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        return max_over_ranks(start.elapsed_time(stop), world) / steps, out
+
+    def parity(gathered: torch.Tensor, counts: torch.Tensor) -> bool:
+        ok = tuple(gathered.shape) == (world, T, B, N // 32)
+        want_counts = torch.zeros(N, dtype=torch.int64, device="cuda")
+        for r in range(world):
+            s = shard(r)
+            ok = ok and torch.equal(mb.pack_spikes(s).data, gathered[r])
+            want_counts += s.sum(dim=(0, 1))
+            del s
+        ok = ok and torch.equal(counts.to(torch.int64), want_counts)
+        flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device="cuda")
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        return bool(flag.item())
+
+    words_bytes = T * B_TOTAL * (N // 32) * 4
+    received = words_bytes * (world - 1) / world  # per rank, whatever the path
+    bound_ms = received / (PEER_GBS * 1e9) * 1e3
+    units = T * B_TOTAL * N
+    out = {"workload": "pack_count (BASELINE config 4: Bernoulli(0.05) bool [128, 1024, 8192], "
+                       f"batch sharded over {world} ranks: [128, {B}, 8192] per rank)",
+           "spikes_per_step": units, "words_bytes_per_step": words_bytes,
+           "received_bytes_per_rank": int(received),
+           "receive_bound_ms": round(bound_ms, 4),
+           "receive_bound_note": f"(w-1)/w of the packed words reach every rank over NVLink; "
+                                 f"{PEER_GBS:.0f} GB/s measured peer bandwidth per direction"}
+    for name, step_fn in (("fused", fused_step), ("nccl", nccl_step)):
+        ms, (gathered, counts) = timed(step_fn)
+        out[name] = {
+            "ms_per_step": round(ms, 4),
+            "spikes_per_s": units / (ms / 1e3),
+            "allgather_busbw_gbs": round(received / (ms / 1e3) / 1e9, 1),
+            "vs_receive_bound": round(ms / bound_ms, 3),
+            "parity_ok": parity(gathered, counts),
+        }
+    out["parity_ok"] = out["fused"]["parity_ok"] and out["nccl"]["parity_ok"]
+    out["limit"] = ("the all-gather's receive side: every rank takes in "
+                    f"{received / 1e6:.0f} MB of other ranks' words per step while its own "
+                    f"packing work shrinks as 1/w; fused step = "
+                    f"{out['fused']['vs_receive_bound']}x the receive bound")
+    exchange.close()
+    return out
 
 
 def build_network(name: str, device: str, seed: int):
@@ -743,9 +906,13 @@ def run_pack_count(args, world, rank, local) -> None:
 
 
 # ---------------------------------------------------------------------------
-# CPU arms (oracle = CPU restatement of the reference algorithm)
+# CPU arms: myelin's torch CPU path (restated in oracle/torch_path.py) and the
+# C restatement of the same scan (oracle/scan_oracle.c), on the host's cores
 # ---------------------------------------------------------------------------
-def _oracle_sample(name: str, rows: int):
+C_PORT_ROWS = 32  # C-port sample: 32 of 128 rows, 134 MB per fp32 array (beyond the host LLC)
+
+
+def _oracle_sample(name: str, rows: int, threads: int):
     from oracle import oracle
 
     rng = np.random.default_rng(99)
@@ -766,44 +933,93 @@ def _oracle_sample(name: str, rows: int):
     z = np.zeros((rows, NEURONS), np.float32)
 
     def step():
-        oracle.scan_forward(x, z, z, **kw)
-        oracle.scan_backward(x, z, z, grad_spikes=gs, surrogate="atan", slope=10.0, **kw)
+        oracle.scan_forward(x, z, z, threads=threads, **kw)
+        oracle.scan_backward(x, z, z, grad_spikes=gs, surrogate="atan", slope=10.0,
+                             threads=threads, **kw)
 
-    return step, T_STEPS * rows * NEURONS, oracle.num_threads()
+    return step, T_STEPS * rows * NEURONS
+
+
+def _timed_steps(step, *, warmup: int, steps: int | None = None, seconds: float = 10.0,
+                 min_steps: int = 3) -> list[float]:
+    """Per-step wall times (perf_counter), after ``warmup`` untimed steps: exactly
+    ``steps`` if given, else until ``seconds`` have passed (at least ``min_steps``).
+    Both CPU arms use this one method, so their figures are comparable."""
+
+    for _ in range(warmup):
+        step()
+    times: list[float] = []
+    t_start = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+        if steps is not None and len(times) >= steps:
+            break
+        if steps is None and len(times) >= min_steps and time.perf_counter() - t_start >= seconds:
+            break
+    return times
+
+
+def c_port_figure(name: str, *, threads: int, warmup: int = 2, steps: int | None = None,
+                  seconds: float = 5.0) -> dict:
+    step, units = _oracle_sample(name, C_PORT_ROWS, threads)
+    times = _timed_steps(step, warmup=warmup, steps=steps, seconds=seconds)
+    med = statistics.median(times)
+    return {"value": units / med, "unit": "neuron-steps/s", "cores": threads, "kind": "port",
+            "sample": f"{name}: T={T_STEPS}, B={C_PORT_ROWS} of {BATCH}, N={NEURONS} "
+                      f"(134 MB per fp32 array, beyond the host's last-level cache); median of "
+                      f"{len(times)} fwd+bwd passes of the C restatement (OpenMP, {threads} "
+                      "threads)"}
+
+
+def torch_path_figure(*, threads: int, warmup: int = 1, steps: int | None = None,
+                      seconds: float = 10.0) -> dict:
+    from oracle import torch_path
+
+    r = torch_path.time_config3(threads=threads, warmup=warmup, steps=steps, seconds=seconds,
+                                min_steps=2)
+    med = statistics.median(r["times"])
+    T, B, N = r["shape"]
+    return {"value": r["units"] / med, "unit": "neuron-steps/s", "cores": r["threads"],
+            "kind": "port",
+            "sample": f"myelin's torch CPU path (surrogate_alif_unroll + autograd, restated in "
+                      f"torch): the full config-3 step T={T}, B={B}, N={N}, {r['dtype']}, "
+                      f"median of {len(r['times'])} fwd+bwd steps, torch on {r['threads']} "
+                      "host threads"}
 
 
 def cpu_baseline(name: str, seconds: float = 10.0) -> dict:
-    rows = 4
-    step, units, threads = _oracle_sample(name, rows)
-    step()  # warm
-    n, t0 = 0, time.perf_counter()
-    while time.perf_counter() - t0 < seconds:
-        step()
-        n += 1
-    elapsed = time.perf_counter() - t0
-    return {"value": units * n / elapsed, "unit": "neuron-steps/s", "cores": threads,
-            "kind": "port",
-            "sample": f"{name}: T={T_STEPS}, B={rows} of {BATCH}, N={NEURONS}; {n} fwd+bwd passes "
-                      f"in {elapsed:.1f} s (C restatement, OpenMP, {threads} threads)"}
+    threads = len(os.sched_getaffinity(0))
+    if name == "alif_bf16":
+        base = torch_path_figure(threads=threads, seconds=seconds)
+        base["c_port"] = c_port_figure(name, threads=threads, seconds=seconds / 2)
+        return base
+    return c_port_figure(name, threads=threads, seconds=seconds)
 
 
 def run_reference(args) -> None:
+    """The reference arm: myelin's own CPU implementation of the path (its
+    torch per-timestep loop + autograd, restated in oracle/torch_path.py; the
+    reference tree does not travel to the GPU box) on all of the host's
+    cores, at the GPU arm's config. Under torchrun rank 0 alone runs it (with
+    every host thread, whatever OMP_NUM_THREADS torchrun set) and the value
+    is whole-host throughput, comparable to the GPU arm's whole-job value."""
+
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    threads = len(os.sched_getaffinity(0))
     name = args.workload if args.workload in ("alif_bf16", "lif_fp32") else "alif_bf16"
-    rows = 4
-    step, units, threads = _oracle_sample(name, rows)
-    for _ in range(args.warmup):
-        step()
-    times = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        step()
-        times.append(time.perf_counter() - t0)
-    ms = 1e3 * sum(times) / len(times)
-    value = units / (ms / 1e3)
+    if name == "alif_bf16":
+        fig = torch_path_figure(threads=threads, warmup=min(args.warmup, 3), steps=args.steps)
+        fig["c_port"] = c_port_figure(name, threads=threads, seconds=5.0)
+    else:
+        fig = c_port_figure(name, threads=threads, warmup=args.warmup, steps=args.steps)
+    value = fig["value"]
+    ms = (T_STEPS * BATCH * NEURONS if name == "alif_bf16" else T_STEPS * C_PORT_ROWS * NEURONS) \
+        / value * 1e3
     result = {
         "impl": "reference",
         "metric": "LIF/ALIF fwd+bwd neuron-timesteps/s", "value": value, "unit": "neuron-steps/s",
@@ -811,11 +1027,8 @@ def run_reference(args) -> None:
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16" if name == "alif_bf16" else "f32", "data": "synthetic",
         "config": {"workload": name, "T": T_STEPS, "B_per_gpu": BATCH, "N": NEURONS,
-                   "sample_rows": rows},
-        "cpu_baseline": {"value": value, "unit": "neuron-steps/s", "cores": threads,
-                         "kind": "port",
-                         "sample": f"each step: T={T_STEPS}, B={rows} of {BATCH}, N={NEURONS}, "
-                                   "fwd+bwd of the C restatement (OpenMP, all host threads)"},
+                   "host_threads": threads},
+        "cpu_baseline": fig,
         "e2e": {"value": value, "unit": "neuron-steps/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }

@@ -208,6 +208,71 @@ int mb_gemm_tn(int in_dtype, const void* A, int64_t lda, const void* B, int64_t 
                const void* bias, int bias_dtype, int out_dtype, void* C, int64_t ldc, int64_t M,
                int64_t N, int64_t K, void* stream);
 
+/* Operand layouts of mb_gemm. K-major: element (r, k) at r * ld + k (rows of K
+ * contiguous elements). MN-major: element (r, k) at k * ld + r (K rows of M or
+ * N contiguous elements), e.g. x[T*B, F] read as the M-major A of x^T. */
+enum mb_major { MB_KMAJOR = 0, MB_MNMAJOR = 1 };
+
+/*
+ * General tensor-core GEMM (mb_gemm_tn is the K-major/K-major case):
+ *   C[M, N] = sum over (i, j) of A_i[M, K] * B_j[N, K]^T (+ bias[N])
+ * A_i / B_j: part i / j of A / B (`a_parts`, `b_parts` in 1..3, parts
+ * `*_part_stride` elements apart, multiples of 8), each K-major or MN-major
+ * (`a_major`, `b_major`; an M-major A needs an N-major B). The products kept
+ * are those with i + j <= 2: with an fp32 operand split into 3 bf16 parts
+ * (mb_split_bf16, part p holding the bits 8p below the leading ones) this is
+ * the fp32 product to within 2^-24 relative per term, computed on the 16-bit
+ * tensor cores with fp32 accumulation (bf16x6 for two split operands, x3 when
+ * one side is exact in one part, e.g. 0/1 spikes). `a_nonzero` / `b_nonzero`
+ * (device int per part, nullable, as written by mb_split_bf16) skip the
+ * products of an all-zero part on the device. Leading dimensions: multiples
+ * of 8; K-major also needs K % 8 == 0 and ld >= K; MN-major ld >= M (or N).
+ * Bases 16-byte aligned. Out-of-range elements of the tiles read as zero.
+ * Used for the stream synapse's currents x[T*B, F] * W[F, N] (B = W N-major,
+ * no transposed copy), input gradient G * W^T (both K-major) and weight
+ * gradient x^T G (A = x M-major, B = G N-major; no transposes).
+ * Replaces: the tl.dot contractions of src/myelin/triton/lif.py:554-612 (forward),
+ *   :1136-1180 (input gradient) and :1183-1228 (weight gradient), and the
+ *   torch.matmul projections of src/myelin/autograd.py:445-556.
+ */
+int mb_gemm(int in_dtype, const void* A, int a_major, int64_t lda, int64_t a_part_stride,
+            int a_parts, const int32_t* a_nonzero, const void* B, int b_major, int64_t ldb,
+            int64_t b_part_stride, int b_parts, const int32_t* b_nonzero, const void* bias,
+            int bias_dtype, int out_dtype, void* C, int64_t ldc, int64_t M, int64_t N, int64_t K,
+            void* stream);
+
+/*
+ * Split src[rows, cols] (element (r, c) at r * src_row_stride + c *
+ * src_col_stride, in elements; MB_F32, MB_BF16 or MB_F16) into `parts` (1..3)
+ * bf16 matrices dst + p * dst_part_stride, element (r, c) at r * dst_ld + c,
+ * whose sum is the fp32 source value exactly (part p = the bf16 rounding of
+ * what parts 0..p-1 left; non-finite values stay in part 0). A 16-bit source
+ * takes one part and keeps its own type: a plain re-laid-out copy (a
+ * transposed view, or rows padded to 16 bytes). The destination region
+ * [dst_rows, dst_cols] (at least the source's) is written in full, zeros
+ * outside the source. `nonzero` (nullable, `parts` ints) is set to 1 for each
+ * part holding a nonzero element, for mb_gemm's a_nonzero / b_nonzero.
+ * No reference counterpart (operand preparation for mb_gemm).
+ */
+int mb_split_bf16(int src_dtype, const void* src, int64_t rows, int64_t cols,
+                  int64_t src_row_stride, int64_t src_col_stride, int parts, void* dst,
+                  int64_t dst_rows, int64_t dst_cols, int64_t dst_ld, int64_t dst_part_stride,
+                  int32_t* nonzero, void* stream);
+
+/* Workspace (bytes) mb_column_sums needs for a [rows, cols] source. */
+int64_t mb_column_sums_workspace_bytes(int64_t rows, int64_t cols);
+
+/*
+ * out[c] = sum over r of src[r * ld + c], fp32 accumulation in a fixed order
+ * (deterministic), written as `out_dtype`. `workspace` must hold
+ * mb_column_sums_workspace_bytes(rows, cols) bytes (4-byte aligned).
+ * Replaces: the bias gradient of src/myelin/triton/lif.py:1231-1258 (and
+ *   grad_bias = grad.sum(...) of src/myelin/autograd.py:536-556).
+ */
+int mb_column_sums(int dtype, const void* src, int64_t rows, int64_t cols, int64_t ld,
+                   int out_dtype, void* out, void* workspace, int64_t workspace_bytes,
+                   void* stream);
+
 /*
  * Pack spikes[rows, n] (any dtype; nonzero = spike, -0.0 counts as zero) into
  * int32 words[rows, ceil(n/32)], LSB-first, zero padding bits.

@@ -66,6 +66,15 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mb_gemm_tn": (
         _int, [_int, _vp, _i64, _vp, _i64, _vp, _int, _int, _vp, _i64, _i64, _i64, _i64, _vp]
     ),
+    "mb_gemm": (
+        _int, [_int, _vp, _int, _i64, _i64, _int, _vp, _vp, _int, _i64, _i64, _int, _vp, _vp,
+               _int, _int, _vp, _i64, _i64, _i64, _i64, _vp]
+    ),
+    "mb_split_bf16": (
+        _int, [_int, _vp, _i64, _i64, _i64, _i64, _int, _vp, _i64, _i64, _i64, _i64, _vp, _vp]
+    ),
+    "mb_column_sums_workspace_bytes": (_i64, [_i64, _i64]),
+    "mb_column_sums": (_int, [_int, _vp, _i64, _i64, _i64, _int, _vp, _vp, _i64, _vp]),
     "mb_pack_spikes": (_int, [_int, _vp, _vp, _i64, _i64, _vp]),
     "mb_unpack_spikes": (_int, [_vp, _int, _vp, _i64, _i64, _vp]),
     "mb_count_rows": (_int, [_vp, _i64, _i64, _vp, _vp]),
@@ -265,6 +274,66 @@ def gemm_tn(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor | None,
         )
     check(status, "mb_gemm_tn")
     return out
+
+
+MB_KMAJOR, MB_MNMAJOR = 0, 1  # enum mb_major
+
+
+class GemmOperand:
+    """One mb_gemm operand: ``parts`` matrices of 16-bit elements stored from
+    ``tensor``'s first element, ``part_stride`` elements apart, each K-major
+    (element (r, k) at r * ld + k) or MN-major (element (r, k) at k * ld + r).
+    ``nonzero`` (int32 per part, from ``split_bf16``) lets the kernel skip
+    all-zero parts."""
+
+    def __init__(self, tensor: torch.Tensor, major: int, ld: int, *, parts: int = 1,
+                 part_stride: int = 0, nonzero: torch.Tensor | None = None) -> None:
+        self.tensor, self.major, self.ld = tensor, major, ld
+        self.parts, self.part_stride, self.nonzero = parts, part_stride, nonzero
+
+
+def gemm(a: GemmOperand, b: GemmOperand, M: int, N: int, K: int, out: torch.Tensor,
+         bias: torch.Tensor | None = None) -> torch.Tensor:
+    """out[M, N] = sum over kept part pairs of A_i[M, K] B_j[N, K]^T (+ bias) (``mb_gemm``)."""
+
+    dev = a.tensor.device
+    with torch.cuda.device(dev):
+        status = lib().mb_gemm(
+            dtype_code(a.tensor.dtype), ptr(a.tensor), a.major, a.ld, a.part_stride, a.parts,
+            ptr(a.nonzero), ptr(b.tensor), b.major, b.ld, b.part_stride, b.parts,
+            ptr(b.nonzero), ptr(bias), dtype_code(bias.dtype) if bias is not None else 0,
+            dtype_code(out.dtype), ptr(out), out.stride(0), M, N, K, stream_handle(dev),
+        )
+    check(status, "mb_gemm")
+    return out
+
+
+def split_bf16(src: torch.Tensor, rows: int, cols: int, row_stride: int, col_stride: int,
+               parts: int, dst: torch.Tensor, dst_rows: int, dst_cols: int, dst_ld: int,
+               dst_part_stride: int, nonzero: torch.Tensor | None = None) -> None:
+    """``mb_split_bf16``: element (r, c) of ``src`` (at r * row_stride + c *
+    col_stride from its first element) split into ``parts`` bf16 parts of
+    ``dst`` (or copied, for a 16-bit source), zeros outside the source."""
+
+    with torch.cuda.device(src.device):
+        status = lib().mb_split_bf16(
+            dtype_code(src.dtype), ptr(src), rows, cols, row_stride, col_stride, parts, ptr(dst),
+            dst_rows, dst_cols, dst_ld, dst_part_stride, ptr(nonzero), stream_handle(src.device),
+        )
+    check(status, "mb_split_bf16")
+
+
+def column_sums(src: torch.Tensor, rows: int, cols: int, ld: int, out: torch.Tensor) -> None:
+    """out[c] = sum over r of src[r * ld + c] in a fixed order (``mb_column_sums``)."""
+
+    need = int(lib().mb_column_sums_workspace_bytes(rows, cols))
+    ws = torch.empty(max(need // 4, 1), dtype=torch.float32, device=src.device)
+    with torch.cuda.device(src.device):
+        status = lib().mb_column_sums(
+            dtype_code(src.dtype), ptr(src), rows, cols, ld, dtype_code(out.dtype), ptr(out),
+            ptr(ws), ws.numel() * 4, stream_handle(src.device),
+        )
+    check(status, "mb_column_sums")
 
 
 def num_checkpoints(T: int) -> int:

@@ -93,28 +93,30 @@ class ALIFScanFunction(torch.autograd.Function):
 
 
 def _project(x2: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
-    """currents[T*B, N] = x2[T*B, F] @ weight[F, N] (+ bias).
+    """currents[T*B, N] = x2[T*B, F] @ weight[F, N] (+ bias) on the library's
+    tensor-core GEMM: 16-bit operands read in place (weight as an N-major
+    operand, no transposed copy), fp32 operands as exact 3-way bf16 splits
+    (fp32 products, see ``myelin_b200.projection``); fp32 accumulation, bias
+    added in fp32, one rounding to the input type."""
 
-    16-bit inputs run on the tcgen05 GEMM (fp32 accumulation, bias added in
-    fp32, one rounding to the input type). fp32 inputs keep fp32 arithmetic
-    (cuBLAS SGEMM): the tensor cores have no fp32-exact mode, and spike
-    parity with the fp32 reference needs fp32 products.
-    """
-
-    wt = weight.t().contiguous()  # [N, F]: K-major B operand
-    if cops.gemm_tn_dtype_ok(x2, wt):
-        return cops.gemm_tn(x2, wt, bias)
-    if bias is not None:
-        return torch.addmm(bias, x2, weight)
-    return torch.mm(x2, weight)
+    return cops.linear_project(x2, weight, bias)
 
 
 def _input_grad(g2: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
-    """dX[T*B, F] = G[T*B, N] @ weight[F, N]^T."""
+    """dX[T*B, F] = G[T*B, N] @ weight[F, N]^T (tensor cores, as ``_project``)."""
 
-    if cops.gemm_tn_dtype_ok(g2, weight):
-        return cops.gemm_tn(g2, weight)
-    return torch.mm(g2, weight.t())
+    return cops.linear_input_grad(g2, weight)
+
+
+def _weight_bias_grads(x2: torch.Tensor, g2: torch.Tensor, weight: torch.Tensor,
+                       bias: torch.Tensor | None, need_w: bool, need_b: bool):
+    """(dW = x2^T G on the tensor cores, x2 read as an M-major operand; db =
+    fixed-order column sums of G), each None when not needed."""
+
+    if not (need_w or need_b):
+        return None, None
+    gw, gb = cops.linear_weight_grad(x2, g2, weight, bias if need_b else None)
+    return (gw if need_w else None), gb
 
 
 class LinearScanFunction(torch.autograd.Function):
@@ -123,7 +125,8 @@ class LinearScanFunction(torch.autograd.Function):
     Outputs (final membrane, spikes [T,B,N]) when ``rate_output`` is False,
     else (final membrane, rates [B,N] = count / T). The projected currents are
     kept resident for the backward (no GEMM recompute); the backward runs the
-    reverse scan to get dL/dcurrents, then the two weight-side GEMMs.
+    reverse scan to get dL/dcurrents, then dX and dW on the tensor cores and
+    db as a fixed-order column sum (no library GEMM, no float atomics).
     Reference semantics: src/myelin/autograd.py:445-885.
     """
 
@@ -154,6 +157,8 @@ class LinearScanFunction(torch.autograd.Function):
         ctx.set_materialize_grads(False)
         ctx.save_for_backward(inputs, weight, currents, ckpt_v)
         ctx.has_bias = bias is not None
+        # dtype / device carrier for the bias gradient (no data kept)
+        ctx.bias_like = bias.new_empty(0) if bias is not None else None
         ctx.cfg = (decay, threshold, reset, surrogate, slope, rate_output)
         return vT, out
 
@@ -176,8 +181,9 @@ class LinearScanFunction(torch.autograd.Function):
         )
         g2 = grad_currents.view(T * B, N)
         grad_inputs = _input_grad(g2, weight).view(T, B, F) if need_x else None
-        grad_weight = torch.mm(inputs.reshape(T * B, F).t(), g2) if need_w else None
-        grad_bias = g2.sum(dim=0) if (need_b and ctx.has_bias) else None
+        grad_weight, grad_bias = _weight_bias_grads(
+            inputs.reshape(T * B, F), g2, weight, ctx.bias_like, need_w,
+            need_b and ctx.has_bias)
         return (grad_inputs, grad_weight, grad_bias, *tail)
 
 
@@ -252,8 +258,8 @@ class TwoLayerPackedHiddenRateFunction(torch.autograd.Function):
         g_cur2, _, _ = cops.scan_backward(cur2, ckpt2, None, grad_rates=g_rates, **scan_kw)
         del cur2
         g2 = g_cur2.view(T * B, O)
-        grad_w2 = torch.mm(hidden.t(), g2) if need_w2 else None
-        grad_b2 = g2.sum(dim=0) if (need_b2 and b2 is not None) else None
+        grad_w2, grad_b2 = _weight_bias_grads(hidden, g2, w2, b2, need_w2,
+                                              need_b2 and b2 is not None)
         del hidden
 
         grad_x = grad_w1 = grad_b1 = None
@@ -265,6 +271,6 @@ class TwoLayerPackedHiddenRateFunction(torch.autograd.Function):
             del cur1, g_hidden
             g1 = g_cur1.view(T * B, H)
             grad_x = _input_grad(g1, w1).view(T, B, F) if need_x else None
-            grad_w1 = torch.mm(x2.t(), g1) if need_w1 else None
-            grad_b1 = g1.sum(dim=0) if (need_b1 and b1 is not None) else None
+            grad_w1, grad_b1 = _weight_bias_grads(x2, g1, w1, b1, need_w1,
+                                                  need_b1 and b1 is not None)
         return (grad_x, grad_w1, grad_b1, grad_w2, grad_b2, *tail)

@@ -226,6 +226,92 @@ def gemm_tn_dtype_ok(a: torch.Tensor, b: torch.Tensor) -> bool:
 
 
 # ---------------------------------------------------------------------------
+# stream-synapse projections (myelin_b200.projection: mb_gemm, mb_split_bf16,
+# mb_column_sums)
+# ---------------------------------------------------------------------------
+def _linear_project_impl(x2: torch.Tensor, weight: torch.Tensor,
+                         bias: torch.Tensor | None) -> torch.Tensor:
+    from myelin_b200 import projection
+
+    return projection.project(x2, weight, bias)
+
+
+linear_project_op = torch.library.custom_op(f"{_NS}::linear_project", _linear_project_impl,
+                                            mutates_args=())
+
+
+@linear_project_op.register_fake
+def _linear_project_fake(x2, weight, bias):
+    return x2.new_empty((x2.shape[0], weight.shape[1]))
+
+
+def linear_project(x2: torch.Tensor, weight: torch.Tensor,
+                   bias: torch.Tensor | None = None) -> torch.Tensor:
+    """``x2[M, F] @ weight[F, N] (+ bias)`` on the tensor cores (16-bit or fp32)."""
+
+    if _tracing():
+        return linear_project_op(x2, weight, bias)
+    return _linear_project_impl(x2, weight, bias)
+
+
+def _linear_input_grad_impl(g2: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    from myelin_b200 import projection
+
+    return projection.input_grad(g2, weight)
+
+
+linear_input_grad_op = torch.library.custom_op(f"{_NS}::linear_input_grad",
+                                               _linear_input_grad_impl, mutates_args=())
+
+
+@linear_input_grad_op.register_fake
+def _linear_input_grad_fake(g2, weight):
+    return g2.new_empty((g2.shape[0], weight.shape[0]))
+
+
+def linear_input_grad(g2: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """``g2[M, N] @ weight[F, N]^T`` on the tensor cores."""
+
+    if _tracing():
+        return linear_input_grad_op(g2, weight)
+    return _linear_input_grad_impl(g2, weight)
+
+
+def _linear_weight_grad_impl(x2: torch.Tensor, g2: torch.Tensor, weight_like: torch.Tensor,
+                             bias_like: torch.Tensor | None) -> tuple[torch.Tensor, torch.Tensor]:
+    from myelin_b200 import projection
+
+    gw = projection.weight_grad(x2, g2, weight_like.dtype)
+    gb = (projection.bias_grad(g2, bias_like.dtype) if bias_like is not None
+          else g2.new_empty(0))
+    return gw, gb
+
+
+linear_weight_grad_op = torch.library.custom_op(f"{_NS}::linear_weight_grad",
+                                                _linear_weight_grad_impl, mutates_args=())
+
+
+@linear_weight_grad_op.register_fake
+def _linear_weight_grad_fake(x2, g2, weight_like, bias_like):
+    gw = weight_like.new_empty((x2.shape[1], g2.shape[1]))
+    gb = bias_like.new_empty((g2.shape[1],)) if bias_like is not None else g2.new_empty(0)
+    return gw, gb
+
+
+def linear_weight_grad(x2: torch.Tensor, g2: torch.Tensor, weight_like: torch.Tensor,
+                       bias_like: torch.Tensor | None
+                       ) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """``(x2^T @ g2, column sums of g2)`` in the weight's / bias's dtypes; the
+    bias gradient is None when ``bias_like`` is None."""
+
+    if _tracing():
+        gw, gb = linear_weight_grad_op(x2, g2, weight_like, bias_like)
+    else:
+        gw, gb = _linear_weight_grad_impl(x2, g2, weight_like, bias_like)
+    return gw, (gb if bias_like is not None else None)
+
+
+# ---------------------------------------------------------------------------
 # packing
 # ---------------------------------------------------------------------------
 def _pack_impl(spikes: torch.Tensor, rows: int, n: int) -> torch.Tensor:
@@ -370,5 +456,6 @@ def izhikevich_forward(x: torch.Tensor, v0: torch.Tensor, u0: torch.Tensor,
     return _izhikevich_impl(x, v0, u0, list(params))
 
 
-OPS = (scan_forward_op, scan_backward_op, gemm_tn_op, pack_op, unpack_op, count_rows_op,
-       count_columns_op, pack_count_op, izhikevich_op)
+OPS = (scan_forward_op, scan_backward_op, gemm_tn_op, linear_project_op, linear_input_grad_op,
+       linear_weight_grad_op, pack_op, unpack_op, count_rows_op, count_columns_op, pack_count_op,
+       izhikevich_op)

@@ -1,0 +1,227 @@
+// Operand preparation for the tensor-core GEMM and the bias gradient.
+//
+// mb_split_bf16: an fp32 matrix becomes 1-3 bf16 matrices whose sum is the
+// original value exactly (part p holds the bits 8p below the leading ones),
+// so that mb_gemm can form fp32 products on the 16-bit tensor cores; 16-bit
+// inputs are copied (one part), which also serves to re-lay out an operand
+// whose strides the tensor-map copies cannot take (a transposed view, or rows
+// not a multiple of 16 bytes, as for a 10-wide readout layer).
+//
+// mb_column_sums: per-column sums of a [rows, cols] matrix in fp32 with a
+// fixed summation order (row slices summed in order, then the slices in
+// order), e.g. the bias gradient db = sum over t, b of dL/dcurrents.
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace mb {
+namespace {
+
+template <typename TS>
+__device__ __forceinline__ float load_as_float(const TS* p) {
+  if constexpr (std::is_same<TS, float>::value) return __ldg(p);
+  else return Elem<TS>::to_f(*p);
+}
+
+// One element -> up to 3 bf16 parts; returns a bitmask of nonzero parts.
+// (A float16 destination is a plain one-part conversion.)
+template <typename TD>
+__device__ __forceinline__ uint32_t split_one(float x, int parts, TD* out, int64_t part_stride) {
+  if constexpr (std::is_same<TD, __half>::value) {
+    out[0] = __float2half_rn(x);
+    return x != 0.0f ? 1u : 0u;
+  } else {
+    if (!isfinite(x)) {  // inf / nan stay in the leading part, the rest are zero
+      out[0] = __float2bfloat16_rn(x);
+      for (int p = 1; p < parts; ++p) out[p * part_stride] = __float2bfloat16_rn(0.0f);
+      return 1u;
+    }
+    uint32_t nz = 0;
+    float rest = x;
+    for (int p = 0; p < parts; ++p) {
+      const __nv_bfloat16 h = __float2bfloat16_rn(rest);
+      out[p * part_stride] = h;
+      const float hf = __bfloat162float(h);
+      nz |= (hf != 0.0f) ? (1u << p) : 0u;
+      rest = __fsub_rn(rest, hf);  // exact: the rounding error of a bf16 rounding
+    }
+    return nz;
+  }
+}
+
+// Destination region [dst_rows, dst_cols] (each >= the source's): element
+// (r, c) is the split of src(r, c) inside the source and zero outside it.
+template <typename TS, typename TD>
+__global__ void split_bf16_kernel(const TS* __restrict__ src, int64_t rows, int64_t cols,
+                                  int64_t rs, int64_t cs, int parts,
+                                  TD* __restrict__ dst, int64_t dst_rows,
+                                  int64_t dst_cols, int64_t ld, int64_t part_stride,
+                                  int32_t* nonzero) {
+  const int64_t total = dst_rows * dst_cols;
+  uint32_t nz = 0;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = i / dst_cols;
+    const int64_t c = i - r * dst_cols;
+    const float x = (r < rows && c < cols) ? load_as_float(src + r * rs + c * cs) : 0.0f;
+    nz |= split_one(x, parts, dst + r * ld + c, part_stride);
+  }
+  if (nonzero != nullptr) {
+    nz = __reduce_or_sync(0xffffffffu, nz);
+    if ((threadIdx.x & 31) == 0) {
+      for (int p = 0; p < parts; ++p) {
+        if (nz & (1u << p)) atomicOr(nonzero + p, 1);
+      }
+    }
+  }
+}
+
+// Column sums, stage 1: block (cb, slice) sums rows [slice * rows_per_slice,
+// ...) of 256 consecutive columns, one column per thread, in row order.
+template <typename TS>
+__global__ void column_sums_partial_kernel(const TS* __restrict__ src, int64_t rows, int64_t cols,
+                                           int64_t ld, int64_t rows_per_slice,
+                                           float* __restrict__ partial) {
+  const int64_t c = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t r0 = int64_t(blockIdx.y) * rows_per_slice;
+  const int64_t r1 = imin64(rows, r0 + rows_per_slice);
+  if (c >= cols) return;
+  float acc = 0.0f;
+  for (int64_t r = r0; r < r1; ++r) acc += load_as_float(src + r * ld + c);
+  partial[int64_t(blockIdx.y) * cols + c] = acc;
+}
+
+// Stage 2: sum the slices of each column in slice order, write out.
+template <typename TO>
+__global__ void column_sums_final_kernel(const float* __restrict__ partial, int64_t slices,
+                                         int64_t cols, TO* __restrict__ out) {
+  const int64_t c = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  float acc = 0.0f;
+  for (int64_t s = 0; s < slices; ++s) acc += partial[s * cols + c];
+  out[c] = Elem<TO>::from_f(acc);
+}
+
+int64_t column_slices(int64_t rows, int64_t cols) {
+  const int64_t col_blocks = ceil_div(cols, 256);
+  int64_t slices = ceil_div(148 * 8, col_blocks);  // about 8 blocks per SM
+  const int64_t max_by_rows = ceil_div(rows, 128);  // at least 128 rows per slice
+  if (slices > max_by_rows) slices = max_by_rows;
+  return slices < 1 ? 1 : slices;
+}
+
+}  // namespace
+}  // namespace mb
+
+using namespace mb;
+
+extern "C" int mb_split_bf16(int src_dtype, const void* src, int64_t rows, int64_t cols,
+                             int64_t src_row_stride, int64_t src_col_stride, int parts, void* dst,
+                             int64_t dst_rows, int64_t dst_cols, int64_t dst_ld,
+                             int64_t dst_part_stride, int32_t* nonzero, void* stream) {
+  clear_error();
+  MB_CHECK_ARG(src_dtype == MB_F32 || src_dtype == MB_BF16 || src_dtype == MB_F16,
+               "mb_split_bf16: source must be float32, bfloat16 or float16");
+  MB_CHECK_ARG(parts >= 1 && parts <= 3, "mb_split_bf16: parts must be 1, 2 or 3");
+  MB_CHECK_ARG(src_dtype == MB_F32 || parts == 1,
+               "mb_split_bf16: a 16-bit source is copied in one part (of its own type)");
+  MB_CHECK_ARG(rows >= 0 && cols >= 0, "mb_split_bf16: negative size");
+  MB_CHECK_ARG(dst_rows >= rows && dst_cols >= cols && dst_ld >= dst_cols,
+               "mb_split_bf16: destination region smaller than the source");
+  MB_CHECK_ARG(parts == 1 || dst_part_stride >= dst_rows * dst_ld,
+               "mb_split_bf16: part stride smaller than a part");
+  cudaStream_t s = as_stream(stream);
+  if (nonzero != nullptr) cudaMemsetAsync(nonzero, 0, sizeof(int32_t) * parts, s);
+  if (dst_rows == 0 || dst_cols == 0) {
+    MB_CHECK_LAUNCH("mb_split_bf16");
+    return 0;
+  }
+  MB_CHECK_ARG((src != nullptr || rows * cols == 0) && dst != nullptr,
+               "mb_split_bf16: null pointer");
+  const int64_t total = dst_rows * dst_cols;
+  const unsigned grid = static_cast<unsigned>(imin64(ceil_div(total, 256), 148 * 16));
+  auto* out = static_cast<__nv_bfloat16*>(dst);
+  switch (src_dtype) {
+    case MB_F32:
+      split_bf16_kernel<float, __nv_bfloat16><<<grid, 256, 0, s>>>(
+          static_cast<const float*>(src), rows, cols, src_row_stride, src_col_stride, parts, out,
+          dst_rows, dst_cols, dst_ld, dst_part_stride, nonzero);
+      break;
+    case MB_BF16:
+      split_bf16_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, 256, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(src), rows, cols, src_row_stride, src_col_stride,
+          parts, out, dst_rows, dst_cols, dst_ld, dst_part_stride, nonzero);
+      break;
+    default:  // float16 stays float16 (one part)
+      split_bf16_kernel<__half, __half><<<grid, 256, 0, s>>>(
+          static_cast<const __half*>(src), rows, cols, src_row_stride, src_col_stride, parts,
+          static_cast<__half*>(dst), dst_rows, dst_cols, dst_ld, dst_part_stride, nonzero);
+      break;
+  }
+  MB_CHECK_LAUNCH("mb_split_bf16");
+  return 0;
+}
+
+extern "C" int64_t mb_column_sums_workspace_bytes(int64_t rows, int64_t cols) {
+  if (rows <= 0 || cols <= 0) return 0;
+  return column_slices(rows, cols) * cols * int64_t(sizeof(float));
+}
+
+extern "C" int mb_column_sums(int dtype, const void* src, int64_t rows, int64_t cols, int64_t ld,
+                              int out_dtype, void* out, void* workspace, int64_t workspace_bytes,
+                              void* stream) {
+  clear_error();
+  MB_CHECK_ARG(dtype == MB_F32 || dtype == MB_BF16 || dtype == MB_F16,
+               "mb_column_sums: source must be float32, bfloat16 or float16");
+  MB_CHECK_ARG(out_dtype == MB_F32 || out_dtype == MB_BF16 || out_dtype == MB_F16,
+               "mb_column_sums: output must be float32, bfloat16 or float16");
+  MB_CHECK_ARG(rows >= 0 && cols >= 0 && ld >= cols, "mb_column_sums: bad shape");
+  cudaStream_t s = as_stream(stream);
+  if (cols == 0) return 0;
+  MB_CHECK_ARG(out != nullptr, "mb_column_sums: null output");
+  if (rows == 0) {
+    cudaMemsetAsync(out, 0, cols * (out_dtype == MB_F32 ? 4 : 2), s);
+    MB_CHECK_LAUNCH("mb_column_sums");
+    return 0;
+  }
+  MB_CHECK_ARG(src != nullptr, "mb_column_sums: null source");
+  const int64_t slices = column_slices(rows, cols);
+  const int64_t need = slices * cols * int64_t(sizeof(float));
+  MB_CHECK_ARG(workspace != nullptr && workspace_bytes >= need && aligned_to(workspace, 4),
+               "mb_column_sums: workspace of %lld bytes required, got %lld", (long long)need,
+               (long long)workspace_bytes);
+  float* partial = static_cast<float*>(workspace);
+  const dim3 grid1(static_cast<unsigned>(ceil_div(cols, 256)), static_cast<unsigned>(slices));
+  const int64_t per = ceil_div(rows, slices);
+  switch (dtype) {
+    case MB_F32:
+      column_sums_partial_kernel<float><<<grid1, 256, 0, s>>>(static_cast<const float*>(src),
+                                                              rows, cols, ld, per, partial);
+      break;
+    case MB_BF16:
+      column_sums_partial_kernel<__nv_bfloat16><<<grid1, 256, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(src), rows, cols, ld, per, partial);
+      break;
+    default:
+      column_sums_partial_kernel<__half><<<grid1, 256, 0, s>>>(static_cast<const __half*>(src),
+                                                               rows, cols, ld, per, partial);
+      break;
+  }
+  const unsigned grid2 = static_cast<unsigned>(ceil_div(cols, 256));
+  switch (out_dtype) {
+    case MB_F32:
+      column_sums_final_kernel<float><<<grid2, 256, 0, s>>>(partial, slices, cols,
+                                                            static_cast<float*>(out));
+      break;
+    case MB_BF16:
+      column_sums_final_kernel<__nv_bfloat16><<<grid2, 256, 0, s>>>(
+          partial, slices, cols, static_cast<__nv_bfloat16*>(out));
+      break;
+    default:
+      column_sums_final_kernel<__half><<<grid2, 256, 0, s>>>(partial, slices, cols,
+                                                             static_cast<__half*>(out));
+      break;
+  }
+  MB_CHECK_LAUNCH("mb_column_sums");
+  return 0;
+}

@@ -38,6 +38,9 @@ constexpr int kStages = 4;
 constexpr int kThreads = 192;
 constexpr int kUmmaK = 16;
 
+// Up to this many (A part, B part) products summed into one accumulator.
+constexpr int kMaxSegments = 6;
+
 struct GemmArgs {
   const void* bias;
   void* C;
@@ -46,7 +49,28 @@ struct GemmArgs {
   int bias_dtype;  // MB_F32 / MB_BF16 / MB_F16
   int vec_ok;      // C rows 16-byte aligned: 16-byte stores
   int tma_store;   // write C through smem + bulk tensor stores (tma_c valid)
+  // C = sum over segments q of A[seg_a[q]] * B[seg_b[q]]^T: the K loop runs
+  // over every enabled segment in turn. Segment q > 0 is skipped when a_nonzero
+  // or b_nonzero (device flags, one int per part, nullable) says its A or B
+  // part is all zeros; segment 0 always runs.
+  int nseg;
+  int8_t seg_a[kMaxSegments];
+  int8_t seg_b[kMaxSegments];
+  const int32_t* a_nonzero;
+  const int32_t* b_nonzero;
 };
+
+// Which segments this launch runs (bit q = segment q); read once per thread
+// that walks the K loop, so the copy and MMA threads agree.
+__device__ __forceinline__ uint32_t segment_mask(const GemmArgs& a) {
+  uint32_t m = 1u;
+  for (int q = 1; q < a.nseg; ++q) {
+    const bool on = (a.a_nonzero == nullptr || __ldg(a.a_nonzero + a.seg_a[q]) != 0) &&
+                    (a.b_nonzero == nullptr || __ldg(a.b_nonzero + a.seg_b[q]) != 0);
+    m |= on ? (1u << q) : 0u;
+  }
+  return m;
+}
 
 template <int BN>
 struct Layout {
@@ -65,15 +89,6 @@ struct Layout {
 // ---------------------------------------------------------------------------
 // PTX wrappers
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_addr(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_addr(bar))
-      : "memory");
-}
-
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0,
                                              int c1) {
   asm volatile(
@@ -94,6 +109,17 @@ __device__ __forceinline__ void tma_store_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
+// 3-D tiled loads: {inner, outer, part} coordinates over an operand stored as
+// [parts, outer, ld] (the part dimension has extent 1 for plain operands).
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1,
+                                            int c2, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_addr(bar))
+      : "memory");
+}
+
 // Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of
 // 128 bytes, 8-row groups 1024 bytes apart (the layout the TMA copy writes).
 __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
@@ -106,13 +132,61 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
   return d;
 }
 
-// Instruction descriptor of kind::f16: fp32 accumulate, A/B type, both K-major.
-template <typename TIn, int BN>
+// Bytes of one MN-major swizzle block in shared memory: 64 MN-elements
+// (128 B) x kBK K-rows, as one TMA box writes it.
+constexpr uint32_t kMnBlockBytes = 128 * kBK;
+
+// Shared-memory matrix descriptor: MN-major operand (the M or N index is the
+// contiguous one), 128-byte swizzle. A K-row holds 64 consecutive M/N
+// elements (128 B); 8 K-rows form one 1024-byte swizzle atom (stride byte
+// offset); the next 64 M/N elements start kMnBlockBytes further on (leading
+// byte offset), the next TMA box.
+__device__ __forceinline__ uint64_t sw128_mnmajor_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= uint64_t((saddr >> 4) & 0x3fffu);       // start address
+  d |= uint64_t(kMnBlockBytes >> 4) << 16;      // leading byte offset: next 64 M/N elements
+  d |= uint64_t(1024 >> 4) << 32;               // stride byte offset: next 8 K-rows
+  d |= uint64_t(1) << 46;                       // descriptor version
+  d |= uint64_t(2) << 61;                       // 128-byte swizzle
+  return d;
+}
+
+// Descriptor of the k-th 16-deep K step of a staged operand tile.
+template <bool MN>
+__device__ __forceinline__ uint64_t operand_desc(uint32_t base, int k) {
+  if constexpr (MN) {
+    return sw128_mnmajor_desc(base + uint32_t(k) * kUmmaK * 128);  // 16 K-rows of 128 B
+  } else {
+    return sw128_kmajor_desc(base + uint32_t(k) * kUmmaK * 2);  // 16 elements along a row
+  }
+}
+
+// Stage one operand tile (ROWS M/N-elements x kBK K-elements of part `part`)
+// into shared memory: one box of kBK x ROWS for a K-major operand, ROWS/64
+// boxes of 64 x kBK (kMnBlockBytes apart) for an MN-major one.
+template <bool MN, int ROWS>
+__device__ __forceinline__ void load_operand(uint8_t* dst, const CUtensorMap* map, int64_t mn0,
+                                             int kb, int part, uint64_t* bar) {
+  if constexpr (MN) {
+#pragma unroll
+    for (int j = 0; j < ROWS / 64; ++j) {
+      tma_load_3d(dst + j * kMnBlockBytes, map, static_cast<int>(mn0) + 64 * j, kb * kBK, part,
+                  bar);
+    }
+  } else {
+    tma_load_3d(dst, map, kb * kBK, static_cast<int>(mn0), part, bar);
+  }
+}
+
+// Instruction descriptor of kind::f16: fp32 accumulate, A/B type, A/B major.
+template <typename TIn, int BN, bool A_MN = false, bool B_MN = false>
 __device__ __forceinline__ uint32_t mma_idesc() {
   constexpr uint32_t ab = std::is_same<TIn, __nv_bfloat16>::value ? 1u : 0u;
   return (1u << 4)            // D = F32
          | (ab << 7)          // A format
          | (ab << 10)         // B format
+         | (uint32_t(A_MN) << 15)  // A MN-major
+         | (uint32_t(B_MN) << 16)  // B MN-major
          | (uint32_t(BN >> 3) << 17)
          | (uint32_t(kBM >> 4) << 24);
 }
@@ -324,10 +398,10 @@ __device__ __forceinline__ void drain_tile(uint32_t tbase, int64_t row0, int64_t
   }
 }
 
-template <typename TIn, typename TOut, int BN>
+template <typename TIn, typename TOut, int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                   const __grid_constant__ CUtensorMap tma_c, const GemmArgs args) {
+                   const __grid_constant__ CUtensorMap tma_c, const __grid_constant__ GemmArgs args) {
   using L = Layout<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -375,19 +449,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
+      const uint32_t segs = segment_mask(args);
       for (int64_t tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-        const int tm = static_cast<int>(tile / n_tiles);
-        const int tn = static_cast<int>(tile % n_tiles);
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
-          const int s = static_cast<int>(it % kStages);
-          const uint32_t use = it / kStages;
-          if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1)) {
-            ok = false;
-            break;
+        const int64_t tm = tile / n_tiles;
+        const int64_t tn = tile % n_tiles;
+        for (int q = 0; q < args.nseg && ok; ++q) {
+          if (((segs >> q) & 1u) == 0) continue;
+          for (int kb = 0; kb < kblocks; ++kb, ++it) {
+            const int s = static_cast<int>(it % kStages);
+            const uint32_t use = it / kStages;
+            if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[s], L::kStageBytes);
+            load_operand<A_MN, kBM>(sa + s * L::kABytes, &tma_a, tm * kBM, kb, args.seg_a[q],
+                                    &full[s]);
+            load_operand<B_MN, BN>(sb + s * L::kBBytes, &tma_b, tn * BN, kb, args.seg_b[q],
+                                   &full[s]);
           }
-          mbar_arrive_expect_tx(&full[s], L::kStageBytes);
-          tma_load_2d(sa + s * L::kABytes, &tma_a, kb * kBK, tm * kBM, &full[s]);
-          tma_load_2d(sb + s * L::kBBytes, &tma_b, kb * kBK, tn * BN, &full[s]);
         }
       }
       // every issued copy has landed before the CTA can retire; a wait that
@@ -400,7 +480,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = mma_idesc<TIn, BN>();
+      const uint32_t idesc = mma_idesc<TIn, BN, A_MN, B_MN>();
+      const uint32_t segs = segment_mask(args);
       uint32_t it = 0, local = 0;
       bool ok = true;
       for (int64_t tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++local) {
@@ -409,21 +490,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (use_b > 0 && !mbar_wait_bounded(&acc_empty[b], (use_b - 1) & 1)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + b * BN;
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
-          const int s = static_cast<int>(it % kStages);
-          if (!mbar_wait_bounded(&full[s], (it / kStages) & 1)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a0 = smem_addr(sa + s * L::kABytes);
-          const uint32_t b0 = smem_addr(sb + s * L::kBBytes);
+        bool acc = false;  // the tile's first MMA overwrites the accumulator
+        for (int q = 0; q < args.nseg && ok; ++q) {
+          if (((segs >> q) & 1u) == 0) continue;
+          for (int kb = 0; kb < kblocks; ++kb, ++it) {
+            const int s = static_cast<int>(it % kStages);
+            if (!mbar_wait_bounded(&full[s], (it / kStages) & 1)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a0 = smem_addr(sa + s * L::kABytes);
+            const uint32_t b0 = smem_addr(sb + s * L::kBBytes);
 #pragma unroll
-          for (int k = 0; k < kBK / kUmmaK; ++k) {
-            mma_f16(d_tmem, sw128_kmajor_desc(a0 + k * kUmmaK * 2),
-                    sw128_kmajor_desc(b0 + k * kUmmaK * 2), idesc, (kb | k) != 0);
+            for (int k = 0; k < kBK / kUmmaK; ++k) {
+              mma_f16(d_tmem, operand_desc<A_MN>(a0, k), operand_desc<B_MN>(b0, k), idesc,
+                      (acc || k != 0) ? 1u : 0u);
+            }
+            acc = true;
+            mma_commit(&empty[s]);  // the stage is free once these MMAs finish
           }
-          mma_commit(&empty[s]);  // the stage is free once these MMAs finish
         }
         if (ok) mma_commit(&acc_full[b]);  // the tile's accumulator is complete
       }
@@ -520,15 +606,32 @@ __device__ __forceinline__ void cluster_sync_all() {
                    : "memory");
 }
 
-// 2-D tiled load into this CTA's shared memory whose completion bytes are
-// counted on the barrier at cluster address `bar_cluster` (the leader's).
-__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int c0, int c1,
-                                                 uint32_t bar_cluster) {
+// 3-D tiled load ({inner, outer, part}) into this CTA's shared memory whose
+// completion bytes are counted on the barrier at cluster address
+// `bar_cluster` (the leader's). Loads of this GPU's own memory only.
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, int c0, int c1,
+                                                 int c2, uint32_t bar_cluster) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar_cluster)
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar_cluster)
       : "memory");
+}
+
+// load_operand for one CTA of the pair: its 128 M/N-elements of the tile.
+template <bool MN>
+__device__ __forceinline__ void load_operand_pair(uint8_t* dst, const CUtensorMap* map,
+                                                  int64_t mn0, int kb, int part,
+                                                  uint32_t bar_cluster) {
+  if constexpr (MN) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      tma_load_3d_pair(dst + j * kMnBlockBytes, map, static_cast<int>(mn0) + 64 * j, kb * kBK,
+                       part, bar_cluster);
+    }
+  } else {
+    tma_load_3d_pair(dst, map, kb * kBK, static_cast<int>(mn0), part, bar_cluster);
+  }
 }
 
 __device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
@@ -553,18 +656,18 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
                : "memory");
 }
 
-template <typename TIn>
+template <typename TIn, bool A_MN, bool B_MN>
 __device__ __forceinline__ uint32_t mma_idesc_pair() {
   constexpr uint32_t ab = std::is_same<TIn, __nv_bfloat16>::value ? 1u : 0u;
-  return (1u << 4) | (ab << 7) | (ab << 10) | (uint32_t(k2BN >> 3) << 17) |
-         (uint32_t(k2BM >> 4) << 24);
+  return (1u << 4) | (ab << 7) | (ab << 10) | (uint32_t(A_MN) << 15) | (uint32_t(B_MN) << 16) |
+         (uint32_t(k2BN >> 3) << 17) | (uint32_t(k2BM >> 4) << 24);
 }
 
-template <typename TIn, typename TOut>
+template <typename TIn, typename TOut, bool A_MN, bool B_MN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
     gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
                         const __grid_constant__ CUtensorMap tma_b,
-                        const __grid_constant__ CUtensorMap tma_c, const GemmArgs args) {
+                        const __grid_constant__ CUtensorMap tma_c, const __grid_constant__ GemmArgs args) {
   using L = Layout2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -616,20 +719,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
+      const uint32_t segs = segment_mask(args);
       for (int64_t tile = pair; tile < tiles && ok; tile += pairs) {
-        const int tm = static_cast<int>(tile / n_tiles);
-        const int tn = static_cast<int>(tile % n_tiles);
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
-          const int s = static_cast<int>(it % k2Stages);
-          const uint32_t use = it / k2Stages;
-          if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1)) {
-            ok = false;
-            break;
+        const int64_t tm = tile / n_tiles;
+        const int64_t tn = tile % n_tiles;
+        for (int q = 0; q < args.nseg && ok; ++q) {
+          if (((segs >> q) & 1u) == 0) continue;
+          for (int kb = 0; kb < kblocks; ++kb, ++it) {
+            const int s = static_cast<int>(it % k2Stages);
+            const uint32_t use = it / k2Stages;
+            if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1)) {
+              ok = false;
+              break;
+            }
+            const uint32_t bar = cluster_addr(smem_addr(&full[s]), 0);
+            if (leader) mbar_arrive_expect_tx(&full[s], 2 * L::kStageBytes);
+            load_operand_pair<A_MN>(sa + s * L::kABytes, &tma_a, tm * k2BM + int64_t(rank) * 128,
+                                    kb, args.seg_a[q], bar);
+            load_operand_pair<B_MN>(sb + s * L::kBBytes, &tma_b, tn * k2BN + int64_t(rank) * 128,
+                                    kb, args.seg_b[q], bar);
           }
-          const uint32_t bar = cluster_addr(smem_addr(&full[s]), 0);
-          if (leader) mbar_arrive_expect_tx(&full[s], 2 * L::kStageBytes);
-          tma_load_2d_pair(sa + s * L::kABytes, &tma_a, kb * kBK, tm * k2BM + int(rank) * 128, bar);
-          tma_load_2d_pair(sb + s * L::kBBytes, &tma_b, kb * kBK, tn * k2BN + int(rank) * 128, bar);
         }
       }
       if (leader) {
@@ -644,7 +753,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0 && leader) {
-      const uint32_t idesc = mma_idesc_pair<TIn>();
+      const uint32_t idesc = mma_idesc_pair<TIn, A_MN, B_MN>();
+      const uint32_t segs = segment_mask(args);
       uint32_t it = 0, local = 0;
       bool ok = true;
       for (int64_t tile = pair; tile < tiles && ok; tile += pairs, ++local) {
@@ -653,23 +763,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
         if (use_b > 0 && !mbar_wait_bounded(&acc_empty[b], (use_b - 1) & 1)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + b * k2BN;
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
-          const int s = static_cast<int>(it % k2Stages);
-          if (!mbar_wait_bounded(&full[s], (it / k2Stages) & 1)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a0 = smem_addr(sa + s * L::kABytes);
-          const uint32_t b0 = smem_addr(sb + s * L::kBBytes);
+        bool acc = false;  // the tile's first MMA overwrites the accumulator
+        for (int q = 0; q < args.nseg && ok; ++q) {
+          if (((segs >> q) & 1u) == 0) continue;
+          for (int kb = 0; kb < kblocks; ++kb, ++it) {
+            const int s = static_cast<int>(it % k2Stages);
+            if (!mbar_wait_bounded(&full[s], (it / k2Stages) & 1)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a0 = smem_addr(sa + s * L::kABytes);
+            const uint32_t b0 = smem_addr(sb + s * L::kBBytes);
 #pragma unroll
-          for (int k = 0; k < kBK / kUmmaK; ++k) {
-            mma_f16_pair(d_tmem, sw128_kmajor_desc(a0 + k * kUmmaK * 2),
-                         sw128_kmajor_desc(b0 + k * kUmmaK * 2), idesc, (kb | k) != 0);
+            for (int k = 0; k < kBK / kUmmaK; ++k) {
+              mma_f16_pair(d_tmem, operand_desc<A_MN>(a0, k), operand_desc<B_MN>(b0, k), idesc,
+                           (acc || k != 0) ? 1u : 0u);
+            }
+            acc = true;
+            // the stage is free in both CTAs once these MMAs finish
+            mma_commit_pair(cluster_addr(smem_addr(&empty[s]), 0));
+            mma_commit_pair(cluster_addr(smem_addr(&empty[s]), 1));
           }
-          // the stage is free in both CTAs once these MMAs finish
-          mma_commit_pair(cluster_addr(smem_addr(&empty[s]), 0));
-          mma_commit_pair(cluster_addr(smem_addr(&empty[s]), 1));
         }
         if (ok) {  // the tile's accumulator halves are complete in both CTAs
           mma_commit_pair(cluster_addr(smem_addr(&acc_full[b]), 0));
@@ -719,18 +834,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
 // ---------------------------------------------------------------------------
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() { return tma_encode_fn(); }
 
-// 2-D map over a row-major [rows, k] matrix with leading dimension ld
-// (elements); box = 64 k-elements x box_rows rows, 128-byte swizzle.
-bool make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int64_t ld,
-              int box_rows, bool bf16) {
+// One GEMM operand in global memory: `parts` matrices of 16-bit elements, part
+// p starting p * part_stride elements after `ptr`. K-major: rows of K
+// contiguous elements, row r at r * ld; MN-major: K rows of M (or N)
+// contiguous elements, row k at k * ld.
+struct Operand {
+  const void* ptr;
+  int64_t ld;
+  int64_t part_stride;
+  int parts;
+  bool mn_major;
+};
+
+// 3-D map {inner, outer, part} over an operand whose M/N extent is `mn`:
+// K-major box 64 K-elements x box_rows rows, MN-major box 64 M/N-elements x
+// kBK K-rows; 128-byte swizzle either way. Elements outside the operand
+// (K and M/N tails) read as zero.
+bool make_operand_map(CUtensorMap* map, const Operand& op, int64_t mn, int64_t k, int box_rows,
+                      bool bf16) {
   auto fn = encode_fn();
   if (fn == nullptr) return false;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
-  cuuint32_t estride[2] = {1, 1};
+  const int64_t inner = op.mn_major ? mn : k;
+  const int64_t outer = op.mn_major ? k : mn;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer),
+                        static_cast<cuuint64_t>(op.parts)};
+  const int64_t part_bytes = (op.parts > 1 ? op.part_stride : outer * op.ld) * 2;
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(op.ld * 2), static_cast<cuuint64_t>(part_bytes)};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(kBK),
+                       static_cast<cuuint32_t>(op.mn_major ? kBK : box_rows), 1};
+  cuuint32_t estride[3] = {1, 1, 1};
   const CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                        2, const_cast<void*>(ptr), dims, strides, box, estride,
+                        3, const_cast<void*>(op.ptr), dims, strides, box, estride,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
@@ -762,10 +896,10 @@ int sm_count() {
   return n > 0 ? n : 148;
 }
 
-template <typename TIn, typename TOut, int BN>
+template <typename TIn, typename TOut, int BN, bool A_MN, bool B_MN>
 int launch(const CUtensorMap& ma, const CUtensorMap& mb_, const CUtensorMap& mc,
            const GemmArgs& args, cudaStream_t s) {
-  auto kern = gemm_tn_kernel<TIn, TOut, BN>;
+  auto kern = gemm_tn_kernel<TIn, TOut, BN, A_MN, B_MN>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        static_cast<int>(Layout<BN>::kSmem));
   const int64_t tiles = ((args.M + kBM - 1) / kBM) * ((args.N + BN - 1) / BN);
@@ -774,10 +908,10 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb_, const CUtensorMap& mc,
   return 0;
 }
 
-template <typename TIn, typename TOut>
+template <typename TIn, typename TOut, bool A_MN, bool B_MN>
 int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb_, const CUtensorMap& mc,
                 const GemmArgs& args, cudaStream_t s) {
-  auto kern = gemm_tn_pair_kernel<TIn, TOut>;
+  auto kern = gemm_tn_pair_kernel<TIn, TOut, A_MN, B_MN>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        static_cast<int>(Layout2::kSmem));
   const int64_t tiles = ((args.M + k2BM - 1) / k2BM) * ((args.N + k2BN - 1) / k2BN);
@@ -795,43 +929,77 @@ int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb_, const CUtensorMap
 //    epilogue, is faster (K = 1024: 1062 vs 937);
 //  - small problems (under two waves of one-SM tiles) go to the pair kernel
 //    (6400 x 1024 x 784: 440 vs 306).
-bool use_pair(const GemmArgs& args, bool out_f32) {
+// `k_eff` is the K loop length summed over the segments.
+bool use_pair(const GemmArgs& args, int64_t k_eff, bool out_f32) {
   const int sms = sm_count();
   const int64_t pair_tiles = ((args.M + k2BM - 1) / k2BM) * ((args.N + k2BN - 1) / k2BN);
   const int64_t single_tiles = ((args.M + kBM - 1) / kBM) * ((args.N + 255) / 256);
   if (args.M < k2BM || args.N < k2BN || pair_tiles < sms / 2) return false;
-  return (args.K >= 2048 && !out_f32) || single_tiles < 2 * sms;
+  return (k_eff >= 2048 && !out_f32) || single_tiles < 2 * sms;
+}
+
+template <typename TIn, typename TOut, bool A_MN, bool B_MN>
+int launch_majors(const Operand& A, const Operand& B, GemmArgs args, int out_dtype,
+                  cudaStream_t s) {
+  const bool bf16 = std::is_same<TIn, __nv_bfloat16>::value;
+  CUtensorMap ma, mbm, mc;
+  memset(&mc, 0, sizeof(mc));
+  args.tma_store = make_c_map(&mc, args.C, args.M, args.N, args.ldc, out_dtype) ? 1 : 0;
+  if (use_pair(args, args.K * args.nseg, out_dtype == MB_F32)) {
+    // both operand maps: each CTA's 128 rows (K-major) / 64-wide blocks (MN-major)
+    if (!make_operand_map(&ma, A, args.M, args.K, 128, bf16) ||
+        !make_operand_map(&mbm, B, args.N, args.K, 128, bf16)) {
+      set_error("mb_gemm: cuTensorMapEncodeTiled failed (shape or alignment)");
+      return 1;
+    }
+    return launch_pair<TIn, TOut, A_MN, B_MN>(ma, mbm, mc, args, s);
+  }
+  const int bn = args.N >= 192 ? 256 : (args.N > 64 ? 128 : 64);
+  if (!make_operand_map(&ma, A, args.M, args.K, kBM, bf16) ||
+      !make_operand_map(&mbm, B, args.N, args.K, bn, bf16)) {
+    set_error("mb_gemm: cuTensorMapEncodeTiled failed (shape or alignment)");
+    return 1;
+  }
+  if (bn == 256) return launch<TIn, TOut, 256, A_MN, B_MN>(ma, mbm, mc, args, s);
+  if (bn == 128) return launch<TIn, TOut, 128, A_MN, B_MN>(ma, mbm, mc, args, s);
+  return launch<TIn, TOut, 64, A_MN, B_MN>(ma, mbm, mc, args, s);
 }
 
 template <typename TIn, typename TOut>
-int launch_bn(const void* A, int64_t lda, const void* B, int64_t ldb, GemmArgs args,
-              int out_dtype, cudaStream_t s) {
-  const bool bf16 = std::is_same<TIn, __nv_bfloat16>::value;
-  CUtensorMap ma, mbm;
-  if (use_pair(args, out_dtype == MB_F32)) {
-    // both operand maps: 64 K-elements x 128 rows (each CTA's half of the pair tile)
-    if (!make_map(&ma, A, args.M, args.K, lda, 128, bf16) ||
-        !make_map(&mbm, B, args.N, args.K, ldb, 128, bf16)) {
-      set_error("mb_gemm_tn: cuTensorMapEncodeTiled failed (shape or alignment)");
-      return 1;
-    }
-    CUtensorMap mc;
-    memset(&mc, 0, sizeof(mc));
-    args.tma_store = make_c_map(&mc, args.C, args.M, args.N, args.ldc, out_dtype) ? 1 : 0;
-    return launch_pair<TIn, TOut>(ma, mbm, mc, args, s);
+int launch_typed(const Operand& A, const Operand& B, const GemmArgs& args, int out_dtype,
+                 cudaStream_t s) {
+  if (!A.mn_major && !B.mn_major) return launch_majors<TIn, TOut, false, false>(A, B, args, out_dtype, s);
+  if (!A.mn_major && B.mn_major) return launch_majors<TIn, TOut, false, true>(A, B, args, out_dtype, s);
+  return launch_majors<TIn, TOut, true, true>(A, B, args, out_dtype, s);
+}
+
+// Check one operand's layout; `mn` is its M (A) or N (B) extent.
+bool operand_ok(const Operand& op, int64_t mn, int64_t K, const char* name) {
+  if (op.parts < 1 || op.parts > 3) {
+    set_error("mb_gemm: %s parts must be 1, 2 or 3 (got %d)", name, op.parts);
+    return false;
   }
-  const int bn = args.N >= 192 ? 256 : (args.N > 64 ? 128 : 64);
-  if (!make_map(&ma, A, args.M, args.K, lda, kBM, bf16) ||
-      !make_map(&mbm, B, args.N, args.K, ldb, bn, bf16)) {
-    set_error("mb_gemm_tn: cuTensorMapEncodeTiled failed (shape or alignment)");
-    return 1;
+  if (op.ptr == nullptr || !aligned_to(op.ptr, 16)) {
+    set_error("mb_gemm: %s must be a 16-byte aligned device pointer", name);
+    return false;
   }
-  CUtensorMap mc;
-  memset(&mc, 0, sizeof(mc));
-  args.tma_store = make_c_map(&mc, args.C, args.M, args.N, args.ldc, out_dtype) ? 1 : 0;
-  if (bn == 256) return launch<TIn, TOut, 256>(ma, mbm, mc, args, s);
-  if (bn == 128) return launch<TIn, TOut, 128>(ma, mbm, mc, args, s);
-  return launch<TIn, TOut, 64>(ma, mbm, mc, args, s);
+  if (op.ld % 8 != 0) {
+    set_error("mb_gemm: leading dimension of %s must be a multiple of 8 (16-byte rows)", name);
+    return false;
+  }
+  if (op.mn_major ? op.ld < mn : (op.ld < K || K % 8 != 0)) {
+    set_error(op.mn_major ? "mb_gemm: %s: leading dimension smaller than its M/N extent"
+                          : "mb_gemm: %s: K must be a multiple of 8 and at most the leading "
+                            "dimension",
+              name);
+    return false;
+  }
+  const int64_t rows = op.mn_major ? K : mn;
+  if (op.parts > 1 && (op.part_stride % 8 != 0 || op.part_stride < rows * op.ld)) {
+    set_error("mb_gemm: %s part stride must be a multiple of 8 covering a whole part", name);
+    return false;
+  }
+  return true;
 }
 
 }  // namespace
@@ -839,40 +1007,80 @@ int launch_bn(const void* A, int64_t lda, const void* B, int64_t ldb, GemmArgs a
 
 using namespace mb;
 
-extern "C" int mb_gemm_tn(int in_dtype, const void* A, int64_t lda, const void* B, int64_t ldb,
-                          const void* bias, int bias_dtype, int out_dtype, void* C, int64_t ldc,
-                          int64_t M, int64_t N, int64_t K, void* stream) {
+extern "C" int mb_gemm(int in_dtype, const void* A, int a_major, int64_t lda, int64_t a_part_stride,
+                       int a_parts, const int32_t* a_nonzero, const void* B, int b_major,
+                       int64_t ldb, int64_t b_part_stride, int b_parts, const int32_t* b_nonzero,
+                       const void* bias, int bias_dtype, int out_dtype, void* C, int64_t ldc,
+                       int64_t M, int64_t N, int64_t K, void* stream) {
   clear_error();
   MB_CHECK_ARG(in_dtype == MB_BF16 || in_dtype == MB_F16,
-               "mb_gemm_tn: inputs must be bfloat16 or float16 (got dtype %d)", in_dtype);
+               "mb_gemm: inputs must be bfloat16 or float16 (got dtype %d)", in_dtype);
   MB_CHECK_ARG(out_dtype == MB_F32 || out_dtype == in_dtype,
-               "mb_gemm_tn: output must be float32 or the input type");
+               "mb_gemm: output must be float32 or the input type");
   MB_CHECK_ARG(bias == nullptr || bias_dtype == MB_F32 || bias_dtype == MB_BF16 ||
                    bias_dtype == MB_F16,
-               "mb_gemm_tn: bias must be float32, bfloat16 or float16");
-  MB_CHECK_ARG(M >= 0 && N >= 0 && K >= 0, "mb_gemm_tn: negative size");
+               "mb_gemm: bias must be float32, bfloat16 or float16");
+  MB_CHECK_ARG((a_major == MB_KMAJOR || a_major == MB_MNMAJOR) &&
+                   (b_major == MB_KMAJOR || b_major == MB_MNMAJOR),
+               "mb_gemm: unknown operand major");
+  MB_CHECK_ARG(!(a_major == MB_MNMAJOR && b_major == MB_KMAJOR),
+               "mb_gemm: an M-major A needs an N-major B");
+  MB_CHECK_ARG(M >= 0 && N >= 0 && K >= 0, "mb_gemm: negative size");
   if (M == 0 || N == 0) return 0;
-  MB_CHECK_ARG(K > 0, "mb_gemm_tn: K must be positive");
-  MB_CHECK_ARG(K % 8 == 0 && lda % 8 == 0 && ldb % 8 == 0 && lda >= K && ldb >= K,
-               "mb_gemm_tn: K and leading dimensions must be multiples of 8 (16-byte rows)");
-  MB_CHECK_ARG(aligned_to(A, 16) && aligned_to(B, 16), "mb_gemm_tn: A and B must be 16-byte aligned");
-  MB_CHECK_ARG(ldc >= N, "mb_gemm_tn: ldc < N");
-  MB_CHECK_ARG(M < (int64_t(1) << 31) && N < (int64_t(1) << 31), "mb_gemm_tn: M or N too large");
+  MB_CHECK_ARG(K > 0, "mb_gemm: K must be positive");
+  MB_CHECK_ARG(M < (int64_t(1) << 31) && N < (int64_t(1) << 31) && K < (int64_t(1) << 31),
+               "mb_gemm: M, N or K too large");
+  MB_CHECK_ARG(ldc >= N, "mb_gemm: ldc < N");
+  MB_CHECK_ARG(C != nullptr, "mb_gemm: null C");
+  const Operand a{A, lda, a_part_stride, a_parts, a_major == MB_MNMAJOR};
+  const Operand b{B, ldb, b_part_stride, b_parts, b_major == MB_MNMAJOR};
+  if (!operand_ok(a, M, K, "A") || !operand_ok(b, N, K, "B")) return 1;
+
   const int64_t out_elt = out_dtype == MB_F32 ? 4 : 2;
-  GemmArgs args{bias, C, ldc, M, N, K, bias_dtype,
-                (ldc * out_elt) % 16 == 0 && aligned_to(C, 16) ? 1 : 0, 0};
+  GemmArgs args{};
+  args.bias = bias;
+  args.C = C;
+  args.ldc = ldc;
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.bias_dtype = bias_dtype;
+  args.vec_ok = (ldc * out_elt) % 16 == 0 && aligned_to(C, 16) ? 1 : 0;
+  args.a_nonzero = a_nonzero;
+  args.b_nonzero = b_nonzero;
+  // (A part i, B part j) products with i + j <= 2: part p of a 3-way split
+  // carries the bits 8p below the leading ones, so the dropped products sit
+  // under 2^-24 of the result (bf16x6 for two 3-way split fp32 operands)
+  args.nseg = 0;
+  for (int order = 0; order <= 2; ++order) {
+    for (int i = 0; i <= order; ++i) {
+      const int j = order - i;
+      if (i < a_parts && j < b_parts) {
+        args.seg_a[args.nseg] = static_cast<int8_t>(i);
+        args.seg_b[args.nseg] = static_cast<int8_t>(j);
+        ++args.nseg;
+      }
+    }
+  }
   cudaStream_t s = as_stream(stream);
   int rc;
   if (in_dtype == MB_BF16) {
-    rc = out_dtype == MB_F32 ? launch_bn<__nv_bfloat16, float>(A, lda, B, ldb, args, out_dtype, s)
-                             : launch_bn<__nv_bfloat16, __nv_bfloat16>(A, lda, B, ldb, args, out_dtype, s);
+    rc = out_dtype == MB_F32 ? launch_typed<__nv_bfloat16, float>(a, b, args, out_dtype, s)
+                             : launch_typed<__nv_bfloat16, __nv_bfloat16>(a, b, args, out_dtype, s);
   } else {
-    rc = out_dtype == MB_F32 ? launch_bn<__half, float>(A, lda, B, ldb, args, out_dtype, s)
-                             : launch_bn<__half, __half>(A, lda, B, ldb, args, out_dtype, s);
+    rc = out_dtype == MB_F32 ? launch_typed<__half, float>(a, b, args, out_dtype, s)
+                             : launch_typed<__half, __half>(a, b, args, out_dtype, s);
   }
   if (rc != 0) return rc;
-  MB_CHECK_LAUNCH("mb_gemm_tn");
+  MB_CHECK_LAUNCH("mb_gemm");
   return 0;
+}
+
+extern "C" int mb_gemm_tn(int in_dtype, const void* A, int64_t lda, const void* B, int64_t ldb,
+                          const void* bias, int bias_dtype, int out_dtype, void* C, int64_t ldc,
+                          int64_t M, int64_t N, int64_t K, void* stream) {
+  return mb_gemm(in_dtype, A, MB_KMAJOR, lda, 0, 1, nullptr, B, MB_KMAJOR, ldb, 0, 1, nullptr,
+                 bias, bias_dtype, out_dtype, C, ldc, M, N, K, stream);
 }
 
 namespace mb {

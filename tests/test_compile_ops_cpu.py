@@ -19,7 +19,8 @@ import myelin_b200 as mb
 from myelin_b200 import _native as nat
 from myelin_b200 import compile_ops as cops
 
-OP_NAMES = ("scan_forward", "scan_backward", "gemm_tn", "pack_spikes", "unpack_spikes",
+OP_NAMES = ("scan_forward", "scan_backward", "gemm_tn", "linear_project", "linear_input_grad",
+            "linear_weight_grad", "pack_spikes", "unpack_spikes",
             "count_rows", "count_columns", "pack_count_spikes", "izhikevich_forward")
 
 
@@ -88,10 +89,10 @@ def test_linear_stream_forward_traces_to_gemm_and_scan():
     x, w, b = _fake(((8, 4, 32), torch.bfloat16), ((32, 48), torch.bfloat16),
                     ((48,), torch.bfloat16))
     gm, ops = _traced_ops(f, x, w, b)
-    assert ops == {"gemm_tn", "scan_forward"}
+    assert ops == {"linear_project", "scan_forward"}
 
 
-def test_fp32_linear_keeps_library_gemm():
+def test_fp32_linear_traces_to_tensor_core_projection():
     params = mb.LIFParams(tau_mem=20.0)
 
     def f(x, w, b):
@@ -100,7 +101,8 @@ def test_fp32_linear_keeps_library_gemm():
     x, w, b = _fake(((8, 4, 32), torch.float32), ((32, 48), torch.float32),
                     ((48,), torch.float32))
     _, ops = _traced_ops(f, x, w, b)
-    assert ops == {"scan_forward"}  # fp32 projection: cuBLAS through torch (exact fp32)
+    # fp32 projection: exact 3-way bf16 splits on the library's GEMM, no torch matmul
+    assert ops == {"linear_project", "scan_forward"}
 
 
 @pytest.mark.parametrize("neuron", [nat.MB_LIF, nat.MB_ALIF])

@@ -74,7 +74,9 @@ def test_config2_shape_flip_rate_and_gradients(oracle):
     state, spikes = mb.linear_surrogate_lif_forward(xd, wd, bd, params, surrogate="fast_sigmoid",
                                                     surrogate_slope=25.0)
     # oracle on the GPU's own currents: the scan must be bit-exact on identical inputs
-    cur = torch.addmm(bd.detach(), xd.detach().reshape(T * B, F), wd.detach()).reshape(T, B, N)
+    from myelin_b200.autograd import _project
+
+    cur = _project(xd.detach().reshape(T * B, F), wd.detach(), bd.detach()).reshape(T, B, N)
     kw = dict(decay=np.float32(1 - 1 / 20.0), threshold=np.float32(1.0), reset=np.float32(0.0))
     ref = oracle.scan_forward(host(cur), np.zeros((B, N), np.float32), **kw)
     assert np.array_equal(host(spikes).astype(np.uint8), ref["spikes"])
@@ -88,9 +90,14 @@ def test_config2_shape_flip_rate_and_gradients(oracle):
     bwd = oracle.scan_backward(host(cur), np.zeros((B, N), np.float32), grad_spikes=gs.numpy(),
                                surrogate="fast_sigmoid", slope=25.0, **kw)
     dx, dw, db = oracle.linear_backward(x.numpy(), w.numpy(), bwd["grad_x"])
-    assert_close_scaled(host(xd.grad), dx, rtol=1e-4, what="grad_x")
-    assert_close_scaled(host(wd.grad), dw, rtol=1e-4, what="grad_w")
-    assert_close_scaled(host(bd.grad), db, rtol=1e-4, what="grad_b")
+    # the north star's fp32 bar (1e-5), with the scaled floor of assert_close_scaled
+    assert_close_scaled(host(xd.grad), dx, rtol=1e-5, what="grad_x")
+    assert_close_scaled(host(wd.grad), dw, rtol=1e-5, what="grad_w")
+    assert_close_scaled(host(bd.grad), db, rtol=1e-5, what="grad_b")
+    # and the plain elementwise rtol 1e-5 pass rate, reported next to it
+    for name, got, want in (("grad_x", host(xd.grad), dx), ("grad_w", host(wd.grad), dw)):
+        rate = float(np.mean(np.abs(got - want) <= 1e-5 * np.abs(want) + 1e-30))
+        print(f"{name}: plain rtol 1e-5 pass rate {rate:.6f}")
 
 
 def test_packed_forward_matches_dense_forward():

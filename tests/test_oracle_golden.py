@@ -231,3 +231,32 @@ def test_izhikevich_oracle_matches_reference_golden(oracle, name):
     assert np.array_equal(oracle.pack(spikes), g["packed"])
     assert np.array_equal(vT, g["vT"])
     assert np.array_equal(uT, g["uT"])
+
+
+def test_torch_path_port_matches_reference_fixture():
+    """The torch restatement that bench.py times as myelin's torch CPU path
+    (oracle/torch_path.py) computes what the reference's loop computes: same
+    spikes, final state and autograd gradients as the fixture made with the
+    reference's own ``hard_surrogate_spike`` and atan surrogate."""
+
+    from oracle import torch_path
+
+    g = load_golden("alif_subtract_atan")
+    x = torch.from_numpy(g["x"]).requires_grad_(True)
+    v0 = torch.from_numpy(g["v0"]).requires_grad_(True)
+    a0 = torch.from_numpy(g["a0"]).requires_grad_(True)
+    m, a, spikes = torch_path.alif_atan_unroll(
+        x, v0, a0, decay=1.0 - 1.0 / float(g["tau_mem"]), threshold=float(g["threshold"]),
+        beta=float(g["beta"]), adaptation_decay=1.0 - 1.0 / float(g["tau_adaptation"]),
+        reset=float(g["reset"]), slope=float(g["slope"]), subtract=True)
+    from oracle import oracle as o
+
+    assert np.array_equal(o.pack(spikes.detach().numpy()), g["packed"])
+    np.testing.assert_allclose(m.detach().numpy(), g["vT"], rtol=0, atol=1e-6)
+    np.testing.assert_allclose(a.detach().numpy(), g["aT"], rtol=0, atol=1e-6)
+    loss = ((spikes * torch.from_numpy(g["grad_spikes"])).sum()
+            + (m * torch.from_numpy(g["grad_vT"])).sum() + (a * torch.from_numpy(g["grad_aT"])).sum())
+    gx, gv0, ga0 = torch.autograd.grad(loss, (x, v0, a0))
+    assert_close_scaled(gx.numpy(), g["grad_x"], what="grad_x")
+    assert_close_scaled(gv0.numpy(), g["grad_v0"], what="grad_v0")
+    assert_close_scaled(ga0.numpy(), g["grad_a0"], what="grad_a0")
