@@ -228,6 +228,11 @@ enum mb_major { MB_KMAJOR = 0, MB_MNMAJOR = 1 };
  * products of an all-zero part on the device. Leading dimensions: multiples
  * of 8; K-major also needs K % 8 == 0 and ld >= K; MN-major ld >= M (or N).
  * Bases 16-byte aligned. Out-of-range elements of the tiles read as zero.
+ * fp32 output from split operands is accumulated in K slices of at most 2048
+ * (the tensor cores' fp32 accumulation of one MMA is not correctly rounded, so
+ * its error grows with the MMAs summed into one accumulator), each slice into
+ * `workspace` (mb_gemm_workspace_bytes; nullable when that is 0), and the
+ * slices are then summed in order in fp32: deterministic.
  * Used for the stream synapse's currents x[T*B, F] * W[F, N] (B = W N-major,
  * no transposed copy), input gradient G * W^T (both K-major) and weight
  * gradient x^T G (A = x M-major, B = G N-major; no transposes).
@@ -239,7 +244,12 @@ int mb_gemm(int in_dtype, const void* A, int a_major, int64_t lda, int64_t a_par
             int a_parts, const int32_t* a_nonzero, const void* B, int b_major, int64_t ldb,
             int64_t b_part_stride, int b_parts, const int32_t* b_nonzero, const void* bias,
             int bias_dtype, int out_dtype, void* C, int64_t ldc, int64_t M, int64_t N, int64_t K,
-            void* stream);
+            void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Workspace (bytes) mb_gemm needs for these sizes, part counts and output type
+ * (0 unless fp32 output from split operands runs in K slices). */
+int64_t mb_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int a_parts, int b_parts,
+                                int out_dtype);
 
 /*
  * Split src[rows, cols] (element (r, c) at r * src_row_stride + c *

@@ -68,8 +68,9 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "mb_gemm": (
         _int, [_int, _vp, _int, _i64, _i64, _int, _vp, _vp, _int, _i64, _i64, _int, _vp, _vp,
-               _int, _int, _vp, _i64, _i64, _i64, _i64, _vp]
+               _int, _int, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _vp]
     ),
+    "mb_gemm_workspace_bytes": (_i64, [_i64, _i64, _i64, _int, _int, _int]),
     "mb_split_bf16": (
         _int, [_int, _vp, _i64, _i64, _i64, _i64, _int, _vp, _i64, _i64, _i64, _i64, _vp, _vp]
     ),
@@ -297,12 +298,15 @@ def gemm(a: GemmOperand, b: GemmOperand, M: int, N: int, K: int, out: torch.Tens
     """out[M, N] = sum over kept part pairs of A_i[M, K] B_j[N, K]^T (+ bias) (``mb_gemm``)."""
 
     dev = a.tensor.device
+    need = int(lib().mb_gemm_workspace_bytes(M, N, K, a.parts, b.parts, dtype_code(out.dtype)))
+    ws = torch.empty(need // 4, dtype=torch.float32, device=dev) if need > 0 else None
     with torch.cuda.device(dev):
         status = lib().mb_gemm(
             dtype_code(a.tensor.dtype), ptr(a.tensor), a.major, a.ld, a.part_stride, a.parts,
             ptr(a.nonzero), ptr(b.tensor), b.major, b.ld, b.part_stride, b.parts,
             ptr(b.nonzero), ptr(bias), dtype_code(bias.dtype) if bias is not None else 0,
-            dtype_code(out.dtype), ptr(out), out.stride(0), M, N, K, stream_handle(dev),
+            dtype_code(out.dtype), ptr(out), out.stride(0), M, N, K, ptr(ws), need,
+            stream_handle(dev),
         )
     check(status, "mb_gemm")
     return out

@@ -58,6 +58,12 @@ struct GemmArgs {
   int8_t seg_b[kMaxSegments];
   const int32_t* a_nonzero;
   const int32_t* b_nonzero;
+  // Split K: each output tile is computed as k_slices independent partial
+  // sums (k-blocks [s * kb_per_slice, (s + 1) * kb_per_slice) for slice s),
+  // written as fp32 to slice s of C = a [k_slices, M, ldc] workspace (no
+  // bias); a second kernel sums the slices in order. k_slices == 1: plain.
+  int k_slices;
+  int kb_per_slice;
 };
 
 // Which segments this launch runs (bit q = segment q); read once per thread
@@ -89,6 +95,16 @@ struct Layout {
 // ---------------------------------------------------------------------------
 // PTX wrappers
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0,
+                                             int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(c0), "r"(c1), "r"(c2), "r"(smem_addr(src))
+      : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0,
                                              int c1) {
   asm volatile(
@@ -348,19 +364,22 @@ __device__ __forceinline__ void stage_row32(uint8_t* slot, int r, const float (&
 // taddr's quarter, columns b*BN ..) -> bias add in fp32 -> one rounding to TOut
 // -> global memory, either staged in swizzled shared memory and written with
 // bulk tensor stores (tma_store) or with direct row stores. TMEM loads are
-// double-buffered: chunk ci+1 loads while chunk ci is converted.
+// double-buffered: chunk ci+1 loads while chunk ci is converted. With split K
+// (args.k_slices > 1) the tile goes to slice `slice` of the fp32 workspace
+// (a 3-D tensor map over [k_slices, M, ldc]).
 template <typename TOut, int BN>
 __device__ __forceinline__ void drain_tile(uint32_t tbase, int64_t row0, int64_t col_tile0,
                                            int lane, const GemmArgs& args,
                                            const CUtensorMap* tma_c, uint8_t* slots,
-                                           uint32_t& nstore) {
+                                           uint32_t& nstore, int slice) {
   constexpr int kSlotBytes = 32 * 32 * int(sizeof(TOut));
   constexpr int kSlots = 2 * (32 * 32 * 4) / kSlotBytes;  // 2 (fp32) or 4 (16-bit)
   const bool has_bias = args.bias != nullptr;
   const bool vec_ok = args.vec_ok != 0;
   const bool use_tma = args.tma_store != 0;
   const int64_t row = row0 + lane;
-  TOut* crow = static_cast<TOut*>(args.C) + row * args.ldc;
+  const bool sliced = args.k_slices > 1;
+  TOut* crow = static_cast<TOut*>(args.C) + (row + (sliced ? slice * args.M : 0)) * args.ldc;
   uint32_t r[2][32];
   tmem_ld32_issue(tbase, r[0]);
 #pragma unroll
@@ -390,7 +409,10 @@ __device__ __forceinline__ void drain_tile(uint32_t tbase, int64_t row0, int64_t
       stage_row32<TOut>(slot, lane, v);
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) tma_store_2d(tma_c, slot, static_cast<int>(col0), static_cast<int>(row0));
+      if (lane == 0) {
+        if (sliced) tma_store_3d(tma_c, slot, static_cast<int>(col0), static_cast<int>(row0), slice);
+        else tma_store_2d(tma_c, slot, static_cast<int>(col0), static_cast<int>(row0));
+      }
       ++nstore;
     } else if (row < args.M) {
       store_row32<TOut>(crow + col0, v, valid, vec_ok);
@@ -420,6 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t m_tiles = (args.M + kBM - 1) / kBM;
   const int64_t n_tiles = (args.N + BN - 1) / BN;
   const int64_t tiles = m_tiles * n_tiles;
+  const int64_t units = tiles * args.k_slices;  // (tile, K slice) work units
   const int kblocks = static_cast<int>((args.K + kBK - 1) / kBK);
 
   if (threadIdx.x == 0) {
@@ -450,12 +473,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0;
       bool ok = true;
       const uint32_t segs = segment_mask(args);
-      for (int64_t tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+      for (int64_t unit = blockIdx.x; unit < units && ok; unit += gridDim.x) {
+        const int64_t tile = unit / args.k_slices;
+        const int kb0 = static_cast<int>(unit % args.k_slices) * args.kb_per_slice;
+        const int kb1 = min(kblocks, kb0 + args.kb_per_slice);
         const int64_t tm = tile / n_tiles;
         const int64_t tn = tile % n_tiles;
-        for (int q = 0; q < args.nseg && ok; ++q) {
+        // smallest products first: they are summed while the accumulator is small
+        for (int q = args.nseg - 1; q >= 0 && ok; --q) {
           if (((segs >> q) & 1u) == 0) continue;
-          for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          for (int kb = kb0; kb < kb1; ++kb, ++it) {
             const int s = static_cast<int>(it % kStages);
             const uint32_t use = it / kStages;
             if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1)) {
@@ -484,16 +511,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t segs = segment_mask(args);
       uint32_t it = 0, local = 0;
       bool ok = true;
-      for (int64_t tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++local) {
+      for (int64_t unit = blockIdx.x; unit < units && ok; unit += gridDim.x, ++local) {
+        const int kb0 = static_cast<int>(unit % args.k_slices) * args.kb_per_slice;
+        const int kb1 = min(kblocks, kb0 + args.kb_per_slice);
         const uint32_t b = local & 1;
         const uint32_t use_b = local >> 1;
         if (use_b > 0 && !mbar_wait_bounded(&acc_empty[b], (use_b - 1) & 1)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + b * BN;
         bool acc = false;  // the tile's first MMA overwrites the accumulator
-        for (int q = 0; q < args.nseg && ok; ++q) {
+        for (int q = args.nseg - 1; q >= 0 && ok; --q) {
           if (((segs >> q) & 1u) == 0) continue;
-          for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          for (int kb = kb0; kb < kb1; ++kb, ++it) {
             const int s = static_cast<int>(it % kStages);
             if (!mbar_wait_bounded(&full[s], (it / kStages) & 1)) {
               ok = false;
@@ -524,15 +553,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* slots = sepi + (warp - 2) * 2 * L::kEpiSlotBytes;
     uint32_t nstore = 0;
     uint32_t local = 0;
-    for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
+    for (int64_t unit = blockIdx.x; unit < units; unit += gridDim.x, ++local) {
       const uint32_t b = local & 1;
       if (!mbar_wait_bounded(&acc_full[b], (local >> 1) & 1)) break;
       tc_fence_after();
+      const int64_t tile = unit / args.k_slices;
       const int64_t tm = tile / n_tiles;
       const int64_t tn = tile % n_tiles;
       drain_tile<TOut, BN>(tmem_base + (uint32_t(quarter * 32) << 16) + b * BN,
                            tm * kBM + quarter * 32, tn * BN, lane, args, &tma_c, slots,
-                           nstore);
+                           nstore, static_cast<int>(unit % args.k_slices));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
@@ -690,6 +720,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
   const int64_t m_tiles = (args.M + k2BM - 1) / k2BM;
   const int64_t n_tiles = (args.N + k2BN - 1) / k2BN;
   const int64_t tiles = m_tiles * n_tiles;
+  const int64_t units = tiles * args.k_slices;  // (tile, K slice) work units
   const int kblocks = static_cast<int>((args.K + kBK - 1) / kBK);
 
   if (threadIdx.x == 0) {
@@ -720,12 +751,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
       uint32_t it = 0;
       bool ok = true;
       const uint32_t segs = segment_mask(args);
-      for (int64_t tile = pair; tile < tiles && ok; tile += pairs) {
+      for (int64_t unit = pair; unit < units && ok; unit += pairs) {
+        const int64_t tile = unit / args.k_slices;
+        const int kb0 = static_cast<int>(unit % args.k_slices) * args.kb_per_slice;
+        const int kb1 = min(kblocks, kb0 + args.kb_per_slice);
         const int64_t tm = tile / n_tiles;
         const int64_t tn = tile % n_tiles;
-        for (int q = 0; q < args.nseg && ok; ++q) {
+        for (int q = args.nseg - 1; q >= 0 && ok; --q) {
           if (((segs >> q) & 1u) == 0) continue;
-          for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          for (int kb = kb0; kb < kb1; ++kb, ++it) {
             const int s = static_cast<int>(it % k2Stages);
             const uint32_t use = it / k2Stages;
             if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1)) {
@@ -757,16 +791,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
       const uint32_t segs = segment_mask(args);
       uint32_t it = 0, local = 0;
       bool ok = true;
-      for (int64_t tile = pair; tile < tiles && ok; tile += pairs, ++local) {
+      for (int64_t unit = pair; unit < units && ok; unit += pairs, ++local) {
+        const int kb0 = static_cast<int>(unit % args.k_slices) * args.kb_per_slice;
+        const int kb1 = min(kblocks, kb0 + args.kb_per_slice);
         const uint32_t b = local & 1;
         const uint32_t use_b = local >> 1;
         if (use_b > 0 && !mbar_wait_bounded(&acc_empty[b], (use_b - 1) & 1)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + b * k2BN;
         bool acc = false;  // the tile's first MMA overwrites the accumulator
-        for (int q = 0; q < args.nseg && ok; ++q) {
+        for (int q = args.nseg - 1; q >= 0 && ok; --q) {
           if (((segs >> q) & 1u) == 0) continue;
-          for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          for (int kb = kb0; kb < kb1; ++kb, ++it) {
             const int s = static_cast<int>(it % k2Stages);
             if (!mbar_wait_bounded(&full[s], (it / k2Stages) & 1)) {
               ok = false;
@@ -803,16 +839,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
     uint8_t* slots = sepi + (warp - 2) * 2 * L::kEpiSlotBytes;
     uint32_t nstore = 0;
     uint32_t local = 0;
-    for (int64_t tile = pair; tile < tiles; tile += pairs, ++local) {
+    for (int64_t unit = pair; unit < units; unit += pairs, ++local) {
       const uint32_t b = local & 1;
       if (!mbar_wait_bounded(&acc_full[b], (local >> 1) & 1)) break;
       tc_fence_after();
+      const int64_t tile = unit / args.k_slices;
       const int64_t tm = tile / n_tiles;
       const int64_t tn = tile % n_tiles;
       drain_tile<TOut, k2BN / 2>(
           tmem_base + (uint32_t(quarter * 32) << 16) + b * k2BN + half * (k2BN / 2),
           tm * k2BM + int64_t(rank) * 128 + quarter * 32, tn * k2BN + half * (k2BN / 2), lane,
-          args, &tma_c, slots, nstore);
+          args, &tma_c, slots, nstore, static_cast<int>(unit % args.k_slices));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(cluster_addr(smem_addr(&acc_empty[b]), 0));
@@ -890,6 +927,63 @@ bool make_c_map(CUtensorMap* map, void* ptr, int64_t M, int64_t N, int64_t ldc, 
   return r == CUDA_SUCCESS;
 }
 
+// 3-D map over the split-K workspace [k_slices, M, ldc] of fp32 partial sums
+// for the epilogue's bulk tensor stores (box 32 x 32 x 1, 128-byte swizzle).
+bool make_slices_map(CUtensorMap* map, void* ptr, int64_t M, int64_t N, int64_t ldc, int slices) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  if (!aligned_to(ptr, 16) || (ldc * 4) % 16 != 0) return false;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M),
+                        static_cast<cuuint64_t>(slices)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ldc * 4), static_cast<cuuint64_t>(M * ldc * 4)};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estride[3] = {1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, ptr, dims, strides, box, estride,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// Sum of the split-K partial sums in slice order (+ bias), one rounding to TOut.
+template <typename TOut>
+__global__ void slices_reduce_kernel(const float* __restrict__ partial, int slices, int64_t M,
+                                     int64_t N, int64_t pld, const void* bias, int bias_dtype,
+                                     TOut* __restrict__ C, int64_t ldc) {
+  const int64_t total = M * N;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t m = i / N;
+    const int64_t n = i - m * N;
+    float acc = 0.0f;
+    for (int sl = 0; sl < slices; ++sl) acc += partial[(sl * M + m) * pld + n];
+    if (bias != nullptr) {
+      if (bias_dtype == MB_F32) acc += static_cast<const float*>(bias)[n];
+      else if (bias_dtype == MB_BF16) acc += __bfloat162float(static_cast<const __nv_bfloat16*>(bias)[n]);
+      else acc += __half2float(static_cast<const __half*>(bias)[n]);
+    }
+    C[m * ldc + n] = Elem<TOut>::from_f(acc);
+  }
+}
+
+// K slices for a launch: fp32 output from split (fp32) operands is summed in
+// slices of at most kSliceKBlocks k-blocks. The tensor cores' fp32
+// accumulation of each MMA is not correctly rounded, so its error grows with
+// the number of MMAs summed into one accumulator; slices bound that count and
+// are added in fp32 (correctly rounded) afterwards.
+constexpr int kSliceKBlocks = 32;  // K = 2048 per slice
+
+int k_slices_for(int64_t K, int a_parts, int b_parts, int out_dtype, int* kb_per_slice) {
+  const int kblocks = static_cast<int>((K + kBK - 1) / kBK);
+  *kb_per_slice = kblocks;
+  if (out_dtype != MB_F32 || (a_parts == 1 && b_parts == 1) || kblocks <= kSliceKBlocks) return 1;
+  int slices = (kblocks + kSliceKBlocks - 1) / kSliceKBlocks;
+  const int per = (kblocks + slices - 1) / slices;
+  *kb_per_slice = per;
+  return (kblocks + per - 1) / per;
+}
+
+int64_t slices_pld(int64_t N) { return (N + 3) / 4 * 4; }
+
 int sm_count() {
   int dev = 0, n = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
@@ -944,7 +1038,11 @@ int launch_majors(const Operand& A, const Operand& B, GemmArgs args, int out_dty
   const bool bf16 = std::is_same<TIn, __nv_bfloat16>::value;
   CUtensorMap ma, mbm, mc;
   memset(&mc, 0, sizeof(mc));
-  args.tma_store = make_c_map(&mc, args.C, args.M, args.N, args.ldc, out_dtype) ? 1 : 0;
+  args.tma_store = (args.k_slices > 1
+                        ? make_slices_map(&mc, args.C, args.M, args.N, args.ldc, args.k_slices)
+                        : make_c_map(&mc, args.C, args.M, args.N, args.ldc, out_dtype))
+                       ? 1
+                       : 0;
   if (use_pair(args, args.K * args.nseg, out_dtype == MB_F32)) {
     // both operand maps: each CTA's 128 rows (K-major) / 64-wide blocks (MN-major)
     if (!make_operand_map(&ma, A, args.M, args.K, 128, bf16) ||
@@ -1007,11 +1105,20 @@ bool operand_ok(const Operand& op, int64_t mn, int64_t K, const char* name) {
 
 using namespace mb;
 
+extern "C" int64_t mb_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int a_parts,
+                                           int b_parts, int out_dtype) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  int per = 0;
+  const int slices = k_slices_for(K, a_parts, b_parts, out_dtype, &per);
+  return slices > 1 ? int64_t(slices) * M * slices_pld(N) * int64_t(sizeof(float)) : 0;
+}
+
 extern "C" int mb_gemm(int in_dtype, const void* A, int a_major, int64_t lda, int64_t a_part_stride,
                        int a_parts, const int32_t* a_nonzero, const void* B, int b_major,
                        int64_t ldb, int64_t b_part_stride, int b_parts, const int32_t* b_nonzero,
                        const void* bias, int bias_dtype, int out_dtype, void* C, int64_t ldc,
-                       int64_t M, int64_t N, int64_t K, void* stream) {
+                       int64_t M, int64_t N, int64_t K, void* workspace, int64_t workspace_bytes,
+                       void* stream) {
   clear_error();
   MB_CHECK_ARG(in_dtype == MB_BF16 || in_dtype == MB_F16,
                "mb_gemm: inputs must be bfloat16 or float16 (got dtype %d)", in_dtype);
@@ -1063,7 +1170,30 @@ extern "C" int mb_gemm(int in_dtype, const void* A, int a_major, int64_t lda, in
     }
   }
   cudaStream_t s = as_stream(stream);
+  args.k_slices = k_slices_for(K, a_parts, b_parts, out_dtype, &args.kb_per_slice);
   int rc;
+  if (args.k_slices > 1) {
+    // fp32 partial sums per K slice into the workspace, then their ordered sum
+    const int64_t pld = slices_pld(N);
+    const int64_t need = int64_t(args.k_slices) * M * pld * int64_t(sizeof(float));
+    MB_CHECK_ARG(workspace != nullptr && workspace_bytes >= need && aligned_to(workspace, 16),
+                 "mb_gemm: workspace of %lld bytes (16-byte aligned) required, got %lld",
+                 (long long)need, (long long)workspace_bytes);
+    GemmArgs part = args;
+    part.C = workspace;
+    part.ldc = pld;
+    part.bias = nullptr;
+    part.vec_ok = 1;
+    rc = in_dtype == MB_BF16 ? launch_typed<__nv_bfloat16, float>(a, b, part, MB_F32, s)
+                             : launch_typed<__half, float>(a, b, part, MB_F32, s);
+    if (rc != 0) return rc;
+    const unsigned grid = static_cast<unsigned>(imin64(ceil_div(M * N, 256), 148 * 8));
+    slices_reduce_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(workspace),
+                                                     args.k_slices, M, N, pld, bias, bias_dtype,
+                                                     static_cast<float*>(C), ldc);
+    MB_CHECK_LAUNCH("mb_gemm");
+    return 0;
+  }
   if (in_dtype == MB_BF16) {
     rc = out_dtype == MB_F32 ? launch_typed<__nv_bfloat16, float>(a, b, args, out_dtype, s)
                              : launch_typed<__nv_bfloat16, __nv_bfloat16>(a, b, args, out_dtype, s);
@@ -1080,7 +1210,7 @@ extern "C" int mb_gemm_tn(int in_dtype, const void* A, int64_t lda, const void* 
                           const void* bias, int bias_dtype, int out_dtype, void* C, int64_t ldc,
                           int64_t M, int64_t N, int64_t K, void* stream) {
   return mb_gemm(in_dtype, A, MB_KMAJOR, lda, 0, 1, nullptr, B, MB_KMAJOR, ldb, 0, 1, nullptr,
-                 bias, bias_dtype, out_dtype, C, ldc, M, N, K, stream);
+                 bias, bias_dtype, out_dtype, C, ldc, M, N, K, nullptr, 0, stream);
 }
 
 namespace mb {

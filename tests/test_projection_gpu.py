@@ -94,6 +94,21 @@ def test_fp32_projections_split_into_bf16_parts(M, F, N):
            "dW (real input)")
 
 
+def test_fp32_weight_gradient_over_long_k_runs_in_slices():
+    """K = T*B = 51200 (config-5 rows) in fp32: 25 K slices summed in order;
+    the bar is the same 1e-5 (scaled) against float64."""
+
+    lib = nat.lib()
+    M, F, N = 51200, 64, 96
+    assert lib.mb_gemm_workspace_bytes(F, N, M, 3, 3, nat.MB_F32) > 0
+    assert lib.mb_gemm_workspace_bytes(F, N, M, 1, 1, nat.MB_F32) == 0
+    gen = torch.Generator(device=DEV).manual_seed(13)
+    x = _rand((M, F), gen)
+    g = _rand((M, N), gen, scale=0.01)
+    _check(projection.weight_grad(x, g, torch.float32), x.double().t() @ g.double(), 1e-5,
+           "dW over K = 51200")
+
+
 def test_split_parts_sum_exactly_and_flag_nonzero_parts():
     gen = torch.Generator(device=DEV).manual_seed(11)
     src = torch.randn((37, 45), generator=gen, device=DEV) * 3.0
@@ -130,7 +145,7 @@ def test_mb_gemm_rejects_m_major_a_with_k_major_b():
     c = torch.zeros((64, 64), dtype=torch.float32, device=DEV)
     rc = lib.mb_gemm(nat.MB_BF16, a.data_ptr(), nat.MB_MNMAJOR, 64, 0, 1, None, a.data_ptr(),
                      nat.MB_KMAJOR, 64, 0, 1, None, None, 0, nat.MB_F32, c.data_ptr(), 64, 64, 64,
-                     64, None)
+                     64, None, 0, None)
     assert rc != 0 and "M-major A" in lib.mb_last_error().decode()
 
 
