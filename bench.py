@@ -262,6 +262,7 @@ def run_gpu(args) -> None:
         barrier(world)
         torch.cuda.synchronize()
         start.record(stream)
+        t_host = time.perf_counter()
         for k in range(args.steps):
             e0, e1, e2 = ev[k]
             e0.record(stream)
@@ -270,6 +271,9 @@ def run_gpu(args) -> None:
             torch.autograd.grad(spikes, x, gs)
             e2.record(stream)
         stop.record(stream)
+        # host time to issue the steps: at or above the device time per step,
+        # the eager step is bound by the host's per-call work
+        host_ms = (time.perf_counter() - t_host) * 1e3 / args.steps
         torch.cuda.synchronize()
         barrier(world)
     total_ms = max_over_ranks(start.elapsed_time(stop), world)
@@ -357,6 +361,7 @@ def run_gpu(args) -> None:
         "gpu_launches": 2 * args.steps,
         "device_status": status,
         "graph_replay": graph,
+        "host_issue_ms_per_step": round(host_ms, 4),
     }
     clk = clocks.summary()
     if clk is not None:
@@ -672,9 +677,11 @@ def run_network(args, world, rank, local) -> None:
     ms = max_over_ranks(start.elapsed_time(stop), world) / args.steps
     units = T * B * neurons
     flops = 0
-    for layer in model:
+    for index, layer in enumerate(model):
         fi, fo = layer.synapse.weight.shape
-        flops += 2 * T * B * fi * fo * 3  # forward projection, input grad, weight grad
+        # forward projection and weight gradient; the input gradient except for
+        # the first layer, whose input (the data) needs none
+        flops += 2 * T * B * fi * fo * (3 if index > 0 else 2)
     result = {
         "metric": "LIF/ALIF fwd+bwd neuron-timesteps/s (training step)",
         "value": units * world / (ms / 1e3), "unit": "neuron-steps/s", "n_gpus": world,
