@@ -267,11 +267,19 @@ __device__ __forceinline__ float rcp_approx(float x) {
 // Step, so membranes and spike decisions are bit-identical. It works with the
 // negated threshold nth = -theta (exact: fl(-thr + fl(-beta * a)) is
 // -fl(thr + fl(beta * a))), so that p - theta = p + nth needs no negation.
+//
+// The spike is also produced as a float 0/1 (sf, one set instruction per lane)
+// so that the subtractive reset is one packed fused multiply-add,
+// m = sf * nth + p: exactly fl(p + nth) = fl(p - theta) where sf = 1 and p
+// where sf = 0 (the only difference from a select: a membrane of -0 that does
+// not spike comes back as +0 when the threshold is negative; values compare
+// equal). The adaptation adds sf directly.
 template <int KIND, int RESET>
 struct Step2 {
   F2 p;     // pre-reset membranes
   F2 nth;   // minus the thresholds used this step
   F2 diff;  // p - theta (subtractive reset only)
+  F2 sf;    // spikes as 1.0f / 0.0f
   bool s0, s1;
   __device__ __forceinline__ void run(F2& m, F2& a, F2 x, const F2 decay, const F2 nthr,
                                       const float reset_v, const F2 adapt_decay,
@@ -280,14 +288,15 @@ struct Step2 {
     nth = (KIND == MB_ALIF) ? add2(nthr, mul2_exact(nbeta, a)) : nthr;
     s0 = p.x >= -nth.x;
     s1 = p.y >= -nth.y;
+    sf = f2(ge_f(p.x, -nth.x), ge_f(p.y, -nth.y));
     if (RESET == MB_RESET_HARD) {
       m = f2(s0 ? reset_v : p.x, s1 ? reset_v : p.y);
     } else {
       diff = add2(p, nth);
-      m = f2(s0 ? diff.x : p.x, s1 ? diff.y : p.y);
+      m = fma2(sf, nth, p);
     }
     if (KIND == MB_ALIF) {
-      a = add2(mul2_exact(a, adapt_decay), f2(s0 ? 1.0f : 0.0f, s1 ? 1.0f : 0.0f));
+      a = add2(mul2_exact(a, adapt_decay), sf);
     }
   }
 };

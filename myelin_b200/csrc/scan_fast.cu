@@ -1,16 +1,19 @@
 // Warp-specialized LIF/ALIF scan kernels for 16-byte-aligned [T, B*N] rows.
 //
-// CTA = kConsumerWarps compute warps + 1 copy warp. The copy warp streams the
-// CTA's tile (kTileN consecutive flat neurons) of every kChunk-step chunk into
-// a ring of shared-memory stages with 1-D bulk async copies (the TMA engine);
-// each stage has a "full" mbarrier (copy bytes landed) and an "empty" mbarrier
-// (every compute warp is done with it). Compute threads own two neighbouring
-// neurons each, so every smem read, global store and bf16 conversion moves a
-// pair. No CTA-wide barrier is taken after set-up.
+// CTA = kWarps compute warps over a tile of kTileN consecutive flat neurons
+// (two per thread). Every kChunk-step chunk of the tile travels through a
+// ring of shared-memory stages: one 2-D bulk tensor copy (TMA) per input
+// array brings a [kChunk x kTileN] box in, completing on the stage's "full"
+// mbarrier. There is no copy warp: the compute warp that finishes a stage
+// last (a counter per stage, acquire-release) writes it back (dense outputs,
+// one bulk tensor store) and refills it with the chunk RING steps ahead, so
+// every warp of the CTA computes and no CTA-wide barrier is taken after
+// set-up. Compute threads own two neighbouring neurons each, so every smem
+// read, global store and bf16 conversion moves a pair.
 //
 // Forward: the state is carried in fp32 registers; per step it writes dense
-// spikes (a pair per store) and/or packed words (two ballots interleaved into
-// two 32-neuron words per warp), and at each chunk start the fp32 checkpoint.
+// spikes (into the stage, over the inputs they came from) and/or packed words
+// and/or spike counts, and at each chunk start the fp32 checkpoint.
 // Backward: chunks run last to first; each is replayed from its checkpoint
 // into registers (bit-identical to the forward) and then walked in reverse.
 #include <climits>
@@ -26,15 +29,25 @@ namespace mb {
 
 namespace {
 
-constexpr int kConsumerWarps = 4;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kTileN = kConsumerWarps * 32 * 2;  // neurons per CTA
-constexpr int kFwdRing = 4;                      // stages (chunks) in flight, forward
-constexpr int kBwdRing = 3;                      // stages in flight, backward
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kTileN = kWarps * 32 * 2;  // neurons per CTA
+
+// Stages in flight and resident CTAs per SM (the register budget the kernel is
+// compiled for), per element type: the forward's stage is one input box, the
+// backward's two input boxes plus the chunk's fp32 checkpoints.
+// (Measured on B200 at BASELINE config 3, ALIF bf16: forward 5 stages x 5
+// CTAs 0.1068 ms against 4 x 6 0.1088 and 3 x 8 0.1108; backward 2 stages x
+// 4 CTAs 0.1398 against 3 x 4 0.1417 and 2 x 5 0.1434.)
+template <typename T>
+struct FwdCfg {
+  static constexpr int kRing = sizeof(T) == 2 ? 5 : 3;
+  static constexpr int kMinBlocks = sizeof(T) == 2 ? 5 : 4;
+};
 
 template <typename T>
-__host__ __device__ constexpr size_t fwd_smem() {
-  return size_t(kFwdRing) * kChunk * kTileN * sizeof(T) + 3 * kFwdRing * sizeof(uint64_t);
+__host__ __device__ constexpr size_t fwd_smem(int ring) {
+  return size_t(ring) * kChunk * kTileN * sizeof(T) + ring * (sizeof(uint64_t) + sizeof(uint32_t));
 }
 
 // Backward stage: kChunk rows of x, kChunk rows of grad_spikes, then the fp32
@@ -45,8 +58,13 @@ __host__ __device__ constexpr size_t bwd_stage_bytes() {
 }
 
 template <typename T>
-__host__ __device__ constexpr size_t bwd_smem() {
-  return size_t(kBwdRing) * bwd_stage_bytes<T>() + 3 * kBwdRing * sizeof(uint64_t);
+struct BwdCfg {
+  static constexpr int kRing = 2;
+};
+
+template <typename T>
+__host__ __device__ constexpr size_t bwd_smem(int ring) {
+  return size_t(ring) * bwd_stage_bytes<T>() + ring * (sizeof(uint64_t) + sizeof(uint32_t));
 }
 
 // Output modes of the forward (what the caller asked for), fixed at compile
@@ -58,10 +76,10 @@ enum BwdMode { kBwdSpikes = 0, kBwdRates = 1, kBwdAny = 2 };
 
 // Resident CTAs per SM the backward is compiled for (a register budget). LIF
 // fits 4 without spilling. ALIF (two state adjoints, two replayed states)
-// also runs at 4 for one gradient input: a small spill (24 bytes) costs less
-// than the occupancy lost at 3 (measured 0.155 vs 0.179 ms at config 3). With
-// both spike and rate gradients the spill grows past 100 bytes, so that mode
-// runs at 3; the exp-based surrogates (sigmoid, multi-Gaussian) hold more
+// also runs at 4 for one gradient input: a small spill costs less than the
+// occupancy lost at 3 (measured 0.155 vs 0.179 ms at config 3). With both
+// spike and rate gradients the spill grows past 100 bytes, so that mode runs
+// at 3; the exp-based surrogates (sigmoid, multi-Gaussian) hold more
 // temporaries and run at 2.
 constexpr int bwd_min_blocks(int kind, int surr, int mode) {
   return kind == MB_LIF ? 4
@@ -86,49 +104,43 @@ PairConsts pair_consts(float decay, float thr, float adapt_decay, float beta, fl
                     dup2(sd.k0), dup2(sd.k1), dup2(1.0f)};
 }
 
-template <typename T>
-__device__ __forceinline__ void queue_chunk_rows(T* dst, const T* src, int64_t t0, int len,
-                                                 int64_t BN, int64_t e0, uint32_t row_bytes,
-                                                 uint64_t* bar) {
-  for (int j = 0; j < len; ++j) {
-    bulk_copy_g2s(dst + j * kTileN, src + (t0 + j) * BN + e0, row_bytes, bar);
-  }
-}
-
-// A compute thread's part in writing a finished stage back to global memory.
-// Every compute thread orders its shared-memory writes for the async proxy;
-// each warp then arrives on `done`; thread 0 waits (bounded) for all warps,
-// issues one bulk tensor store of the stage at (c0, c1), waits until the
-// store has read the stage, and releases it on `empty` (count 1). Returns
-// false if the wait ran out (status recorded).
-__device__ __forceinline__ bool store_stage(const void* stage, uint64_t* done, uint64_t* empty,
-                                            int64_t use, int ring, const CUtensorMap* map,
-                                            int64_t c0, int64_t c1) {
+// Called by every compute thread when it is done with a stage (its reads of
+// the inputs and its writes of the outputs). Orders the thread's shared-memory
+// accesses before later async-proxy accesses (the store that reads the stage,
+// the copies that refill it), then counts the warp in on the stage's counter
+// with an acquire-release add at CTA scope. Returns true in lane 0 of the warp
+// that arrives last: every other warp's accesses to the stage happen before
+// what that lane does next. The last lane puts the counter back to 0 (before
+// any refill of the stage, whose completion the next users acquire).
+__device__ __forceinline__ bool last_warp_done(uint32_t* counter) {
   fence_proxy_async_smem();
   __syncwarp();
-  if ((threadIdx.x & 31) == 0) mbar_arrive(done);
-  if (threadIdx.x == 0) {
-    if (!mbar_wait_bounded(done, static_cast<uint32_t>((use / ring) & 1))) return false;
-    tma_store_box_2d(map, stage, static_cast<int>(c0), static_cast<int>(c1));
-    bulk_wait_read_all();
-    mbar_arrive(empty);
-  }
+  if ((threadIdx.x & 31) != 0) return false;
+  uint32_t old;
+  asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
+               : "=r"(old)
+               : "r"(smem_addr(counter))
+               : "memory");
+  if (old != kWarps - 1) return false;
+  *counter = 0;
   return true;
 }
 
 // ---------------------------------------------------------------------------
 // Forward
 // ---------------------------------------------------------------------------
-template <typename T, int KIND, int RESET, int MODE>
-__global__ void __launch_bounds__(kThreads, 6) scan_fwd_fast_kernel(
-    const ScanFwdArgs a, const PairConsts c, const __grid_constant__ CUtensorMap out_map) {
+template <typename T, int KIND, int RESET, int MODE, int RING, int MINB>
+__global__ void __launch_bounds__(kThreads, MINB) scan_fwd_fast_kernel(
+    const ScanFwdArgs a, const PairConsts c, const __grid_constant__ CUtensorMap in_map,
+    const __grid_constant__ CUtensorMap out_map) {
   using P = Pair<T>;
   using V = typename P::V;
+  constexpr int kRing = RING;
+  constexpr uint32_t kStageBytes = uint32_t(kChunk) * kTileN * sizeof(T);
   extern __shared__ __align__(128) unsigned char smem_raw[];
   T* ring = reinterpret_cast<T*>(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + size_t(kFwdRing) * kChunk * kTileN * sizeof(T));
-  uint64_t* empty = full + kFwdRing;
-  uint64_t* done = empty + kFwdRing;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + size_t(kRing) * kStageBytes);
+  uint32_t* done = reinterpret_cast<uint32_t*>(full + kRing);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -138,38 +150,25 @@ __global__ void __launch_bounds__(kThreads, 6) scan_fwd_fast_kernel(
   constexpr bool kDense = MODE == kFwdDense || MODE == kFwdAny;
   const bool do_dense = kDense && (MODE != kFwdAny || a.spikes != nullptr);
 
+  // chunk k into stage k % kRing: one box of kChunk rows x kTileN neurons
+  // (rows past T and neurons past B*N read as zero and are never used)
+  auto refill = [&](int64_t k) {
+    const int st = static_cast<int>(k % kRing);
+    mbar_arrive_expect_tx(&full[st], kStageBytes);
+    tma_load_box_2d(ring + size_t(st) * kChunk * kTileN, &in_map, static_cast<int>(e0),
+                    static_cast<int>(k * kChunk), &full[st]);
+  };
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kFwdRing; ++s) {
+    for (int s = 0; s < kRing; ++s) {
       mbar_init(&full[s], 1);
-      // with dense output the stage is released by the thread that stores it
-      mbar_init(&empty[s], do_dense ? 1 : kConsumerWarps);
-      mbar_init(&done[s], kConsumerWarps);
+      done[s] = 0;
     }
     fence_barrier_init();
+    for (int64_t k = 0; k < imin64(kRing, K); ++k) refill(k);
   }
   __syncthreads();
 
-  if (warp == kConsumerWarps) {
-    // copy warp: one lane streams every chunk of this tile through the ring
-    if (lane == 0) {
-      const T* x = static_cast<const T*>(a.x);
-      const uint32_t row_bytes = uint32_t(tile_n) * uint32_t(sizeof(T));
-      for (int64_t k = 0; k < K; ++k) {
-        const int s = static_cast<int>(k % kFwdRing);
-        if (k >= kFwdRing &&
-            !mbar_wait_bounded(&empty[s], static_cast<uint32_t>(((k / kFwdRing) - 1) & 1))) {
-          break;
-        }
-        const int64_t t0 = k * kChunk;
-        const int len = static_cast<int>(imin64(kChunk, a.T - t0));
-        mbar_arrive_expect_tx(&full[s], row_bytes * uint32_t(len));
-        queue_chunk_rows(ring + s * kChunk * kTileN, x, t0, len, a.BN, e0, row_bytes, &full[s]);
-      }
-    }
-    return;
-  }
-
-  const int tid = threadIdx.x;  // 0 .. 32*kConsumerWarps-1
+  const int tid = threadIdx.x;  // 0 .. kThreads - 1
   // Neurons of a thread: the adjacent pair e, e + 1 (e = e0 + 2 tid), so that
   // one vector access moves both; or, for packed output only (kSplit), lane l
   // of warp w owns neurons l and l + 32 of the warp's 64 (ea = e0 + 64 w + l,
@@ -204,10 +203,9 @@ __global__ void __launch_bounds__(kThreads, 6) scan_fwd_fast_kernel(
   constexpr bool kRates = MODE == kFwdRates || MODE == kFwdAny;
   const bool do_packed = kPacked && (MODE != kFwdAny || a.packed != nullptr);
   // Dense spikes overwrite the x values they came from in the stage (each
-  // thread its own pair); when all compute warps are done with a chunk, one
-  // thread writes the whole stage [16 rows x 256 neurons] with one bulk tensor
-  // store (clipped at the tensor's edges) and then releases the stage. The
-  // per-step global store and its address arithmetic disappear.
+  // thread its own pair); the warp that finishes the chunk last writes the
+  // whole stage [16 rows x 256 neurons] with one bulk tensor store (clipped
+  // at the tensor's edges) before refilling it.
   // packed words: this warp's 64 neurons are flat words q and q+1; with
   // N % 32 == 0 every word lies wholly inside or wholly outside the tile
   const int64_t words_per_t = a.BN >> 5;
@@ -227,6 +225,7 @@ __global__ void __launch_bounds__(kThreads, 6) scan_fwd_fast_kernel(
     if constexpr (KIND == kIzhikevich) {
       st.s0 = izh_step(m.x, ad.x, xf.x, izc);
       st.s1 = izh_step(m.y, ad.y, xf.y, izc);
+      st.sf = f2(st.s0 ? 1.0f : 0.0f, st.s1 ? 1.0f : 0.0f);
     } else {
       st.run(m, ad, f2(xf), decay, nthr, reset_v, adapt_decay, nbeta);
     }
@@ -234,7 +233,10 @@ __global__ void __launch_bounds__(kThreads, 6) scan_fwd_fast_kernel(
       c0 += st.s0 ? 1 : 0;
       c1 += st.s1 ? 1 : 0;
     }
-    if (kDense && (MODE != kFwdAny || do_dense)) *slot = P::spikes(st.s0, st.s1);
+    if (kDense && (MODE != kFwdAny || do_dense)) {
+      const float2 sf = split(st.sf);
+      *slot = P::from_f2(sf.x, sf.y);  // exact 0 / 1 in every I/O type
+    }
     if (kPacked && (MODE != kFwdAny || pk != nullptr)) {
       const uint32_t even = __ballot_sync(0xffffffffu, st.s0);
       const uint32_t odd = __ballot_sync(0xffffffffu, st.s1);
@@ -247,8 +249,8 @@ __global__ void __launch_bounds__(kThreads, 6) scan_fwd_fast_kernel(
   };
 
   for (int64_t k = 0; k < K; ++k) {
-    const int s = static_cast<int>(k % kFwdRing);
-    if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>((k / kFwdRing) & 1))) {
+    const int s = static_cast<int>(k % kRing);
+    if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>((k / kRing) & 1))) {
       bulk_wait_all();  // stores of earlier chunks finish before the early exit
       return;
     }
@@ -265,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, 6) scan_fwd_fast_kernel(
       reinterpret_cast<float2*>(a.ckpt_v + k * a.BN)[e >> 1] = split(m);
       if (kTwoStates) reinterpret_cast<float2*>(a.ckpt_a + k * a.BN)[e >> 1] = split(ad);
     }
-    T* stage = ring + s * kChunk * kTileN;
+    T* stage = ring + size_t(s) * kChunk * kTileN;
     V* row = reinterpret_cast<V*>(stage) + tid;
     const T* srow = stage + 64 * warp + lane;  // split layout: neurons l and l + 32
     const int len = static_cast<int>(imin64(kChunk, a.T - k * kChunk));
@@ -291,15 +293,14 @@ __global__ void __launch_bounds__(kThreads, 6) scan_fwd_fast_kernel(
     } else {
       for (int j = 0; j < len; ++j) step(P::to_f2(row[j * (kTileN / 2)]), row + j * (kTileN / 2));
     }
-    if (kDense && (MODE != kFwdAny || do_dense)) {
-      if (!store_stage(stage, &done[s], &empty[s], k, kFwdRing, &out_map, e0, k * kChunk)) {
-        bulk_wait_all();
-        return;
+    if (last_warp_done(&done[s])) {
+      if (kDense && (MODE != kFwdAny || do_dense)) {
+        tma_store_box_2d(&out_map, stage, static_cast<int>(e0), static_cast<int>(k * kChunk));
+        bulk_wait_read_all();  // the stage may be refilled once the store has read it
       }
-    } else {
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
+      if (k + kRing < K) refill(k + kRing);
     }
+    __syncwarp();
   }
   if (kDense && (MODE != kFwdAny || do_dense)) bulk_wait_all();
 
@@ -325,21 +326,21 @@ __global__ void __launch_bounds__(kThreads, 6) scan_fwd_fast_kernel(
 // ---------------------------------------------------------------------------
 // Backward
 // ---------------------------------------------------------------------------
-template <typename T, int KIND, int RESET, int SURR, int MODE>
-__global__ void __launch_bounds__(kThreads, bwd_min_blocks(KIND, SURR, MODE)) scan_bwd_fast_kernel(
-    const ScanBwdArgs a, const PairConsts c, const __grid_constant__ CUtensorMap out_map) {
+template <typename T, int KIND, int RESET, int SURR, int MODE, int RING, int MINB>
+__global__ void __launch_bounds__(kThreads, MINB) scan_bwd_fast_kernel(
+    const ScanBwdArgs a, const PairConsts c, const __grid_constant__ CUtensorMap x_map,
+    const __grid_constant__ CUtensorMap g_map, const __grid_constant__ CUtensorMap out_map) {
   using P = Pair<T>;
   using V = typename P::V;
+  constexpr int kRing = RING;
+  constexpr uint32_t kBoxBytes = uint32_t(kChunk) * kTileN * sizeof(T);
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + kBwdRing * bwd_stage_bytes<T>());
-  uint64_t* empty = full + kBwdRing;
-  uint64_t* done = empty + kBwdRing;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + kRing * bwd_stage_bytes<T>());
+  uint32_t* done = reinterpret_cast<uint32_t*>(full + kRing);
   auto stage_x = [&](int s) { return reinterpret_cast<T*>(smem_raw + s * bwd_stage_bytes<T>()); };
   auto stage_g = [&](int s) { return stage_x(s) + kChunk * kTileN; };
   auto stage_c = [&](int s) { return reinterpret_cast<float*>(stage_g(s) + kChunk * kTileN); };
 
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
   const int64_t e0 = int64_t(blockIdx.x) * kTileN;
   const int tile_n = static_cast<int>(imin64(kTileN, a.BN - e0));
   const int64_t K = (a.T + kChunk - 1) / kChunk;
@@ -348,41 +349,33 @@ __global__ void __launch_bounds__(kThreads, bwd_min_blocks(KIND, SURR, MODE)) sc
   const bool has_gs = kSpikes && (MODE != kBwdAny || a.grad_spikes != nullptr);
   const bool has_alif = KIND == MB_ALIF;
 
+  // the i-th chunk from the end into stage i % kRing: a box of x rows, a box
+  // of grad_spikes rows (rows past T and neurons past B*N read as zero and
+  // are never used) and the chunk's checkpoint rows (exactly the tile)
+  auto refill = [&](int64_t i) {
+    const int st = static_cast<int>(i % kRing);
+    const int64_t k = K - 1 - i;
+    const uint32_t ckpt_bytes = uint32_t(tile_n) * 4u;
+    mbar_arrive_expect_tx(&full[st], kBoxBytes * (has_gs ? 2u : 1u) +
+                                         ckpt_bytes * (has_alif ? 2u : 1u));
+    tma_load_box_2d(stage_x(st), &x_map, static_cast<int>(e0), static_cast<int>(k * kChunk),
+                    &full[st]);
+    if (has_gs) {
+      tma_load_box_2d(stage_g(st), &g_map, static_cast<int>(e0), static_cast<int>(k * kChunk),
+                      &full[st]);
+    }
+    bulk_copy_g2s(stage_c(st), a.ckpt_v + k * a.BN + e0, ckpt_bytes, &full[st]);
+    if (has_alif) bulk_copy_g2s(stage_c(st) + kTileN, a.ckpt_a + k * a.BN + e0, ckpt_bytes, &full[st]);
+  };
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kBwdRing; ++s) {
+    for (int s = 0; s < kRing; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);  // released by the thread that stores the stage
-      mbar_init(&done[s], kConsumerWarps);
+      done[s] = 0;
     }
     fence_barrier_init();
+    for (int64_t i = 0; i < imin64(kRing, K); ++i) refill(i);
   }
   __syncthreads();
-
-  if (warp == kConsumerWarps) {
-    if (lane == 0) {
-      const T* x = static_cast<const T*>(a.x);
-      const T* gs = static_cast<const T*>(a.grad_spikes);
-      const uint32_t row_bytes = uint32_t(tile_n) * uint32_t(sizeof(T));
-      for (int64_t i = 0; i < K; ++i) {
-        const int s = static_cast<int>(i % kBwdRing);
-        if (i >= kBwdRing &&
-            !mbar_wait_bounded(&empty[s], static_cast<uint32_t>(((i / kBwdRing) - 1) & 1))) {
-          break;
-        }
-        const int64_t k = K - 1 - i;
-        const int64_t t0 = k * kChunk;
-        const int len = static_cast<int>(imin64(kChunk, a.T - t0));
-        const uint32_t ckpt_bytes = uint32_t(tile_n) * 4u;
-        mbar_arrive_expect_tx(&full[s], row_bytes * uint32_t(len) * (has_gs ? 2u : 1u) +
-                                            ckpt_bytes * (has_alif ? 2u : 1u));
-        queue_chunk_rows(stage_x(s), x, t0, len, a.BN, e0, row_bytes, &full[s]);
-        if (has_gs) queue_chunk_rows(stage_g(s), gs, t0, len, a.BN, e0, row_bytes, &full[s]);
-        bulk_copy_g2s(stage_c(s), a.ckpt_v + k * a.BN + e0, ckpt_bytes, &full[s]);
-        if (has_alif) bulk_copy_g2s(stage_c(s) + kTileN, a.ckpt_a + k * a.BN + e0, ckpt_bytes, &full[s]);
-      }
-    }
-    return;
-  }
 
   const int tid = threadIdx.x;
   const bool valid = 2 * tid < tile_n;
@@ -441,13 +434,13 @@ __global__ void __launch_bounds__(kThreads, bwd_min_blocks(KIND, SURR, MODE)) sc
 
   // grad_x overwrites the x values of the stage (x is dead once the chunk is
   // replayed; each thread its own pair) and the finished stage goes out with
-  // one bulk tensor store (store_stage).
+  // one bulk tensor store.
   for (int64_t i = 0; i < K; ++i) {
-    const int s = static_cast<int>(i % kBwdRing);
+    const int s = static_cast<int>(i % kRing);
     const int64_t k = K - 1 - i;
     const int64_t t0 = k * kChunk;
     const int len = static_cast<int>(imin64(kChunk, a.T - t0));
-    if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>((i / kBwdRing) & 1))) {
+    if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>((i / kRing) & 1))) {
       bulk_wait_all();  // stores of earlier chunks finish before the early exit
       return;
     }
@@ -490,10 +483,14 @@ __global__ void __launch_bounds__(kThreads, bwd_min_blocks(KIND, SURR, MODE)) sc
         }
       }
     }
-    if (!store_stage(stage_x(s), &done[s], &empty[s], i, kBwdRing, &out_map, e0, t0)) {
-      bulk_wait_all();
-      return;
+    // the warp done last with the chunk writes grad_x (it overwrote x in the
+    // stage) and refills the stage with the chunk kRing further back
+    if (last_warp_done(&done[s])) {
+      tma_store_box_2d(&out_map, stage_x(s), static_cast<int>(e0), static_cast<int>(t0));
+      bulk_wait_read_all();
+      if (i + kRing < K) refill(i + kRing);
     }
+    __syncwarp();
   }
   bulk_wait_all();
   if (!valid) return;
@@ -527,17 +524,24 @@ bool fast_layout_ok(int64_t BN, size_t elt, std::initializer_list<const void*> r
 
 using Map = CUtensorMap;
 
-template <typename T, int KIND, int RESET, int MODE>
-void fwd_fast_mode(const ScanFwdArgs& a, const Map& om, cudaStream_t stream) {
-  auto k = scan_fwd_fast_kernel<T, KIND, RESET, MODE>;
-  allow_smem(k, fwd_smem<T>());
-  k<<<static_cast<unsigned>(ceil_div(a.BN, kTileN)), kThreads, fwd_smem<T>(), stream>>>(
+// The tensor maps of one launch: the input rows the stages load (x), the
+// spike-gradient rows (backward), and the output rows the stages store.
+struct Maps {
+  Map in, g, out;
+};
+
+template <typename T, int KIND, int RESET, int MODE, int RING = FwdCfg<T>::kRing,
+          int MINB = FwdCfg<T>::kMinBlocks>
+void fwd_fast_mode(const ScanFwdArgs& a, const Maps& om, cudaStream_t stream) {
+  auto k = scan_fwd_fast_kernel<T, KIND, RESET, MODE, RING, MINB>;
+  allow_smem(k, fwd_smem<T>(RING));
+  k<<<static_cast<unsigned>(ceil_div(a.BN, kTileN)), kThreads, fwd_smem<T>(RING), stream>>>(
       a, pair_consts<MB_SURR_NONE>(a.decay, a.threshold, a.adapt_decay, a.beta, a.reset, 0.0f),
-      om);
+      om.in, om.out);
 }
 
 template <typename T, int KIND, int RESET>
-void fwd_fast(const ScanFwdArgs& a, const Map& om, cudaStream_t stream) {
+void fwd_fast(const ScanFwdArgs& a, const Maps& om, cudaStream_t stream) {
   const bool d = a.spikes != nullptr, p = a.packed != nullptr, r = a.rates != nullptr;
   if (d && !p && !r) fwd_fast_mode<T, KIND, RESET, kFwdDense>(a, om, stream);
   else if (!d && p && !r) fwd_fast_mode<T, KIND, RESET, kFwdPacked>(a, om, stream);
@@ -546,7 +550,7 @@ void fwd_fast(const ScanFwdArgs& a, const Map& om, cudaStream_t stream) {
 }
 
 template <typename T>
-void fwd_fast_dispatch(int neuron, int reset_mode, const ScanFwdArgs& a, const Map& om,
+void fwd_fast_dispatch(int neuron, int reset_mode, const ScanFwdArgs& a, const Maps& om,
                        cudaStream_t stream) {
   if (neuron == kIzhikevich) {
     fwd_fast<T, kIzhikevich, MB_RESET_HARD>(a, om, stream);
@@ -559,16 +563,18 @@ void fwd_fast_dispatch(int neuron, int reset_mode, const ScanFwdArgs& a, const M
   }
 }
 
-template <typename T, int KIND, int RESET, int SURR, int MODE>
-void bwd_fast_mode(const ScanBwdArgs& a, const Map& om, cudaStream_t stream) {
-  auto k = scan_bwd_fast_kernel<T, KIND, RESET, SURR, MODE>;
-  allow_smem(k, bwd_smem<T>());
-  k<<<static_cast<unsigned>(ceil_div(a.BN, kTileN)), kThreads, bwd_smem<T>(), stream>>>(
-      a, pair_consts<SURR>(a.decay, a.threshold, a.adapt_decay, a.beta, a.reset, a.slope), om);
+template <typename T, int KIND, int RESET, int SURR, int MODE, int RING = BwdCfg<T>::kRing,
+          int MINB = bwd_min_blocks(KIND, SURR, MODE)>
+void bwd_fast_mode(const ScanBwdArgs& a, const Maps& om, cudaStream_t stream) {
+  auto k = scan_bwd_fast_kernel<T, KIND, RESET, SURR, MODE, RING, MINB>;
+  allow_smem(k, bwd_smem<T>(RING));
+  k<<<static_cast<unsigned>(ceil_div(a.BN, kTileN)), kThreads, bwd_smem<T>(RING), stream>>>(
+      a, pair_consts<SURR>(a.decay, a.threshold, a.adapt_decay, a.beta, a.reset, a.slope),
+      om.in, om.g, om.out);
 }
 
 template <typename T, int KIND, int RESET, int SURR>
-void bwd_fast(const ScanBwdArgs& a, const Map& om, cudaStream_t stream) {
+void bwd_fast(const ScanBwdArgs& a, const Maps& om, cudaStream_t stream) {
   const bool g = a.grad_spikes != nullptr, r = a.grad_rates != nullptr;
   if (g && !r) bwd_fast_mode<T, KIND, RESET, SURR, kBwdSpikes>(a, om, stream);
   else if (!g && r) bwd_fast_mode<T, KIND, RESET, SURR, kBwdRates>(a, om, stream);
@@ -576,7 +582,7 @@ void bwd_fast(const ScanBwdArgs& a, const Map& om, cudaStream_t stream) {
 }
 
 template <typename T, int KIND, int RESET>
-void bwd_fast_surr(int surrogate, const ScanBwdArgs& a, const Map& om, cudaStream_t stream) {
+void bwd_fast_surr(int surrogate, const ScanBwdArgs& a, const Maps& om, cudaStream_t stream) {
   switch (surrogate) {
     case MB_SURR_SIGMOID: bwd_fast<T, KIND, RESET, MB_SURR_SIGMOID>(a, om, stream); break;
     case MB_SURR_FAST_SIGMOID: bwd_fast<T, KIND, RESET, MB_SURR_FAST_SIGMOID>(a, om, stream); break;
@@ -592,7 +598,7 @@ void bwd_fast_surr(int surrogate, const ScanBwdArgs& a, const Map& om, cudaStrea
 
 template <typename T>
 void bwd_fast_dispatch(int neuron, int reset_mode, int surrogate, const ScanBwdArgs& a,
-                       const Map& om, cudaStream_t stream) {
+                       const Maps& om, cudaStream_t stream) {
   if (neuron == MB_LIF) {
     if (reset_mode == MB_RESET_HARD) bwd_fast_surr<T, MB_LIF, MB_RESET_HARD>(surrogate, a, om, stream);
     else bwd_fast_surr<T, MB_LIF, MB_RESET_SUBTRACT>(surrogate, a, om, stream);
@@ -604,9 +610,11 @@ void bwd_fast_dispatch(int neuron, int reset_mode, int surrogate, const ScanBwdA
 
 size_t dtype_size(int dtype) { return dtype == MB_F32 ? 4 : 2; }
 
-// Tensor map over a [T, BN] output written stage by stage: box = one stage
-// (kTileN neurons x kChunk rows), no swizzle (the stage is dense row-major).
-bool make_stage_map(Map* map, void* ptr, int dtype, int64_t BN, int64_t T) {
+// Tensor map over [T, BN] rows moved stage by stage (loaded inputs, stored
+// outputs): box = one stage (kTileN neurons x kChunk rows), no swizzle (the
+// stage is dense row-major).
+bool make_stage_map(Map* map, const void* cptr, int dtype, int64_t BN, int64_t T) {
+  void* ptr = const_cast<void*>(cptr);
   std::memset(map, 0, sizeof(Map));
   if (ptr == nullptr) return true;  // no such output: the kernel never uses the map
   auto fn = tma_encode_fn();
@@ -636,8 +644,12 @@ bool launch_scan_fwd_fast(int dtype, int neuron, int reset_mode, const ScanFwdAr
                                                    a.ckpt_a})) {
     return false;
   }
-  Map om;
-  if (!make_stage_map(&om, a.spikes, dtype, a.BN, a.T)) return false;
+  Maps om;
+  if (!make_stage_map(&om.in, a.x, dtype, a.BN, a.T) ||
+      !make_stage_map(&om.out, a.spikes, dtype, a.BN, a.T)) {
+    return false;
+  }
+  std::memset(&om.g, 0, sizeof(Map));
   switch (dtype) {
     case MB_F32: fwd_fast_dispatch<float>(neuron, reset_mode, a, om, stream); break;
     case MB_BF16: fwd_fast_dispatch<__nv_bfloat16>(neuron, reset_mode, a, om, stream); break;
@@ -654,8 +666,12 @@ bool launch_scan_bwd_fast(int dtype, int neuron, int reset_mode, int surrogate,
                       {a.grad_rates, a.grad_vT, a.grad_aT, a.grad_v0, a.grad_a0})) {
     return false;
   }
-  Map om;
-  if (!make_stage_map(&om, a.grad_x, dtype, a.BN, a.T)) return false;
+  Maps om;
+  if (!make_stage_map(&om.in, a.x, dtype, a.BN, a.T) ||
+      !make_stage_map(&om.g, a.grad_spikes, dtype, a.BN, a.T) ||
+      !make_stage_map(&om.out, a.grad_x, dtype, a.BN, a.T)) {
+    return false;
+  }
   switch (dtype) {
     case MB_F32: bwd_fast_dispatch<float>(neuron, reset_mode, surrogate, a, om, stream); break;
     case MB_BF16:

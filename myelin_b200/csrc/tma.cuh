@@ -39,4 +39,18 @@ __device__ __forceinline__ void tma_store_box_2d(const CUtensorMap* map, const v
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
 
+// 2-D bulk tensor load of one box at (c0, c1) into dense shared memory (128-byte
+// aligned), completing as transaction bytes on the mbarrier `bar`. The whole
+// box is written: elements outside the tensor read as zero, and the
+// transaction count is the full box size. Loads of this GPU's own memory only.
+__device__ __forceinline__ void tma_load_box_2d(void* dst, const CUtensorMap* map, int c0, int c1,
+                                                uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1),
+      "r"(static_cast<uint32_t>(__cvta_generic_to_shared(bar)))
+      : "memory");
+}
+
 }  // namespace mb
