@@ -228,11 +228,14 @@ enum mb_major { MB_KMAJOR = 0, MB_MNMAJOR = 1 };
  * products of an all-zero part on the device. Leading dimensions: multiples
  * of 8; K-major also needs K % 8 == 0 and ld >= K; MN-major ld >= M (or N).
  * Bases 16-byte aligned. Out-of-range elements of the tiles read as zero.
- * fp32 output from split operands is accumulated in K slices of at most 2048
- * (the tensor cores' fp32 accumulation of one MMA is not correctly rounded, so
- * its error grows with the MMAs summed into one accumulator), each slice into
- * `workspace` (mb_gemm_workspace_bytes; nullable when that is 0), and the
- * slices are then summed in order in fp32: deterministic.
+ * K is accumulated in slices, each into an fp32 partial in `workspace`
+ * (mb_gemm_workspace_bytes; nullable when that is 0) and the slices are then
+ * summed in order in fp32 (+ bias): deterministic. Slices are used for fp32
+ * output from split operands (at most 2048 of K each: the tensor cores' fp32
+ * accumulation of one MMA is not correctly rounded, so its error grows with
+ * the MMAs summed into one accumulator), and to occupy the SMs when the
+ * output has few tiles and K is long (the weight gradient of a small or
+ * narrow layer, K = T*B).
  * Used for the stream synapse's currents x[T*B, F] * W[F, N] (B = W N-major,
  * no transposed copy), input gradient G * W^T (both K-major) and weight
  * gradient x^T G (A = x M-major, B = G N-major; no transposes).
@@ -247,7 +250,7 @@ int mb_gemm(int in_dtype, const void* A, int a_major, int64_t lda, int64_t a_par
             void* workspace, int64_t workspace_bytes, void* stream);
 
 /* Workspace (bytes) mb_gemm needs for these sizes, part counts and output type
- * (0 unless fp32 output from split operands runs in K slices). */
+ * on the current device (0 when K is not sliced). */
 int64_t mb_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int a_parts, int b_parts,
                                 int out_dtype);
 

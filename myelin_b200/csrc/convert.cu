@@ -51,20 +51,25 @@ __device__ __forceinline__ uint32_t split_one(float x, int parts, TD* out, int64
 
 // Destination region [dst_rows, dst_cols] (each >= the source's): element
 // (r, c) is the split of src(r, c) inside the source and zero outside it.
+// Rows are spread over blockIdx.y (grid-stride), columns over the threads of
+// blockIdx.x: consecutive threads touch consecutive columns (coalesced loads
+// for a row-major source, coalesced stores of every part).
 template <typename TS, typename TD>
 __global__ void split_bf16_kernel(const TS* __restrict__ src, int64_t rows, int64_t cols,
                                   int64_t rs, int64_t cs, int parts,
                                   TD* __restrict__ dst, int64_t dst_rows,
                                   int64_t dst_cols, int64_t ld, int64_t part_stride,
                                   int32_t* nonzero) {
-  const int64_t total = dst_rows * dst_cols;
   uint32_t nz = 0;
-  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += int64_t(gridDim.x) * blockDim.x) {
-    const int64_t r = i / dst_cols;
-    const int64_t c = i - r * dst_cols;
-    const float x = (r < rows && c < cols) ? load_as_float(src + r * rs + c * cs) : 0.0f;
-    nz |= split_one(x, parts, dst + r * ld + c, part_stride);
+  const int64_t c0 = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t cstep = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t r = blockIdx.y; r < dst_rows; r += gridDim.y) {
+    const TS* srow = src + r * rs;
+    TD* drow = dst + r * ld;
+    for (int64_t c = c0; c < dst_cols; c += cstep) {
+      const float x = (r < rows && c < cols) ? load_as_float(srow + c * cs) : 0.0f;
+      nz |= split_one(x, parts, drow + c, part_stride);
+    }
   }
   if (nonzero != nullptr) {
     nz = __reduce_or_sync(0xffffffffu, nz);
@@ -87,7 +92,16 @@ __global__ void column_sums_partial_kernel(const TS* __restrict__ src, int64_t r
   const int64_t r1 = imin64(rows, r0 + rows_per_slice);
   if (c >= cols) return;
   float acc = 0.0f;
-  for (int64_t r = r0; r < r1; ++r) acc += load_as_float(src + r * ld + c);
+  int64_t r = r0;
+  // eight loads in flight, then their sums in row order
+  for (; r + 8 <= r1; r += 8) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = load_as_float(src + (r + j) * ld + c);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc += v[j];
+  }
+  for (; r < r1; ++r) acc += load_as_float(src + r * ld + c);
   partial[int64_t(blockIdx.y) * cols + c] = acc;
 }
 
@@ -138,8 +152,10 @@ extern "C" int mb_split_bf16(int src_dtype, const void* src, int64_t rows, int64
   }
   MB_CHECK_ARG((src != nullptr || rows * cols == 0) && dst != nullptr,
                "mb_split_bf16: null pointer");
-  const int64_t total = dst_rows * dst_cols;
-  const unsigned grid = static_cast<unsigned>(imin64(ceil_div(total, 256), 148 * 16));
+  // enough blocks for about 16 per SM: columns in blocks of 256, rows on y
+  const int64_t col_blocks = imin64(ceil_div(dst_cols, 256), 148 * 16);
+  const dim3 grid(static_cast<unsigned>(col_blocks),
+                  static_cast<unsigned>(imin64(dst_rows, imin64(65535, ceil_div(148 * 16, col_blocks)))));
   auto* out = static_cast<__nv_bfloat16*>(dst);
   switch (src_dtype) {
     case MB_F32:

@@ -21,6 +21,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <type_traits>
@@ -965,18 +966,37 @@ __global__ void slices_reduce_kernel(const float* __restrict__ partial, int slic
   }
 }
 
-// K slices for a launch: fp32 output from split (fp32) operands is summed in
-// slices of at most kSliceKBlocks k-blocks. The tensor cores' fp32
-// accumulation of each MMA is not correctly rounded, so its error grows with
-// the number of MMAs summed into one accumulator; slices bound that count and
-// are added in fp32 (correctly rounded) afterwards.
-constexpr int kSliceKBlocks = 32;  // K = 2048 per slice
+int sm_count();
 
-int k_slices_for(int64_t K, int a_parts, int b_parts, int out_dtype, int* kb_per_slice) {
+// K slices for a launch (each slice's partial sums go to an fp32 workspace and
+// a second kernel adds them in order):
+//  - accuracy: fp32 output from split (fp32) operands is summed in slices of
+//    at most kSliceKBlocks k-blocks. The tensor cores' fp32 accumulation of
+//    each MMA is not correctly rounded, so its error grows with the number of
+//    MMAs summed into one accumulator; slices bound that count and are added
+//    in fp32 (correctly rounded) afterwards;
+//  - parallelism: when the output has too few tiles to occupy half of the SMs
+//    and K is long (a weight gradient of a narrow or small layer: K = T * B),
+//    K is split until the (tile, slice) units fill the SMs, each slice at
+//    least kMinSliceKBlocks k-blocks long.
+constexpr int kSliceKBlocks = 32;     // K = 2048 per slice
+constexpr int kMinSliceKBlocks = 8;   // K = 512
+
+int k_slices_for(int64_t M, int64_t N, int64_t K, int a_parts, int b_parts, int out_dtype,
+                 bool occupancy, int* kb_per_slice) {
   const int kblocks = static_cast<int>((K + kBK - 1) / kBK);
-  *kb_per_slice = kblocks;
-  if (out_dtype != MB_F32 || (a_parts == 1 && b_parts == 1) || kblocks <= kSliceKBlocks) return 1;
-  int slices = (kblocks + kSliceKBlocks - 1) / kSliceKBlocks;
+  int slices = 1;
+  if (out_dtype == MB_F32 && (a_parts > 1 || b_parts > 1) && kblocks > kSliceKBlocks) {
+    slices = (kblocks + kSliceKBlocks - 1) / kSliceKBlocks;
+  }
+  const int bn = N >= 192 ? 256 : (N > 64 ? 128 : 64);
+  const int64_t tiles = ((M + kBM - 1) / kBM) * ((N + bn - 1) / bn);
+  const int sms = sm_count();
+  if (occupancy && tiles * slices < sms / 2 && kblocks >= 2 * kMinSliceKBlocks) {
+    const int64_t want = (sms + tiles - 1) / tiles;
+    const int64_t most = kblocks / kMinSliceKBlocks;
+    slices = static_cast<int>(std::max<int64_t>(slices, std::min(want, most)));
+  }
   const int per = (kblocks + slices - 1) / slices;
   *kb_per_slice = per;
   return (kblocks + per - 1) / per;
@@ -997,7 +1017,7 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb_, const CUtensorMap& mc,
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        static_cast<int>(Layout<BN>::kSmem));
   const int64_t tiles = ((args.M + kBM - 1) / kBM) * ((args.N + BN - 1) / BN);
-  const int grid = static_cast<int>(imin64(tiles, sm_count()));
+  const int grid = static_cast<int>(imin64(tiles * args.k_slices, sm_count()));
   kern<<<grid, kThreads, Layout<BN>::kSmem, s>>>(ma, mb_, mc, args);
   return 0;
 }
@@ -1009,7 +1029,7 @@ int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb_, const CUtensorMap
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        static_cast<int>(Layout2::kSmem));
   const int64_t tiles = ((args.M + k2BM - 1) / k2BM) * ((args.N + k2BN - 1) / k2BN);
-  const int pairs = static_cast<int>(imin64(tiles, sm_count() / 2));
+  const int pairs = static_cast<int>(imin64(tiles * args.k_slices, sm_count() / 2));
   kern<<<2 * pairs, k2Threads, Layout2::kSmem, s>>>(ma, mb_, mc, args);
   return 0;
 }
@@ -1109,7 +1129,7 @@ extern "C" int64_t mb_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int 
                                            int b_parts, int out_dtype) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   int per = 0;
-  const int slices = k_slices_for(K, a_parts, b_parts, out_dtype, &per);
+  const int slices = k_slices_for(M, N, K, a_parts, b_parts, out_dtype, true, &per);
   return slices > 1 ? int64_t(slices) * M * slices_pld(N) * int64_t(sizeof(float)) : 0;
 }
 
@@ -1170,11 +1190,18 @@ extern "C" int mb_gemm(int in_dtype, const void* A, int a_major, int64_t lda, in
     }
   }
   cudaStream_t s = as_stream(stream);
-  args.k_slices = k_slices_for(K, a_parts, b_parts, out_dtype, &args.kb_per_slice);
+  const int64_t pld = slices_pld(N);
+  args.k_slices = k_slices_for(M, N, K, a_parts, b_parts, out_dtype, true, &args.kb_per_slice);
+  if (args.k_slices > 1 &&
+      (workspace == nullptr ||
+       workspace_bytes < int64_t(args.k_slices) * M * pld * int64_t(sizeof(float)))) {
+    // no room for the slices that would only add parallelism (e.g. through
+    // mb_gemm_tn, which takes no workspace): keep the ones accuracy needs
+    args.k_slices = k_slices_for(M, N, K, a_parts, b_parts, out_dtype, false, &args.kb_per_slice);
+  }
   int rc;
   if (args.k_slices > 1) {
     // fp32 partial sums per K slice into the workspace, then their ordered sum
-    const int64_t pld = slices_pld(N);
     const int64_t need = int64_t(args.k_slices) * M * pld * int64_t(sizeof(float));
     MB_CHECK_ARG(workspace != nullptr && workspace_bytes >= need && aligned_to(workspace, 16),
                  "mb_gemm: workspace of %lld bytes (16-byte aligned) required, got %lld",
@@ -1188,9 +1215,17 @@ extern "C" int mb_gemm(int in_dtype, const void* A, int a_major, int64_t lda, in
                              : launch_typed<__half, float>(a, b, part, MB_F32, s);
     if (rc != 0) return rc;
     const unsigned grid = static_cast<unsigned>(imin64(ceil_div(M * N, 256), 148 * 8));
-    slices_reduce_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(workspace),
-                                                     args.k_slices, M, N, pld, bias, bias_dtype,
-                                                     static_cast<float*>(C), ldc);
+    const float* ws = static_cast<const float*>(workspace);
+    if (out_dtype == MB_F32) {
+      slices_reduce_kernel<float><<<grid, 256, 0, s>>>(ws, args.k_slices, M, N, pld, bias,
+                                                       bias_dtype, static_cast<float*>(C), ldc);
+    } else if (out_dtype == MB_BF16) {
+      slices_reduce_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+          ws, args.k_slices, M, N, pld, bias, bias_dtype, static_cast<__nv_bfloat16*>(C), ldc);
+    } else {
+      slices_reduce_kernel<__half><<<grid, 256, 0, s>>>(ws, args.k_slices, M, N, pld, bias,
+                                                        bias_dtype, static_cast<__half*>(C), ldc);
+    }
     MB_CHECK_LAUNCH("mb_gemm");
     return 0;
   }
