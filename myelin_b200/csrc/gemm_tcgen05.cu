@@ -368,13 +368,14 @@ __device__ __forceinline__ void stage_row32(uint8_t* slot, int r, const float (&
 // double-buffered: chunk ci+1 loads while chunk ci is converted. With split K
 // (args.k_slices > 1) the tile goes to slice `slice` of the fp32 workspace
 // (a 3-D tensor map over [k_slices, M, ldc]).
-template <typename TOut, int BN>
+template <typename TOut, int BN, int WARP_STAGE_BYTES = 2 * 32 * 32 * 4>
 __device__ __forceinline__ void drain_tile(uint32_t tbase, int64_t row0, int64_t col_tile0,
                                            int lane, const GemmArgs& args,
                                            const CUtensorMap* tma_c, uint8_t* slots,
                                            uint32_t& nstore, int slice) {
   constexpr int kSlotBytes = 32 * 32 * int(sizeof(TOut));
-  constexpr int kSlots = 2 * (32 * 32 * 4) / kSlotBytes;  // 2 (fp32) or 4 (16-bit)
+  // staging slots of this warp: WARP_STAGE_BYTES / slot size
+  constexpr int kSlots = WARP_STAGE_BYTES / kSlotBytes;
   const bool has_bias = args.bias != nullptr;
   const bool vec_ok = args.vec_ok != 0;
   const bool use_tma = args.tma_store != 0;
@@ -600,7 +601,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // and a cluster barrier before TMEM release keeps both CTAs alive until
 // neither can touch the other's shared memory.
 // ---------------------------------------------------------------------------
-constexpr int k2Stages = 5;
+constexpr int k2Stages = 6;
 constexpr int k2EpiWarps = 8;  // two per TMEM lane quarter, 128 columns each
 constexpr int k2Threads = 64 + 32 * k2EpiWarps;
 constexpr int k2BM = 256;  // rows per pair tile (128 per CTA)
@@ -610,8 +611,9 @@ struct Layout2 {
   static constexpr int kABytes = 128 * kBK * 2;  // this CTA's A rows
   static constexpr int kBBytes = 128 * kBK * 2;  // this CTA's B rows
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kEpiSlotBytes = 32 * 32 * 4;
-  static constexpr int kEpiBytes = k2EpiWarps * 2 * kEpiSlotBytes;
+  // epilogue staging per warp: one 32 x 32 fp32 block or two 16-bit blocks
+  static constexpr int kEpiWarpBytes = 32 * 32 * 4;
+  static constexpr int kEpiBytes = k2EpiWarps * kEpiWarpBytes;
   static constexpr int kBarrierBytes = 256;
   static constexpr size_t kSmem =
       size_t(k2Stages) * kStageBytes + kEpiBytes + kBarrierBytes + 1024;
@@ -672,6 +674,17 @@ __device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t adesc, ui
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// Arrive once on the barrier at shared offset `bar` in both CTAs of the pair
+// (one multicast commit) when every pair MMA issued so far by this thread has
+// completed.
+__device__ __forceinline__ void mma_commit_pair_both(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_addr(bar)),
+      "h"(static_cast<uint16_t>(0x3))
+      : "memory");
 }
 
 // Arrive once on the barrier at cluster address `bar_cluster` when every
@@ -819,14 +832,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
             }
             acc = true;
             // the stage is free in both CTAs once these MMAs finish
-            mma_commit_pair(cluster_addr(smem_addr(&empty[s]), 0));
-            mma_commit_pair(cluster_addr(smem_addr(&empty[s]), 1));
+            mma_commit_pair_both(&empty[s]);
           }
         }
-        if (ok) {  // the tile's accumulator halves are complete in both CTAs
-          mma_commit_pair(cluster_addr(smem_addr(&acc_full[b]), 0));
-          mma_commit_pair(cluster_addr(smem_addr(&acc_full[b]), 1));
-        }
+        if (ok) mma_commit_pair_both(&acc_full[b]);  // both CTAs' accumulator halves are complete
       }
       mma_commit_pair(cluster_addr(smem_addr(drained), 0));
       // all MMAs done before TMEM is released (a timeout is recorded in the
@@ -837,7 +846,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
     const int quarter = warp & 3;      // TMEM lanes this warp may access (warp id % 4)
     const int half = (warp - 2) >> 2;  // which 128 of the 256 columns it drains
     const bool use_tma = args.tma_store != 0;
-    uint8_t* slots = sepi + (warp - 2) * 2 * L::kEpiSlotBytes;
+    uint8_t* slots = sepi + (warp - 2) * L::kEpiWarpBytes;
     uint32_t nstore = 0;
     uint32_t local = 0;
     for (int64_t unit = pair; unit < units; unit += pairs, ++local) {
@@ -847,7 +856,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
       const int64_t tile = unit / args.k_slices;
       const int64_t tm = tile / n_tiles;
       const int64_t tn = tile % n_tiles;
-      drain_tile<TOut, k2BN / 2>(
+      drain_tile<TOut, k2BN / 2, L::kEpiWarpBytes>(
           tmem_base + (uint32_t(quarter * 32) << 16) + b * k2BN + half * (k2BN / 2),
           tm * k2BM + int64_t(rank) * 128 + quarter * 32, tn * k2BN + half * (k2BN / 2), lane,
           args, &tma_c, slots, nstore, static_cast<int>(unit % args.k_slices));
