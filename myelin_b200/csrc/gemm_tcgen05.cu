@@ -319,10 +319,15 @@ __device__ __forceinline__ void store_row32(TOut* dst, const float (&v)[32], int
     }
     return;
   }
-  for (int j = 0; j < valid; ++j) {
-    if constexpr (std::is_same<TOut, float>::value) dst[j] = v[j];
-    else if constexpr (std::is_same<TOut, __nv_bfloat16>::value) dst[j] = __float2bfloat16_rn(v[j]);
-    else dst[j] = __float2half_rn(v[j]);
+  // unrolled with a predicate per element: a loop bounded by `valid` would
+  // index v at run time and move it (and every chunk's values) to local memory
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (j < valid) {
+      if constexpr (std::is_same<TOut, float>::value) dst[j] = v[j];
+      else if constexpr (std::is_same<TOut, __nv_bfloat16>::value) dst[j] = __float2bfloat16_rn(v[j]);
+      else dst[j] = __float2half_rn(v[j]);
+    }
   }
 }
 
