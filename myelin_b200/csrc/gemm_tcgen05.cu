@@ -995,6 +995,7 @@ int sm_count();
 //    least kMinSliceKBlocks k-blocks long.
 constexpr int kSliceKBlocks = 32;     // K = 2048 per slice
 constexpr int kMinSliceKBlocks = 8;   // K = 512
+constexpr int kWaveSliceKBlocks = 128;  // K = 8192
 
 int k_slices_for(int64_t M, int64_t N, int64_t K, int a_parts, int b_parts, int out_dtype,
                  bool occupancy, int* kb_per_slice) {
@@ -1010,6 +1011,21 @@ int k_slices_for(int64_t M, int64_t N, int64_t K, int a_parts, int b_parts, int 
     const int64_t want = (sms + tiles - 1) / tiles;
     const int64_t most = kblocks / kMinSliceKBlocks;
     slices = static_cast<int>(std::max<int64_t>(slices, std::min(want, most)));
+  } else if (occupancy && slices == 1 && kblocks >= kWaveSliceKBlocks && M >= 256 && N >= 256) {
+    // long K on the pair kernel (a weight gradient, K = T * B): split K in up
+    // to 4 when that evens out the last wave of pair units by 5 % or more
+    // (256 pair tiles on 74 pairs run 3.46 waves: 86 %; in 2 slices 6.92: 99 %)
+    const int64_t pairs = sms / 2;
+    const int64_t ptiles = ((M + 255) / 256) * ((N + 255) / 256);
+    auto eff = [&](int64_t sl) {
+      const int64_t units = ptiles * sl;
+      return double(units) / double(((units + pairs - 1) / pairs) * pairs);
+    };
+    int best = 1;
+    for (int sl = 2; sl <= 4; ++sl) {
+      if (eff(sl) >= eff(best) + 0.05) best = sl;
+    }
+    slices = best;
   }
   const int per = (kblocks + slices - 1) / slices;
   *kb_per_slice = per;
@@ -1049,21 +1065,20 @@ int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb_, const CUtensorMap
 }
 
 // Kernel choice, from measurements on B200 (bf16, CUDA events):
-//  - the pair kernel halves operand traffic per SM and wins once the main
-//    loop dominates: K >= 2048 with 16-bit output (51200 x 4096 x 4096 with
-//    bias 1420 vs 1368 TFLOP/s; K = 2048 on par or better);
-//  - at smaller K, or with fp32 output, the accumulator drain is the larger
-//    part of a tile and the one-SM kernel, which waits only for its own
-//    epilogue, is faster (K = 1024: 1062 vs 937);
-//  - small problems (under two waves of one-SM tiles) go to the pair kernel
-//    (6400 x 1024 x 784: 440 vs 306).
-// `k_eff` is the K loop length summed over the segments.
+//  - the pair kernel halves operand traffic per SM (each SM loads half of B)
+//    and drains its accumulator with twice the warps; with 16-bit output it
+//    is faster at every K measured (51200 x 4096 x K: K = 256 662 vs 608
+//    TFLOP/s, 512 1212 vs 1150, 1024 1517 vs 1387, 2048 1662 on par);
+//  - fp32 output (one 4 KB staging block per drain warp in the pair kernel)
+//    goes to the pair kernel when the main loop dominates (K per unit >= 2048)
+//    or the problem is small (under two waves of one-SM tiles).
+// `k_eff` is the K loop length of one work unit summed over the segments.
 bool use_pair(const GemmArgs& args, int64_t k_eff, bool out_f32) {
   const int sms = sm_count();
   const int64_t pair_tiles = ((args.M + k2BM - 1) / k2BM) * ((args.N + k2BN - 1) / k2BN);
   const int64_t single_tiles = ((args.M + kBM - 1) / kBM) * ((args.N + 255) / 256);
-  if (args.M < k2BM || args.N < k2BN || pair_tiles < sms / 2) return false;
-  return (k_eff >= 2048 && !out_f32) || single_tiles < 2 * sms;
+  if (args.M < k2BM || args.N < k2BN || pair_tiles * args.k_slices < sms / 2) return false;
+  return !out_f32 || k_eff >= 2048 || single_tiles < 2 * sms;
 }
 
 template <typename TIn, typename TOut, bool A_MN, bool B_MN>
@@ -1077,7 +1092,8 @@ int launch_majors(const Operand& A, const Operand& B, GemmArgs args, int out_dty
                         : make_c_map(&mc, args.C, args.M, args.N, args.ldc, out_dtype))
                        ? 1
                        : 0;
-  if (use_pair(args, args.K * args.nseg, out_dtype == MB_F32)) {
+  const int64_t k_unit = std::min<int64_t>(args.K, int64_t(args.kb_per_slice) * kBK);
+  if (use_pair(args, k_unit * args.nseg, out_dtype == MB_F32)) {
     // both operand maps: each CTA's 128 rows (K-major) / 64-wide blocks (MN-major)
     if (!make_operand_map(&ma, A, args.M, args.K, 128, bf16) ||
         !make_operand_map(&mbm, B, args.N, args.K, 128, bf16)) {

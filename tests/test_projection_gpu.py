@@ -101,9 +101,11 @@ def test_fp32_weight_gradient_over_long_k_runs_in_slices():
     lib = nat.lib()
     M, F, N = 51200, 64, 96
     assert lib.mb_gemm_workspace_bytes(F, N, M, 3, 3, nat.MB_F32) > 0
-    # a large 16-bit problem runs unsliced; a small one is sliced to occupy the SMs
-    assert lib.mb_gemm_workspace_bytes(4096, 4096, M, 1, 1, nat.MB_BF16) == 0
+    # a large 16-bit problem of moderate K runs unsliced; a small one is sliced
+    # to occupy the SMs; a long-K one to even out the last wave
+    assert lib.mb_gemm_workspace_bytes(4096, 4096, 4096, 1, 1, nat.MB_BF16) == 0
     assert lib.mb_gemm_workspace_bytes(F, N, M, 1, 1, nat.MB_BF16) > 0
+    assert lib.mb_gemm_workspace_bytes(4096, 4096, M, 1, 1, nat.MB_BF16) > 0
     gen = torch.Generator(device=DEV).manual_seed(13)
     x = _rand((M, F), gen)
     g = _rand((M, N), gen, scale=0.01)
