@@ -272,6 +272,16 @@ int mb_split_bf16(int src_dtype, const void* src, int64_t rows, int64_t cols,
                   int64_t dst_rows, int64_t dst_cols, int64_t dst_ld, int64_t dst_part_stride,
                   int32_t* nonzero, void* stream);
 
+/*
+ * fp32 product with a short contraction: C[M, N] = A[M, K] * B[N, K]^T, K <= 32,
+ * both operands K-major (leading dimensions lda, ldb), fp32 FMAs with k in
+ * order. For the input gradient of a narrow fp32 layer (G[T*B, 10] * W^T),
+ * where tensor-core tiles would be mostly padding.
+ * Replaces: src/myelin/triton/lif.py:1136-1180 (input gradient) for narrow layers.
+ */
+int mb_gemm_small_k(const float* A, int64_t lda, const float* B, int64_t ldb, float* C,
+                    int64_t ldc, int64_t M, int64_t N, int64_t K, void* stream);
+
 /* Workspace (bytes) mb_column_sums needs for a [rows, cols] source. */
 int64_t mb_column_sums_workspace_bytes(int64_t rows, int64_t cols);
 

@@ -74,6 +74,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mb_split_bf16": (
         _int, [_int, _vp, _i64, _i64, _i64, _i64, _int, _vp, _i64, _i64, _i64, _i64, _vp, _vp]
     ),
+    "mb_gemm_small_k": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp]),
     "mb_column_sums_workspace_bytes": (_i64, [_i64, _i64]),
     "mb_column_sums": (_int, [_int, _vp, _i64, _i64, _i64, _int, _vp, _vp, _i64, _vp]),
     "mb_pack_spikes": (_int, [_int, _vp, _vp, _i64, _i64, _vp]),
@@ -325,6 +326,18 @@ def split_bf16(src: torch.Tensor, rows: int, cols: int, row_stride: int, col_str
             dst_rows, dst_cols, dst_ld, dst_part_stride, ptr(nonzero), stream_handle(src.device),
         )
     check(status, "mb_split_bf16")
+
+
+def gemm_small_k(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """out[M, N] = a[M, K] @ b[N, K]^T in fp32 FMAs, K <= 32 (``mb_gemm_small_k``)."""
+
+    M, K = a.shape
+    N = b.shape[0]
+    with torch.cuda.device(a.device):
+        status = lib().mb_gemm_small_k(ptr(a), a.stride(0), ptr(b), b.stride(0), ptr(out),
+                                       out.stride(0), M, N, K, stream_handle(a.device))
+    check(status, "mb_gemm_small_k")
+    return out
 
 
 def column_sums(src: torch.Tensor, rows: int, cols: int, ld: int, out: torch.Tensor) -> None:

@@ -241,3 +241,60 @@ extern "C" int mb_column_sums(int dtype, const void* src, int64_t rows, int64_t 
   MB_CHECK_LAUNCH("mb_column_sums");
   return 0;
 }
+
+// ---------------------------------------------------------------------------
+// fp32 product with a short contraction (K <= 32), e.g. the input gradient of
+// a 10-wide readout layer: C[M, N] = A[M, K] * B[N, K]^T in fp32 FMAs, k in
+// order (deterministic). Block = 256 threads over 256 columns n and 32 rows m:
+// a thread keeps its B row in registers and takes each A row from shared
+// memory (one broadcast per k); a warp's stores of a row are 128 contiguous
+// bytes.
+// ---------------------------------------------------------------------------
+namespace mb {
+namespace {
+
+constexpr int kSmallK = 32;
+constexpr int kSmallRows = 32;
+
+__global__ void gemm_small_k_kernel(const float* __restrict__ A, int64_t lda,
+                                    const float* __restrict__ B, int64_t ldb, float* __restrict__ C,
+                                    int64_t ldc, int64_t M, int64_t N, int K) {
+  __shared__ float sa[kSmallRows][kSmallK];
+  const int64_t n = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t m0 = int64_t(blockIdx.y) * kSmallRows;
+  for (int i = threadIdx.x; i < kSmallRows * kSmallK; i += blockDim.x) {
+    const int r = i / kSmallK, k = i % kSmallK;
+    sa[r][k] = (m0 + r < M && k < K) ? A[(m0 + r) * lda + k] : 0.0f;
+  }
+  float b[kSmallK];
+#pragma unroll
+  for (int k = 0; k < kSmallK; ++k) b[k] = (n < N && k < K) ? B[n * ldb + k] : 0.0f;
+  __syncthreads();
+  if (n >= N) return;
+  for (int r = 0; r < kSmallRows && m0 + r < M; ++r) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kSmallK; ++k) {
+      if (k < K) acc = __fmaf_rn(sa[r][k], b[k], acc);
+    }
+    C[(m0 + r) * ldc + n] = acc;
+  }
+}
+
+}  // namespace
+}  // namespace mb
+
+extern "C" int mb_gemm_small_k(const float* A, int64_t lda, const float* B, int64_t ldb, float* C,
+                               int64_t ldc, int64_t M, int64_t N, int64_t K, void* stream) {
+  clear_error();
+  MB_CHECK_ARG(M >= 0 && N >= 0 && K >= 0 && K <= kSmallK,
+               "mb_gemm_small_k: K must be in [0, %d]", kSmallK);
+  MB_CHECK_ARG(lda >= K && ldb >= K && ldc >= N, "mb_gemm_small_k: leading dimension too small");
+  if (M == 0 || N == 0) return 0;
+  MB_CHECK_ARG(A != nullptr && B != nullptr && C != nullptr, "mb_gemm_small_k: null pointer");
+  const dim3 grid(static_cast<unsigned>(ceil_div(N, 256)), static_cast<unsigned>(ceil_div(M, kSmallRows)));
+  gemm_small_k_kernel<<<grid, 256, 0, as_stream(stream)>>>(A, lda, B, ldb, C, ldc, M, N,
+                                                           static_cast<int>(K));
+  MB_CHECK_LAUNCH("mb_gemm_small_k");
+  return 0;
+}

@@ -63,6 +63,8 @@ struct GemmArgs {
   // sums (k-blocks [s * kb_per_slice, (s + 1) * kb_per_slice) for slice s),
   // written as fp32 to slice s of C = a [k_slices, M, ldc] workspace (no
   // bias); a second kernel sums the slices in order. k_slices == 1: plain.
+  // Work unit u is tile u % tiles of slice u / tiles: the units running at
+  // once share one slice's rows of both operands, which stay in L2.
   int k_slices;
   int kb_per_slice;
 };
@@ -481,8 +483,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       const uint32_t segs = segment_mask(args);
       for (int64_t unit = blockIdx.x; unit < units && ok; unit += gridDim.x) {
-        const int64_t tile = unit / args.k_slices;
-        const int kb0 = static_cast<int>(unit % args.k_slices) * args.kb_per_slice;
+        const int64_t tile = unit % tiles;
+        const int kb0 = static_cast<int>(unit / tiles) * args.kb_per_slice;
         const int kb1 = min(kblocks, kb0 + args.kb_per_slice);
         const int64_t tm = tile / n_tiles;
         const int64_t tn = tile % n_tiles;
@@ -519,7 +521,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0, local = 0;
       bool ok = true;
       for (int64_t unit = blockIdx.x; unit < units && ok; unit += gridDim.x, ++local) {
-        const int kb0 = static_cast<int>(unit % args.k_slices) * args.kb_per_slice;
+        const int kb0 = static_cast<int>(unit / tiles) * args.kb_per_slice;
         const int kb1 = min(kblocks, kb0 + args.kb_per_slice);
         const uint32_t b = local & 1;
         const uint32_t use_b = local >> 1;
@@ -564,12 +566,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t b = local & 1;
       if (!mbar_wait_bounded(&acc_full[b], (local >> 1) & 1)) break;
       tc_fence_after();
-      const int64_t tile = unit / args.k_slices;
+      const int64_t tile = unit % tiles;
       const int64_t tm = tile / n_tiles;
       const int64_t tn = tile % n_tiles;
       drain_tile<TOut, BN>(tmem_base + (uint32_t(quarter * 32) << 16) + b * BN,
                            tm * kBM + quarter * 32, tn * BN, lane, args, &tma_c, slots,
-                           nstore, static_cast<int>(unit % args.k_slices));
+                           nstore, static_cast<int>(unit / tiles));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
@@ -771,8 +773,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
       bool ok = true;
       const uint32_t segs = segment_mask(args);
       for (int64_t unit = pair; unit < units && ok; unit += pairs) {
-        const int64_t tile = unit / args.k_slices;
-        const int kb0 = static_cast<int>(unit % args.k_slices) * args.kb_per_slice;
+        const int64_t tile = unit % tiles;
+        const int kb0 = static_cast<int>(unit / tiles) * args.kb_per_slice;
         const int kb1 = min(kblocks, kb0 + args.kb_per_slice);
         const int64_t tm = tile / n_tiles;
         const int64_t tn = tile % n_tiles;
@@ -811,7 +813,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
       uint32_t it = 0, local = 0;
       bool ok = true;
       for (int64_t unit = pair; unit < units && ok; unit += pairs, ++local) {
-        const int kb0 = static_cast<int>(unit % args.k_slices) * args.kb_per_slice;
+        const int kb0 = static_cast<int>(unit / tiles) * args.kb_per_slice;
         const int kb1 = min(kblocks, kb0 + args.kb_per_slice);
         const uint32_t b = local & 1;
         const uint32_t use_b = local >> 1;
@@ -858,13 +860,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
       const uint32_t b = local & 1;
       if (!mbar_wait_bounded(&acc_full[b], (local >> 1) & 1)) break;
       tc_fence_after();
-      const int64_t tile = unit / args.k_slices;
+      const int64_t tile = unit % tiles;
       const int64_t tm = tile / n_tiles;
       const int64_t tn = tile % n_tiles;
       drain_tile<TOut, k2BN / 2, L::kEpiWarpBytes>(
           tmem_base + (uint32_t(quarter * 32) << 16) + b * k2BN + half * (k2BN / 2),
           tm * k2BM + int64_t(rank) * 128 + quarter * 32, tn * k2BN + half * (k2BN / 2), lane,
-          args, &tma_c, slots, nstore, static_cast<int>(unit % args.k_slices));
+          args, &tma_c, slots, nstore, static_cast<int>(unit / tiles));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(cluster_addr(smem_addr(&acc_empty[b]), 0));

@@ -24,6 +24,9 @@ src/myelin/modules.py:123) and inputs x [M = T*B, F]:
   part.
 - db is a fixed-order column sum (``mb_column_sums``), deterministic like dW
   (the reference's Triton kernels use float atomics for both).
+- the fp32 input gradient of a narrow layer (N <= 32, the 10-wide readout)
+  is a plain fp32-FMA kernel (``mb_gemm_small_k``): its tensor-core tiles
+  would be mostly padding.
 """
 
 from __future__ import annotations
@@ -34,6 +37,7 @@ from myelin_b200 import _native as nat
 
 HALF_DTYPES = (torch.bfloat16, torch.float16)
 SPLIT_PARTS = 3
+SMALL_K = 32  # mb_gemm_small_k: fp32 contractions this short skip the tensor cores
 
 
 def _round8(n: int) -> int:
@@ -111,6 +115,9 @@ def input_grad(g2: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     out = torch.empty((M, F), dtype=g2.dtype, device=g2.device)
     if M == 0 or F == 0:
         return out
+    if g2.dtype == torch.float32 and N <= SMALL_K and g2.stride(1) == 1 and weight.stride(1) == 1:
+        # a narrow fp32 layer: a 10-deep contraction in plain fp32 FMAs
+        return nat.gemm_small_k(g2, weight, out)
     K = _round8(N)
     if g2.dtype in HALF_DTYPES:
         a, lda = _operand16(g2, rows_out=M, cols_out=K, zero_fill=True)
