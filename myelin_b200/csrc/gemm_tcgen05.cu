@@ -252,44 +252,25 @@ __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// bias[j0 .. j0+31] as floats; 16-byte loads when the run is complete and aligned
-// (all lanes read the same addresses: one broadcast per load).
-__device__ __forceinline__ void load_bias32(const void* bias, int dtype, int64_t j0, int valid,
-                                            float (&bv)[32]) {
-  if (dtype == MB_F32) {
-    const float* p = static_cast<const float*>(bias) + j0;
-    if (valid == 32 && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+// The bias of a warp's NC 32-column chunks starting at column j0, one column
+// per lane per chunk (lane l holds column j0 + 32 c + l in bcol[c]; zero past
+// N or without bias). Loaded before the warp waits for its accumulator, so the
+// load latency overlaps the wait; the epilogue broadcasts each value across
+// the warp with shuffles.
+template <int NC>
+__device__ __forceinline__ void load_bias_cols(const GemmArgs& args, int64_t j0, int lane,
+                                               float (&bcol)[NC]) {
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const float4 f = __ldg(reinterpret_cast<const float4*>(p) + q);
-        bv[4 * q] = f.x; bv[4 * q + 1] = f.y; bv[4 * q + 2] = f.z; bv[4 * q + 3] = f.w;
-      }
-      return;
+  for (int c = 0; c < NC; ++c) {
+    const int64_t j = j0 + 32 * c + lane;
+    float v = 0.0f;
+    if (args.bias != nullptr && j < args.N) {
+      if (args.bias_dtype == MB_F32) v = __ldg(static_cast<const float*>(args.bias) + j);
+      else if (args.bias_dtype == MB_BF16) v = __bfloat162float(static_cast<const __nv_bfloat16*>(args.bias)[j]);
+      else v = __half2float(static_cast<const __half*>(args.bias)[j]);
     }
-#pragma unroll
-    for (int j = 0; j < 32; ++j) bv[j] = j < valid ? __ldg(p + j) : 0.0f;
-    return;
+    bcol[c] = v;
   }
-  const uint16_t* p = static_cast<const uint16_t*>(bias) + j0;
-  const bool is_bf16 = dtype == MB_BF16;
-  auto cvt = [is_bf16](uint32_t h) {
-    return is_bf16 ? __uint_as_float(h << 16) : __half2float(__ushort_as_half(uint16_t(h)));
-  };
-  if (valid == 32 && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint4 u = __ldg(reinterpret_cast<const uint4*>(p) + q);
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        bv[8 * q + 2 * h] = cvt(w[h] & 0xffffu);
-        bv[8 * q + 2 * h + 1] = cvt(w[h] >> 16);
-      }
-    }
-    return;
-  }
-#pragma unroll
-  for (int j = 0; j < 32; ++j) bv[j] = j < valid ? cvt(p[j]) : 0.0f;
 }
 
 template <typename TOut>
@@ -333,13 +314,14 @@ __device__ __forceinline__ void store_row32(TOut* dst, const float (&v)[32], int
   }
 }
 
-// One lane's row of a 32 x 32 output block into a staging slot laid out as
-// the bulk tensor store expects with a 128-byte (fp32 rows) or 64-byte
-// (16-bit rows) swizzle: 16-byte chunk q of row r sits at chunk
-// q ^ (r & 7) (128 B) or q ^ ((r >> 1) & 3) (64 B), so the 32 lanes of a
-// warp writing their rows hit distinct banks.
+// One lane's 32 values of output row r (a 32-column chunk) into a staging slot
+// of 32 rows x 128 bytes laid out as the bulk tensor store expects with the
+// 128-byte swizzle: 16-byte chunk q of row r sits at chunk q ^ (r & 7), so the
+// 32 lanes of a warp writing their rows hit distinct banks. fp32 chunks fill a
+// row; 16-bit chunks fill half `h` of it (two chunks per store, so every
+// store writes whole 128-byte lines).
 template <typename TOut>
-__device__ __forceinline__ void stage_row32(uint8_t* slot, int r, const float (&v)[32]) {
+__device__ __forceinline__ void stage_row32(uint8_t* slot, int r, int h, const float (&v)[32]) {
   if constexpr (std::is_same<TOut, float>::value) {
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
@@ -352,37 +334,41 @@ __device__ __forceinline__ void stage_row32(uint8_t* slot, int r, const float (&
     for (int q = 0; q < 4; ++q) {
       uint32_t w[4];
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        const float a = v[8 * q + 2 * h], b = v[8 * q + 2 * h + 1];
+      for (int e = 0; e < 4; ++e) {
+        const float a = v[8 * q + 2 * e], b = v[8 * q + 2 * e + 1];
         if constexpr (std::is_same<TOut, __nv_bfloat16>::value) {
           const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
-          w[h] = *reinterpret_cast<const uint32_t*>(&p);
+          w[e] = *reinterpret_cast<const uint32_t*>(&p);
         } else {
           const __half2 p = __floats2half2_rn(a, b);
-          w[h] = *reinterpret_cast<const uint32_t*>(&p);
+          w[e] = *reinterpret_cast<const uint32_t*>(&p);
         }
       }
-      const int pq = q ^ ((r >> 1) & 3);
-      *reinterpret_cast<uint4*>(slot + r * 64 + pq * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+      const int pq = (4 * h + q) ^ (r & 7);
+      *reinterpret_cast<uint4*>(slot + r * 128 + pq * 16) = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
 }
 
 // Epilogue of one tile for one warp: its 32 accumulator rows (TMEM lanes
-// taddr's quarter, columns b*BN ..) -> bias add in fp32 -> one rounding to TOut
+// taddr's quarter, columns b*BN ..) -> bias add in fp32 (bcol from
+// load_bias_cols) -> one rounding to TOut
 // -> global memory, either staged in swizzled shared memory and written with
-// bulk tensor stores (tma_store) or with direct row stores. TMEM loads are
+// bulk tensor stores of 32 rows x 128 bytes (tma_store: one store per 32 fp32
+// or 64 16-bit columns) or with direct row stores. TMEM loads are
 // double-buffered: chunk ci+1 loads while chunk ci is converted. With split K
-// (args.k_slices > 1) the tile goes to slice `slice` of the fp32 workspace
-// (a 3-D tensor map over [k_slices, M, ldc]).
+// (args.k_slices > 1, fp32 only) the tile goes to slice `slice` of the fp32
+// workspace (a 3-D tensor map over [k_slices, M, ldc]).
 template <typename TOut, int BN, int WARP_STAGE_BYTES = 2 * 32 * 32 * 4>
 __device__ __forceinline__ void drain_tile(uint32_t tbase, int64_t row0, int64_t col_tile0,
                                            int lane, const GemmArgs& args,
+                                           const float (&bcol)[BN / 32],
                                            const CUtensorMap* tma_c, uint8_t* slots,
                                            uint32_t& nstore, int slice) {
-  constexpr int kSlotBytes = 32 * 32 * int(sizeof(TOut));
-  // staging slots of this warp: WARP_STAGE_BYTES / slot size
-  constexpr int kSlots = WARP_STAGE_BYTES / kSlotBytes;
+  constexpr int kPerStore = sizeof(TOut) == 4 ? 1 : 2;  // 32-column chunks per store
+  constexpr int kSlotBytes = 32 * 128;
+  constexpr int kSlots = WARP_STAGE_BYTES / kSlotBytes;  // staging slots of this warp
+  static_assert(kSlots >= 1 && (BN / 32) % kPerStore == 0, "epilogue staging layout");
   const bool has_bias = args.bias != nullptr;
   const bool vec_ok = args.vec_ok != 0;
   const bool use_tma = args.tma_store != 0;
@@ -390,6 +376,7 @@ __device__ __forceinline__ void drain_tile(uint32_t tbase, int64_t row0, int64_t
   const bool sliced = args.k_slices > 1;
   TOut* crow = static_cast<TOut*>(args.C) + (row + (sliced ? slice * args.M : 0)) * args.ldc;
   uint32_t r[2][32];
+  uint8_t* slot = slots;
   tmem_ld32_issue(tbase, r[0]);
 #pragma unroll
   for (int ci = 0; ci < BN / 32; ++ci) {
@@ -398,32 +385,37 @@ __device__ __forceinline__ void drain_tile(uint32_t tbase, int64_t row0, int64_t
     if (ci + 1 < BN / 32) tmem_ld32_issue(tbase + c + 32, r[(ci + 1) & 1]);  // overlap the next
     const uint32_t(&rc)[32] = r[ci & 1];
     const int64_t col0 = col_tile0 + c;
-    const int valid = static_cast<int>(imin64(32, args.N - col0));
-    if (valid <= 0 || row0 >= args.M) continue;  // warp-uniform
+    const int64_t store_col0 = col_tile0 + (ci / kPerStore) * kPerStore * 32;
+    if (store_col0 >= args.N || row0 >= args.M) continue;  // warp-uniform
+    const int valid = col0 < args.N ? static_cast<int>(imin64(32, args.N - col0)) : 0;
     float v[32];
     if (has_bias) {
-      float bv[32];
-      load_bias32(args.bias, args.bias_dtype, col0, valid, bv);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(rc[j]) + bv[j];
+      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(rc[j]) + __shfl_sync(0xffffffffu, bcol[ci], j);
     } else {
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(rc[j]);
     }
     if (use_tma) {
-      // the slot used kSlots stores ago must have been read out
-      if (lane == 0) tma_store_wait_read<kSlots - 1>();
-      __syncwarp();
-      uint8_t* slot = slots + (nstore % kSlots) * kSlotBytes;
-      stage_row32<TOut>(slot, lane, v);
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        if (sliced) tma_store_3d(tma_c, slot, static_cast<int>(col0), static_cast<int>(row0), slice);
-        else tma_store_2d(tma_c, slot, static_cast<int>(col0), static_cast<int>(row0));
+      const int part = ci % kPerStore;
+      if (part == 0) {
+        // the slot used kSlots stores ago must have been read out
+        if (lane == 0) tma_store_wait_read<kSlots - 1>();
+        __syncwarp();
+        slot = slots + (nstore % kSlots) * kSlotBytes;
       }
-      ++nstore;
-    } else if (row < args.M) {
+      // columns past N are staged too; the store does not write them
+      stage_row32<TOut>(slot, lane, part, v);
+      if (part == kPerStore - 1) {
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (sliced) tma_store_3d(tma_c, slot, static_cast<int>(store_col0), static_cast<int>(row0), slice);
+          else tma_store_2d(tma_c, slot, static_cast<int>(store_col0), static_cast<int>(row0));
+        }
+        ++nstore;
+      }
+    } else if (row < args.M && valid > 0) {
       store_row32<TOut>(crow + col0, v, valid, vec_ok);
     }
   }
@@ -564,13 +556,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t local = 0;
     for (int64_t unit = blockIdx.x; unit < units; unit += gridDim.x, ++local) {
       const uint32_t b = local & 1;
-      if (!mbar_wait_bounded(&acc_full[b], (local >> 1) & 1)) break;
-      tc_fence_after();
       const int64_t tile = unit % tiles;
       const int64_t tm = tile / n_tiles;
       const int64_t tn = tile % n_tiles;
+      float bcol[BN / 32];
+      load_bias_cols(args, tn * BN, lane, bcol);
+      if (!mbar_wait_bounded(&acc_full[b], (local >> 1) & 1)) break;
+      tc_fence_after();
       drain_tile<TOut, BN>(tmem_base + (uint32_t(quarter * 32) << 16) + b * BN,
-                           tm * kBM + quarter * 32, tn * BN, lane, args, &tma_c, slots,
+                           tm * kBM + quarter * 32, tn * BN, lane, args, bcol, &tma_c, slots,
                            nstore, static_cast<int>(unit / tiles));
       tc_fence_before();
       __syncwarp();
@@ -618,8 +612,8 @@ struct Layout2 {
   static constexpr int kABytes = 128 * kBK * 2;  // this CTA's A rows
   static constexpr int kBBytes = 128 * kBK * 2;  // this CTA's B rows
   static constexpr int kStageBytes = kABytes + kBBytes;
-  // epilogue staging per warp: one 32 x 32 fp32 block or two 16-bit blocks
-  static constexpr int kEpiWarpBytes = 32 * 32 * 4;
+  // epilogue staging per warp: one block of 32 rows x 128 bytes
+  static constexpr int kEpiWarpBytes = 32 * 128;
   static constexpr int kEpiBytes = k2EpiWarps * kEpiWarpBytes;
   static constexpr int kBarrierBytes = 256;
   static constexpr size_t kSmem =
@@ -858,15 +852,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
     uint32_t local = 0;
     for (int64_t unit = pair; unit < units; unit += pairs, ++local) {
       const uint32_t b = local & 1;
-      if (!mbar_wait_bounded(&acc_full[b], (local >> 1) & 1)) break;
-      tc_fence_after();
       const int64_t tile = unit % tiles;
       const int64_t tm = tile / n_tiles;
       const int64_t tn = tile % n_tiles;
+      const int64_t col_tile0 = tn * k2BN + half * (k2BN / 2);
+      float bcol[k2BN / 2 / 32];
+      load_bias_cols(args, col_tile0, lane, bcol);
+      if (!mbar_wait_bounded(&acc_full[b], (local >> 1) & 1)) break;
+      tc_fence_after();
       drain_tile<TOut, k2BN / 2, L::kEpiWarpBytes>(
           tmem_base + (uint32_t(quarter * 32) << 16) + b * k2BN + half * (k2BN / 2),
-          tm * k2BM + int64_t(rank) * 128 + quarter * 32, tn * k2BN + half * (k2BN / 2), lane,
-          args, &tma_c, slots, nstore, static_cast<int>(unit / tiles));
+          tm * k2BM + int64_t(rank) * 128 + quarter * 32, col_tile0, lane, args, bcol, &tma_c,
+          slots, nstore, static_cast<int>(unit / tiles));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(cluster_addr(smem_addr(&acc_empty[b]), 0));
@@ -925,7 +922,8 @@ bool make_operand_map(CUtensorMap* map, const Operand& op, int64_t mn, int64_t k
 }
 
 // 2-D map over C[M, N] (leading dimension ldc elements) for the epilogue's
-// bulk tensor stores: box 32 x 32, swizzle matching stage_row32.
+// bulk tensor stores: boxes of 32 rows x 128 bytes (32 fp32 or 64 16-bit
+// columns), 128-byte swizzle matching stage_row32.
 bool make_c_map(CUtensorMap* map, void* ptr, int64_t M, int64_t N, int64_t ldc, int out_dtype) {
   auto fn = encode_fn();
   if (fn == nullptr) return false;
@@ -933,14 +931,14 @@ bool make_c_map(CUtensorMap* map, void* ptr, int64_t M, int64_t N, int64_t ldc, 
   if (!aligned_to(ptr, 16) || (ldc * elt) % 16 != 0) return false;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldc * elt)};
-  cuuint32_t box[2] = {32, 32};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / elt), 32};
   cuuint32_t estride[2] = {1, 1};
   const CUtensorMapDataType dt = out_dtype == MB_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                  : out_dtype == MB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const CUresult r = fn(map, dt, 2, ptr, dims, strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        elt == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
-                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
