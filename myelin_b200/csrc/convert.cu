@@ -256,28 +256,42 @@ namespace {
 constexpr int kSmallK = 32;
 constexpr int kSmallRows = 32;
 
+// C[m, n] = sum_k A[m, k] * B[n, k] for K <= KP (KP = 8, 16 or 32): one thread
+// per output column n holds B's row n in registers, the block's kSmallRows
+// rows of A sit in shared memory, both zero-padded to KP, and k is summed in
+// order with fmaf. The padded terms add 0 * 0 to an accumulator that is never
+// -0 (it starts at +0 and round-to-nearest sums give +0 for x + -x), so they
+// change nothing. Each row of A is read as KP / 4 broadcast 16-byte loads.
+template <int KP>
 __global__ void gemm_small_k_kernel(const float* __restrict__ A, int64_t lda,
                                     const float* __restrict__ B, int64_t ldb, float* __restrict__ C,
                                     int64_t ldc, int64_t M, int64_t N, int K) {
-  __shared__ float sa[kSmallRows][kSmallK];
+  __shared__ __align__(16) float sa[kSmallRows][KP];
   const int64_t n = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t m0 = int64_t(blockIdx.y) * kSmallRows;
-  for (int i = threadIdx.x; i < kSmallRows * kSmallK; i += blockDim.x) {
-    const int r = i / kSmallK, k = i % kSmallK;
+  for (int i = threadIdx.x; i < kSmallRows * KP; i += blockDim.x) {
+    const int r = i / KP, k = i % KP;
     sa[r][k] = (m0 + r < M && k < K) ? A[(m0 + r) * lda + k] : 0.0f;
   }
-  float b[kSmallK];
+  float b[KP];
 #pragma unroll
-  for (int k = 0; k < kSmallK; ++k) b[k] = (n < N && k < K) ? B[n * ldb + k] : 0.0f;
+  for (int k = 0; k < KP; ++k) b[k] = (n < N && k < K) ? B[n * ldb + k] : 0.0f;
   __syncthreads();
   if (n >= N) return;
-  for (int r = 0; r < kSmallRows && m0 + r < M; ++r) {
+  const int rows = static_cast<int>(M - m0 < kSmallRows ? M - m0 : kSmallRows);
+  float* c = C + m0 * ldc + n;
+#pragma unroll 4
+  for (int r = 0; r < rows; ++r) {
     float acc = 0.0f;
 #pragma unroll
-    for (int k = 0; k < kSmallK; ++k) {
-      if (k < K) acc = __fmaf_rn(sa[r][k], b[k], acc);
+    for (int q = 0; q < KP / 4; ++q) {
+      const float4 a = *reinterpret_cast<const float4*>(&sa[r][4 * q]);
+      acc = __fmaf_rn(a.x, b[4 * q], acc);
+      acc = __fmaf_rn(a.y, b[4 * q + 1], acc);
+      acc = __fmaf_rn(a.z, b[4 * q + 2], acc);
+      acc = __fmaf_rn(a.w, b[4 * q + 3], acc);
     }
-    C[(m0 + r) * ldc + n] = acc;
+    c[r * ldc] = acc;
   }
 }
 
@@ -293,8 +307,11 @@ extern "C" int mb_gemm_small_k(const float* A, int64_t lda, const float* B, int6
   if (M == 0 || N == 0) return 0;
   MB_CHECK_ARG(A != nullptr && B != nullptr && C != nullptr, "mb_gemm_small_k: null pointer");
   const dim3 grid(static_cast<unsigned>(ceil_div(N, 256)), static_cast<unsigned>(ceil_div(M, kSmallRows)));
-  gemm_small_k_kernel<<<grid, 256, 0, as_stream(stream)>>>(A, lda, B, ldb, C, ldc, M, N,
-                                                           static_cast<int>(K));
+  cudaStream_t s = as_stream(stream);
+  const int k = static_cast<int>(K);
+  if (K <= 8) gemm_small_k_kernel<8><<<grid, 256, 0, s>>>(A, lda, B, ldb, C, ldc, M, N, k);
+  else if (K <= 16) gemm_small_k_kernel<16><<<grid, 256, 0, s>>>(A, lda, B, ldb, C, ldc, M, N, k);
+  else gemm_small_k_kernel<kSmallK><<<grid, 256, 0, s>>>(A, lda, B, ldb, C, ldc, M, N, k);
   MB_CHECK_LAUNCH("mb_gemm_small_k");
   return 0;
 }

@@ -295,8 +295,7 @@ __global__ void __launch_bounds__(kThreads, MINB) scan_fwd_fast_kernel(
     }
     if (last_warp_done(&done[s])) {
       if (kDense && (MODE != kFwdAny || do_dense)) {
-        tma_store_box_2d_hint(&out_map, stage, static_cast<int>(e0), static_cast<int>(k * kChunk),
-                              l2_evict_first_policy());
+        tma_store_box_2d(&out_map, stage, static_cast<int>(e0), static_cast<int>(k * kChunk));
         bulk_wait_read_all();  // the stage may be refilled once the store has read it
       }
       if (k + kRing < K) refill(k + kRing);
@@ -487,8 +486,7 @@ __global__ void __launch_bounds__(kThreads, MINB) scan_bwd_fast_kernel(
     // the warp done last with the chunk writes grad_x (it overwrote x in the
     // stage) and refills the stage with the chunk kRing further back
     if (last_warp_done(&done[s])) {
-      tma_store_box_2d_hint(&out_map, stage_x(s), static_cast<int>(e0), static_cast<int>(t0),
-                            l2_evict_first_policy());
+      tma_store_box_2d(&out_map, stage_x(s), static_cast<int>(e0), static_cast<int>(t0));
       bulk_wait_read_all();
       if (i + kRing < K) refill(i + kRing);
     }

@@ -39,27 +39,6 @@ __device__ __forceinline__ void tma_store_box_2d(const CUtensorMap* map, const v
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
 
-// L2 policy for data that is written once and not read again by the same
-// kernel: its lines are the first candidates for eviction, so a kernel's
-// streamed output is written back while the kernel runs instead of being left
-// dirty in L2 for the next kernel to flush.
-__device__ __forceinline__ uint64_t l2_evict_first_policy() {
-  uint64_t pol;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
-  return pol;
-}
-
-// tma_store_box_2d with an L2 cache policy (e.g. l2_evict_first_policy()).
-__device__ __forceinline__ void tma_store_box_2d_hint(const CUtensorMap* map, const void* src, int c0,
-                                                      int c1, uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%1, %2}], [%3], %4;" ::"l"(
-          reinterpret_cast<uint64_t>(map)),
-      "r"(c0), "r"(c1), "r"(static_cast<uint32_t>(__cvta_generic_to_shared(src))), "l"(policy)
-      : "memory");
-  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-}
-
 // 2-D bulk tensor load of one box at (c0, c1) into dense shared memory (128-byte
 // aligned), completing as transaction bytes on the mbarrier `bar`. The whole
 // box is written: elements outside the tensor read as zero, and the

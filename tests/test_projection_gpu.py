@@ -143,6 +143,26 @@ def test_transposed_and_strided_operands_are_relaid_out():
     _check(cur.float(), (x.float() @ w.float()).bfloat16().float(), 1e-2, "transposed weight")
 
 
+@pytest.mark.parametrize("K", [1, 7, 8, 10, 16, 17, 32])
+def test_small_k_fp32_kernel_within_k_roundings(K):
+    """``mb_gemm_small_k`` (narrow fp32 layers' input gradient) for K in every
+    padding bucket (8, 16, 32) and ragged M and N, against float64 products:
+    an in-order fmaf sum of K terms is within K * 2^-23 of the sum of the
+    products' magnitudes."""
+
+    gen = torch.Generator(device=DEV).manual_seed(40 + K)
+    M, N = 70, 300
+    a = _rand((M, K), gen)
+    b = _rand((N, K), gen)
+    out = torch.full((M, N), float("nan"), device=DEV)
+    nat.gemm_small_k(a, b, out)
+    torch.cuda.synchronize()
+    ref = a.double() @ b.double().t()
+    mag = a.double().abs() @ b.double().abs().t()
+    assert torch.isfinite(out).all()
+    assert ((out.double() - ref).abs() <= mag * (K * 2.0 ** -23) + 1e-30).all()
+
+
 def test_mb_gemm_rejects_m_major_a_with_k_major_b():
     lib = nat.lib()
     a = torch.zeros((64, 64), dtype=torch.bfloat16, device=DEV)
