@@ -388,6 +388,129 @@ __global__ void __launch_bounds__(kPackCountThreads) pack_count_u8_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// Full-row variant of the fused kernel for the exchange: a block's THREADS
+// threads cover every word column of its rows (W == THREADS), so the words of
+// kRowUnroll consecutive rows are one contiguous run of kRowUnroll * W words
+// in every destination (this rank's slot in its own gather buffer and in each
+// peer's). The threads stage each group of rows in shared memory and one
+// thread sends the group to all NDST destinations as bulk copies
+// (cp.async.bulk shared -> global, no multicast), so NVLink carries runs of
+// kRowUnroll * W * 4 bytes instead of one 128-byte warp store per row and
+// peer, and the threads go on packing the next group while the copies drain.
+// Two staging buffers alternate; a buffer is rewritten only after the copies
+// of two groups ago have read it. Counting is the same as in
+// pack_count_u8_kernel.
+// ---------------------------------------------------------------------------
+constexpr int kMaxDstSlots = 1 + kMaxPeerSlots;
+struct DstSlots {
+  uint32_t* p[kMaxDstSlots];
+};
+
+__device__ __forceinline__ void rows_fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+template <int THREADS, int NDST>
+__global__ void __launch_bounds__(THREADS) pack_count_rows_kernel(
+    const uint4* __restrict__ in, const DstSlots dst, unsigned long long* __restrict__ counts64,
+    unsigned int* __restrict__ counts32, int64_t rows, int64_t rows_per_slice) {
+  extern __shared__ __align__(128) unsigned char rows_smem[];
+  constexpr int kStageWords = kRowUnroll * THREADS;
+  uint32_t* stage = reinterpret_cast<uint32_t*>(rows_smem);           // [2][kRowUnroll][THREADS]
+  auto cnt = reinterpret_cast<int32_t(*)[THREADS + 1]>(rows_smem + 2 * kStageWords * 4);
+  const int tid = threadIdx.x;
+  const int64_t r_begin = int64_t(blockIdx.x) * rows_per_slice;
+  const int64_t r_end = imin64(rows, r_begin + rows_per_slice);
+
+#pragma unroll
+  for (int k = 0; k < 32; ++k) cnt[k][tid] = 0;
+  uint32_t acc[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) acc[q] = 0;
+  int pending = 0;
+  auto flush = [&]() {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) cnt[4 * q + k][tid] += (acc[q] >> (8 * k)) & 0xffu;
+      acc[q] = 0;
+    }
+    pending = 0;
+  };
+
+  const uint4* src = in + tid * 2;  // 2 x 16 bytes of every row
+  constexpr int64_t row_vec = THREADS * 2;
+  int group = 0;
+  for (int64_t r = r_begin; r < r_end; r += kRowUnroll, ++group) {
+    const int nr = static_cast<int>(imin64(kRowUnroll, r_end - r));
+    uint32_t* st = stage + (group & 1) * kStageWords;
+    if (group >= 2) {
+      // the copies of two groups ago have read this buffer
+      if (tid == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+      __syncthreads();
+    }
+    uint4 lo[kRowUnroll], hi[kRowUnroll];
+#pragma unroll
+    for (int u = 0; u < kRowUnroll; ++u) {
+      if (u < nr) {
+        lo[u] = src[(r + u) * row_vec];
+        hi[u] = src[(r + u) * row_vec + 1];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kRowUnroll; ++u) {
+      if (u < nr) {
+        const uint32_t v[8] = {lo[u].x, lo[u].y, lo[u].z, lo[u].w, hi[u].x, hi[u].y, hi[u].z, hi[u].w};
+        uint32_t word = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const uint32_t b = nonzero_bytes(v[q]);
+          word |= ((b * 0x01020408u) >> 24) << (4 * q);
+          acc[q] += b;
+        }
+        st[u * THREADS + tid] = word;
+      }
+    }
+    pending += nr;
+    if (pending > 255 - kRowUnroll) flush();
+    rows_fence_proxy_async();  // this thread's staged words, before the copies read them
+    __syncthreads();
+    if (tid == 0) {
+      const uint32_t bytes = static_cast<uint32_t>(nr) * THREADS * 4u;
+#pragma unroll
+      for (int d = 0; d < NDST; ++d) {
+        asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(
+                         dst.p[d] + r * THREADS),
+                     "r"(static_cast<uint32_t>(__cvta_generic_to_shared(st))), "r"(bytes)
+                     : "memory");
+      }
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+  }
+  if (tid == 0) {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // every copy has landed
+    __threadfence_system();  // and is ordered before the kernel's end for the other GPUs
+  }
+  flush();
+  __syncthreads();
+  const int w = tid >> 5, lane = tid & 31;
+  for (int j = 0; j < 32; ++j) {
+    const int t = 32 * w + j;
+    const unsigned int v = static_cast<unsigned int>(cnt[lane][t]);
+    const int64_t neuron = int64_t(t) * 32 + lane;
+    if (v != 0) {
+      if (counts64) atomicAdd(counts64 + neuron, static_cast<unsigned long long>(v));
+      if (counts32) atomicAdd(counts32 + neuron, v);
+    }
+  }
+}
+
+template <int THREADS>
+constexpr size_t rows_kernel_smem() {
+  return size_t(2) * kRowUnroll * THREADS * 4 + size_t(32) * (THREADS + 1) * 4;
+}
+
+// ---------------------------------------------------------------------------
 // Host side.
 // ---------------------------------------------------------------------------
 static int grid_for(int64_t work_items, int block = 256) {
@@ -536,6 +659,69 @@ static void launch_pack_count_u8(const void* spikes, int32_t* words, const PeerS
     MB_PACK_PEERS(7)
 #undef MB_PACK_PEERS
     default: break;
+  }
+}
+
+// The full-row exchange kernel applies when a row is 128 or 256 words
+// (n = 4096 or 8192 neurons) and every destination is 16-byte aligned.
+static bool pack_count_rows_ok(int64_t n, int32_t* words, void* const* peers, int num_peers) {
+  const int64_t W = n / 32;
+  if (W != 128 && W != 256) return false;
+  if (!aligned_to(words, 16)) return false;
+  for (int d = 0; d < num_peers; ++d) {
+    if (!aligned_to(peers[d], 16)) return false;
+  }
+  return true;
+}
+
+template <int THREADS>
+static void launch_pack_count_rows_t(const void* spikes, const DstSlots& dst, int ndst,
+                                     int64_t rows, int64_t rows_per_slice, int64_t slices,
+                                     unsigned long long* c64, unsigned int* c32, cudaStream_t s) {
+  const auto* in = static_cast<const uint4*>(spikes);
+  constexpr size_t smem = rows_kernel_smem<THREADS>();
+  const unsigned grid = static_cast<unsigned>(slices);
+  switch (ndst) {
+#define MB_PACK_ROWS(K)                                                                        \
+  case K: {                                                                                    \
+    auto kern = pack_count_rows_kernel<THREADS, K>;                                            \
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));        \
+    kern<<<grid, THREADS, smem, s>>>(in, dst, c64, c32, rows, rows_per_slice);                 \
+    break;                                                                                     \
+  }
+    MB_PACK_ROWS(1)
+    MB_PACK_ROWS(2)
+    MB_PACK_ROWS(3)
+    MB_PACK_ROWS(4)
+    MB_PACK_ROWS(5)
+    MB_PACK_ROWS(6)
+    MB_PACK_ROWS(7)
+    MB_PACK_ROWS(8)
+#undef MB_PACK_ROWS
+    default: break;
+  }
+}
+
+// Rows per block: a multiple of kRowUnroll, at most 4 blocks per SM's worth
+// of slices, at least 16 rows per block.
+static void launch_pack_count_rows(const void* spikes, int32_t* words, void* const* peers,
+                                   int num_peers, int64_t rows, int64_t n, int64_t* counts64,
+                                   int32_t* counts32, cudaStream_t s) {
+  DstSlots dst{};
+  dst.p[0] = reinterpret_cast<uint32_t*>(words);
+  for (int d = 0; d < num_peers; ++d) dst.p[1 + d] = static_cast<uint32_t*>(peers[d]);
+  auto* c64 = reinterpret_cast<unsigned long long*>(counts64);
+  auto* c32 = reinterpret_cast<unsigned int*>(counts32);
+  if (c64) cudaMemsetAsync(c64, 0, size_t(n) * sizeof(int64_t), s);
+  if (c32) cudaMemsetAsync(c32, 0, size_t(n) * sizeof(int32_t), s);
+  int64_t slices = imin64(ceil_div(rows, 16), 148 * 4);
+  if (slices < 1) slices = 1;
+  const int64_t per = ceil_div(ceil_div(rows, slices), kRowUnroll) * kRowUnroll;
+  slices = ceil_div(rows, per);
+  if (n / 32 == 256) {
+    launch_pack_count_rows_t<256>(spikes, dst, 1 + num_peers, rows, per, slices, c64, c32, s);
+  } else {
+    launch_pack_count_rows_t<128>(spikes, dst, 1 + num_peers, rows, per, slices, c64, c32, s);
   }
 }
 
@@ -690,7 +876,10 @@ extern "C" int mb_pack_count_scatter(int dtype, const void* spikes, int32_t* wor
                "mb_pack_count_scatter: workspace of %lld bytes required, got %lld",
                (long long)need, (long long)workspace_bytes);
   MB_CHECK_ARG(aligned_to(workspace, 4), "mb_pack_count_scatter: workspace misaligned");
-  if (pack_count_fused_ok(dtype, spikes, n)) {
+  if (pack_count_fused_ok(dtype, spikes, n) && pack_count_rows_ok(n, words, peers, num_peers)) {
+    // whole rows per block: each group of rows goes to every slot as one bulk copy
+    launch_pack_count_rows(spikes, words, peers, num_peers, rows, n, counts64, counts32, s);
+  } else if (pack_count_fused_ok(dtype, spikes, n)) {
     PeerSlots slots{};
     for (int d = 0; d < num_peers; ++d) slots.p[d] = static_cast<uint32_t*>(peers[d]);
     launch_pack_count_u8(spikes, words, slots, num_peers, rows, n, counts64, counts32, s);

@@ -55,8 +55,12 @@ def test_scan_forward_packed_scatter_local_peers(shape, peers):
 
 
 @pytest.mark.parametrize("shape,peers", [
-    ((16, 8, 256), 7),   # fused pack kernel storing to 7 peer slots
-    ((6, 5, 70), 3),     # ragged N: pack + count, then the push
+    ((16, 8, 256), 7),     # fused pack kernel storing to 7 peer slots
+    ((6, 5, 70), 3),       # ragged N: pack + count, then the push
+    ((16, 8, 8192), 7),    # whole-row blocks (256 words), bulk copies to 8 slots
+    ((37, 5, 4096), 2),    # whole-row blocks (128 words), a ragged last group
+    ((128, 64, 8192), 1),  # many groups per block: both staging buffers reused
+    ((3, 1, 8192), 0),     # own slot only, fewer rows than one group
 ])
 def test_pack_count_scatter_local_peers(shape, peers):
     rows, n = shape[0] * shape[1], shape[2]
