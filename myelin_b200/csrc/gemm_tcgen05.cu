@@ -67,7 +67,49 @@ struct GemmArgs {
   // once share one slice's rows of both operands, which stay in L2.
   int k_slices;
   int kb_per_slice;
+  // Tail slicing (two-SM kernel, long K): units [0, full_units) are whole
+  // tiles 0 .. full_units-1, written to C; the remaining tiles (the last,
+  // partial wave) run as k_slices slices each, unit full_units + v being
+  // slice v / tail_tiles of tile full_units + v % tail_tiles, written as fp32
+  // partial sums through the second output map (a [k_slices, M - p_row0,
+  // ldp] workspace holding rows p_row0 .. M-1); a second kernel adds them into
+  // C. full_units == 0: the plain scheme above.
+  int64_t full_units;
+  int64_t p_row0;
 };
+
+// One work unit: its tile, K range and where its result goes.
+struct WorkUnit {
+  int64_t tile;
+  int slice;
+  int kb0, kb1;
+  bool partial;  // a slice of a tail tile (tail slicing): fp32 to the workspace
+};
+
+__device__ __forceinline__ int64_t unit_count(const GemmArgs& a, int64_t tiles) {
+  return a.full_units + (tiles - a.full_units) * a.k_slices;
+}
+
+__device__ __forceinline__ WorkUnit decode_unit(const GemmArgs& a, int64_t unit, int64_t tiles,
+                                                int kblocks) {
+  WorkUnit w;
+  const int64_t v = unit - a.full_units;
+  if (v < 0) {  // a whole tile of the full waves
+    w.tile = unit;
+    w.slice = 0;
+    w.kb0 = 0;
+    w.kb1 = kblocks;
+    w.partial = false;
+    return w;
+  }
+  const int64_t tail = tiles - a.full_units;
+  w.tile = a.full_units + v % tail;
+  w.slice = static_cast<int>(v / tail);
+  w.kb0 = w.slice * a.kb_per_slice;
+  w.kb1 = min(kblocks, w.kb0 + a.kb_per_slice);
+  w.partial = a.full_units > 0;
+  return w;
+}
 
 // Which segments this launch runs (bit q = segment q); read once per thread
 // that walks the K loop, so the copy and MMA threads agree.
@@ -359,21 +401,32 @@ __device__ __forceinline__ void stage_row32(uint8_t* slot, int r, int h, const f
 // double-buffered: chunk ci+1 loads while chunk ci is converted. With split K
 // (args.k_slices > 1, fp32 only) the tile goes to slice `slice` of the fp32
 // workspace (a 3-D tensor map over [k_slices, M, ldc]).
+// Where a drained tile goes: `map` (2-D over C, or 3-D over a slices
+// workspace when `sliced`, with tile row r stored at row r - row_base of the
+// slice); `bias`: add the bias columns.
+struct DrainTarget {
+  const CUtensorMap* map;
+  bool sliced;
+  bool bias;
+  int64_t row_base;
+};
+
 template <typename TOut, int BN, int WARP_STAGE_BYTES = 2 * 32 * 32 * 4>
 __device__ __forceinline__ void drain_tile(uint32_t tbase, int64_t row0, int64_t col_tile0,
                                            int lane, const GemmArgs& args,
-                                           const float (&bcol)[BN / 32],
-                                           const CUtensorMap* tma_c, uint8_t* slots,
-                                           uint32_t& nstore, int slice) {
+                                           const float (&bcol)[BN / 32], const DrainTarget& tgt,
+                                           uint8_t* slots, uint32_t& nstore, int slice) {
   constexpr int kPerStore = sizeof(TOut) == 4 ? 1 : 2;  // 32-column chunks per store
   constexpr int kSlotBytes = 32 * 128;
   constexpr int kSlots = WARP_STAGE_BYTES / kSlotBytes;  // staging slots of this warp
   static_assert(kSlots >= 1 && (BN / 32) % kPerStore == 0, "epilogue staging layout");
-  const bool has_bias = args.bias != nullptr;
+  const bool has_bias = tgt.bias;
   const bool vec_ok = args.vec_ok != 0;
   const bool use_tma = args.tma_store != 0;
   const int64_t row = row0 + lane;
-  const bool sliced = args.k_slices > 1;
+  const bool sliced = tgt.sliced;
+  const CUtensorMap* tma_c = tgt.map;
+  const int store_row0 = static_cast<int>(row0 - tgt.row_base);
   TOut* crow = static_cast<TOut*>(args.C) + (row + (sliced ? slice * args.M : 0)) * args.ldc;
   uint32_t r[2][32];
   uint8_t* slot = slots;
@@ -410,8 +463,8 @@ __device__ __forceinline__ void drain_tile(uint32_t tbase, int64_t row0, int64_t
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          if (sliced) tma_store_3d(tma_c, slot, static_cast<int>(store_col0), static_cast<int>(row0), slice);
-          else tma_store_2d(tma_c, slot, static_cast<int>(store_col0), static_cast<int>(row0));
+          if (sliced) tma_store_3d(tma_c, slot, static_cast<int>(store_col0), store_row0, slice);
+          else tma_store_2d(tma_c, slot, static_cast<int>(store_col0), store_row0);
         }
         ++nstore;
       }
@@ -443,7 +496,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t m_tiles = (args.M + kBM - 1) / kBM;
   const int64_t n_tiles = (args.N + BN - 1) / BN;
   const int64_t tiles = m_tiles * n_tiles;
-  const int64_t units = tiles * args.k_slices;  // (tile, K slice) work units
+  const int64_t units = unit_count(args, tiles);  // (tile, K slice) work units
   const int kblocks = static_cast<int>((args.K + kBK - 1) / kBK);
 
   if (threadIdx.x == 0) {
@@ -475,9 +528,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       const uint32_t segs = segment_mask(args);
       for (int64_t unit = blockIdx.x; unit < units && ok; unit += gridDim.x) {
-        const int64_t tile = unit % tiles;
-        const int kb0 = static_cast<int>(unit / tiles) * args.kb_per_slice;
-        const int kb1 = min(kblocks, kb0 + args.kb_per_slice);
+        const WorkUnit wu = decode_unit(args, unit, tiles, kblocks);
+        const int64_t tile = wu.tile;
+        const int kb0 = wu.kb0, kb1 = wu.kb1;
         const int64_t tm = tile / n_tiles;
         const int64_t tn = tile % n_tiles;
         // smallest products first: they are summed while the accumulator is small
@@ -513,8 +566,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0, local = 0;
       bool ok = true;
       for (int64_t unit = blockIdx.x; unit < units && ok; unit += gridDim.x, ++local) {
-        const int kb0 = static_cast<int>(unit / tiles) * args.kb_per_slice;
-        const int kb1 = min(kblocks, kb0 + args.kb_per_slice);
+        const WorkUnit wu = decode_unit(args, unit, tiles, kblocks);
+        const int kb0 = wu.kb0, kb1 = wu.kb1;
         const uint32_t b = local & 1;
         const uint32_t use_b = local >> 1;
         if (use_b > 0 && !mbar_wait_bounded(&acc_empty[b], (use_b - 1) & 1)) break;
@@ -556,16 +609,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t local = 0;
     for (int64_t unit = blockIdx.x; unit < units; unit += gridDim.x, ++local) {
       const uint32_t b = local & 1;
-      const int64_t tile = unit % tiles;
-      const int64_t tm = tile / n_tiles;
-      const int64_t tn = tile % n_tiles;
+      const WorkUnit wu = decode_unit(args, unit, tiles, kblocks);
+      const int64_t tm = wu.tile / n_tiles;
+      const int64_t tn = wu.tile % n_tiles;
       float bcol[BN / 32];
       load_bias_cols(args, tn * BN, lane, bcol);
       if (!mbar_wait_bounded(&acc_full[b], (local >> 1) & 1)) break;
       tc_fence_after();
+      const DrainTarget tgt{&tma_c, args.k_slices > 1, args.bias != nullptr, 0};
       drain_tile<TOut, BN>(tmem_base + (uint32_t(quarter * 32) << 16) + b * BN,
-                           tm * kBM + quarter * 32, tn * BN, lane, args, bcol, &tma_c, slots,
-                           nstore, static_cast<int>(unit / tiles));
+                           tm * kBM + quarter * 32, tn * BN, lane, args, bcol, tgt, slots,
+                           nstore, wu.slice);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
@@ -712,7 +766,8 @@ template <typename TIn, typename TOut, bool A_MN, bool B_MN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
     gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
                         const __grid_constant__ CUtensorMap tma_b,
-                        const __grid_constant__ CUtensorMap tma_c, const __grid_constant__ GemmArgs args) {
+                        const __grid_constant__ CUtensorMap tma_c, const __grid_constant__ GemmArgs args,
+                        const __grid_constant__ CUtensorMap tma_p) {
   using L = Layout2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -735,7 +790,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
   const int64_t m_tiles = (args.M + k2BM - 1) / k2BM;
   const int64_t n_tiles = (args.N + k2BN - 1) / k2BN;
   const int64_t tiles = m_tiles * n_tiles;
-  const int64_t units = tiles * args.k_slices;  // (tile, K slice) work units
+  const int64_t units = unit_count(args, tiles);  // (tile, K slice) work units
   const int kblocks = static_cast<int>((args.K + kBK - 1) / kBK);
 
   if (threadIdx.x == 0) {
@@ -767,9 +822,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
       bool ok = true;
       const uint32_t segs = segment_mask(args);
       for (int64_t unit = pair; unit < units && ok; unit += pairs) {
-        const int64_t tile = unit % tiles;
-        const int kb0 = static_cast<int>(unit / tiles) * args.kb_per_slice;
-        const int kb1 = min(kblocks, kb0 + args.kb_per_slice);
+        const WorkUnit wu = decode_unit(args, unit, tiles, kblocks);
+        const int64_t tile = wu.tile;
+        const int kb0 = wu.kb0, kb1 = wu.kb1;
         const int64_t tm = tile / n_tiles;
         const int64_t tn = tile % n_tiles;
         for (int q = args.nseg - 1; q >= 0 && ok; --q) {
@@ -807,8 +862,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
       uint32_t it = 0, local = 0;
       bool ok = true;
       for (int64_t unit = pair; unit < units && ok; unit += pairs, ++local) {
-        const int kb0 = static_cast<int>(unit / tiles) * args.kb_per_slice;
-        const int kb1 = min(kblocks, kb0 + args.kb_per_slice);
+        const WorkUnit wu = decode_unit(args, unit, tiles, kblocks);
+        const int kb0 = wu.kb0, kb1 = wu.kb1;
         const uint32_t b = local & 1;
         const uint32_t use_b = local >> 1;
         if (use_b > 0 && !mbar_wait_bounded(&acc_empty[b], (use_b - 1) & 1)) break;
@@ -852,18 +907,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
     uint32_t local = 0;
     for (int64_t unit = pair; unit < units; unit += pairs, ++local) {
       const uint32_t b = local & 1;
-      const int64_t tile = unit % tiles;
-      const int64_t tm = tile / n_tiles;
-      const int64_t tn = tile % n_tiles;
+      const WorkUnit wu = decode_unit(args, unit, tiles, kblocks);
+      const int64_t tm = wu.tile / n_tiles;
+      const int64_t tn = wu.tile % n_tiles;
       const int64_t col_tile0 = tn * k2BN + half * (k2BN / 2);
+      const uint32_t taddr = tmem_base + (uint32_t(quarter * 32) << 16) + b * k2BN + half * (k2BN / 2);
+      const int64_t row0 = tm * k2BM + int64_t(rank) * 128 + quarter * 32;
       float bcol[k2BN / 2 / 32];
       load_bias_cols(args, col_tile0, lane, bcol);
       if (!mbar_wait_bounded(&acc_full[b], (local >> 1) & 1)) break;
       tc_fence_after();
-      drain_tile<TOut, k2BN / 2, L::kEpiWarpBytes>(
-          tmem_base + (uint32_t(quarter * 32) << 16) + b * k2BN + half * (k2BN / 2),
-          tm * k2BM + int64_t(rank) * 128 + quarter * 32, col_tile0, lane, args, bcol, &tma_c,
-          slots, nstore, static_cast<int>(unit / tiles));
+      if (wu.partial) {
+        // a slice of a tail tile: fp32 partial sums to the workspace (no bias)
+        const DrainTarget tgt{&tma_p, true, false, args.p_row0};
+        drain_tile<float, k2BN / 2, L::kEpiWarpBytes>(taddr, row0, col_tile0, lane, args, bcol,
+                                                      tgt, slots, nstore, wu.slice);
+      } else {
+        const DrainTarget tgt{&tma_c, args.k_slices > 1 && args.full_units == 0,
+                              args.bias != nullptr, 0};
+        drain_tile<TOut, k2BN / 2, L::kEpiWarpBytes>(taddr, row0, col_tile0, lane, args, bcol,
+                                                     tgt, slots, nstore, wu.slice);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(cluster_addr(smem_addr(&acc_empty[b]), 0));
@@ -980,6 +1044,34 @@ __global__ void slices_reduce_kernel(const float* __restrict__ partial, int slic
   }
 }
 
+// The tail tiles of a tail-sliced launch: for every element of rows
+// p_row0 .. M-1 whose tile index is >= full_units, the sum of its slices'
+// partial sums in slice order (+ bias), one rounding to TOut. Elements of
+// whole tiles in those rows are left as the GEMM wrote them.
+template <typename TOut>
+__global__ void tail_reduce_kernel(const float* __restrict__ partial, int slices, int64_t M,
+                                   int64_t N, int64_t pld, int64_t p_row0, int64_t full_units,
+                                   int64_t n_tiles, const void* bias, int bias_dtype,
+                                   TOut* __restrict__ C, int64_t ldc) {
+  const int64_t rows = M - p_row0;
+  const int64_t total = rows * N;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = i / N;
+    const int64_t n = i - r * N;
+    const int64_t m = p_row0 + r;
+    if ((m / k2BM) * n_tiles + n / k2BN < full_units) continue;
+    float acc = 0.0f;
+    for (int sl = 0; sl < slices; ++sl) acc += partial[(sl * rows + r) * pld + n];
+    if (bias != nullptr) {
+      if (bias_dtype == MB_F32) acc += static_cast<const float*>(bias)[n];
+      else if (bias_dtype == MB_BF16) acc += __bfloat162float(static_cast<const __nv_bfloat16*>(bias)[n]);
+      else acc += __half2float(static_cast<const __half*>(bias)[n]);
+    }
+    C[m * ldc + n] = Elem<TOut>::from_f(acc);
+  }
+}
+
 int sm_count();
 
 // K slices for a launch (each slice's partial sums go to an fp32 workspace and
@@ -993,6 +1085,8 @@ int sm_count();
 //    and K is long (a weight gradient of a narrow or small layer: K = T * B),
 //    K is split until the (tile, slice) units fill the SMs, each slice at
 //    least kMinSliceKBlocks k-blocks long.
+// (Long K with many tiles is handled by tail slicing, tail_plan below, from
+// kWaveSliceKBlocks k-blocks on.)
 constexpr int kSliceKBlocks = 32;     // K = 2048 per slice
 constexpr int kMinSliceKBlocks = 8;   // K = 512
 constexpr int kWaveSliceKBlocks = 128;  // K = 8192
@@ -1011,21 +1105,6 @@ int k_slices_for(int64_t M, int64_t N, int64_t K, int a_parts, int b_parts, int 
     const int64_t want = (sms + tiles - 1) / tiles;
     const int64_t most = kblocks / kMinSliceKBlocks;
     slices = static_cast<int>(std::max<int64_t>(slices, std::min(want, most)));
-  } else if (occupancy && slices == 1 && kblocks >= kWaveSliceKBlocks && M >= 256 && N >= 256) {
-    // long K on the pair kernel (a weight gradient, K = T * B): split K in up
-    // to 4 when that evens out the last wave of pair units by 5 % or more
-    // (256 pair tiles on 74 pairs run 3.46 waves: 86 %; in 2 slices 6.92: 99 %)
-    const int64_t pairs = sms / 2;
-    const int64_t ptiles = ((M + 255) / 256) * ((N + 255) / 256);
-    auto eff = [&](int64_t sl) {
-      const int64_t units = ptiles * sl;
-      return double(units) / double(((units + pairs - 1) / pairs) * pairs);
-    };
-    int best = 1;
-    for (int sl = 2; sl <= 4; ++sl) {
-      if (eff(sl) >= eff(best) + 0.05) best = sl;
-    }
-    slices = best;
   }
   const int per = (kblocks + slices - 1) / slices;
   *kb_per_slice = per;
@@ -1033,6 +1112,42 @@ int k_slices_for(int64_t M, int64_t N, int64_t K, int a_parts, int b_parts, int 
 }
 
 int64_t slices_pld(int64_t N) { return (N + 3) / 4 * 4; }
+
+// Tail slicing for long K on the two-SM kernel (a weight gradient, K = T * B):
+// the whole waves of pair tiles run unsliced, and only the tiles of the last,
+// partial wave are split into `slices` K slices (as many as fit one wave of
+// pairs, at most 4), so that wave ends after 1/slices of a tile's time. (256
+// pair tiles on 74 pairs: 3 whole waves of 74 tiles, then 34 tiles x 2
+// slices; slicing every tile instead wrote and re-read fp32 partials of the
+// whole output.) Their partial sums go to a workspace covering rows p_row0 ..
+// M-1 of the output.
+struct TailPlan {
+  int64_t full_units = 0;
+  int slices = 1;
+  int kb_per_slice = 0;
+  int64_t p_row0 = 0;
+};
+
+bool tail_plan(int64_t M, int64_t N, int64_t K, TailPlan* plan) {
+  const int kblocks = static_cast<int>((K + kBK - 1) / kBK);
+  if (kblocks < kWaveSliceKBlocks || M < k2BM || N < k2BN) return false;
+  const int64_t pairs = sm_count() / 2;
+  const int64_t n_tiles = (N + k2BN - 1) / k2BN;
+  const int64_t ptiles = ((M + k2BM - 1) / k2BM) * n_tiles;
+  const int64_t tail = ptiles % pairs;
+  if (ptiles <= pairs || tail == 0) return false;
+  const int slices = static_cast<int>(std::min<int64_t>(4, pairs / tail));
+  if (slices < 2 || kblocks / slices < kMinSliceKBlocks) return false;
+  plan->full_units = ptiles - tail;
+  plan->slices = slices;
+  plan->kb_per_slice = (kblocks + slices - 1) / slices;
+  plan->p_row0 = (plan->full_units / n_tiles) * k2BM;
+  return true;
+}
+
+int64_t tail_workspace_bytes(int64_t M, int64_t N, const TailPlan& plan) {
+  return int64_t(plan.slices) * (M - plan.p_row0) * slices_pld(N) * int64_t(sizeof(float));
+}
 
 int sm_count() {
   int dev = 0, n = 148;
@@ -1054,13 +1169,14 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb_, const CUtensorMap& mc,
 
 template <typename TIn, typename TOut, bool A_MN, bool B_MN>
 int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb_, const CUtensorMap& mc,
-                const GemmArgs& args, cudaStream_t s) {
+                const CUtensorMap& mp, const GemmArgs& args, cudaStream_t s) {
   auto kern = gemm_tn_pair_kernel<TIn, TOut, A_MN, B_MN>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        static_cast<int>(Layout2::kSmem));
   const int64_t tiles = ((args.M + k2BM - 1) / k2BM) * ((args.N + k2BN - 1) / k2BN);
-  const int pairs = static_cast<int>(imin64(tiles * args.k_slices, sm_count() / 2));
-  kern<<<2 * pairs, k2Threads, Layout2::kSmem, s>>>(ma, mb_, mc, args);
+  const int64_t units = args.full_units + (tiles - args.full_units) * args.k_slices;
+  const int pairs = static_cast<int>(imin64(units, sm_count() / 2));
+  kern<<<2 * pairs, k2Threads, Layout2::kSmem, s>>>(ma, mb_, mc, args, mp);
   return 0;
 }
 
@@ -1083,10 +1199,25 @@ bool use_pair(const GemmArgs& args, int64_t k_eff, bool out_f32) {
 
 template <typename TIn, typename TOut, bool A_MN, bool B_MN>
 int launch_majors(const Operand& A, const Operand& B, GemmArgs args, int out_dtype,
-                  cudaStream_t s) {
+                  void* partials, cudaStream_t s) {
   const bool bf16 = std::is_same<TIn, __nv_bfloat16>::value;
-  CUtensorMap ma, mbm, mc;
+  CUtensorMap ma, mbm, mc, mp;
   memset(&mc, 0, sizeof(mc));
+  memset(&mp, 0, sizeof(mp));
+  if (args.full_units > 0) {
+    // tail slicing (two-SM kernel only): whole tiles to C, the tail's slices
+    // to the workspace rows p_row0 .. M-1, both through bulk tensor stores
+    if (!make_c_map(&mc, args.C, args.M, args.N, args.ldc, out_dtype) ||
+        !make_slices_map(&mp, partials, args.M - args.p_row0, args.N, slices_pld(args.N),
+                         args.k_slices) ||
+        !make_operand_map(&ma, A, args.M, args.K, 128, bf16) ||
+        !make_operand_map(&mbm, B, args.N, args.K, 128, bf16)) {
+      set_error("mb_gemm: cuTensorMapEncodeTiled failed (shape or alignment)");
+      return 1;
+    }
+    args.tma_store = 1;
+    return launch_pair<TIn, TOut, A_MN, B_MN>(ma, mbm, mc, mp, args, s);
+  }
   args.tma_store = (args.k_slices > 1
                         ? make_slices_map(&mc, args.C, args.M, args.N, args.ldc, args.k_slices)
                         : make_c_map(&mc, args.C, args.M, args.N, args.ldc, out_dtype))
@@ -1100,7 +1231,7 @@ int launch_majors(const Operand& A, const Operand& B, GemmArgs args, int out_dty
       set_error("mb_gemm: cuTensorMapEncodeTiled failed (shape or alignment)");
       return 1;
     }
-    return launch_pair<TIn, TOut, A_MN, B_MN>(ma, mbm, mc, args, s);
+    return launch_pair<TIn, TOut, A_MN, B_MN>(ma, mbm, mc, mp, args, s);
   }
   const int bn = args.N >= 192 ? 256 : (args.N > 64 ? 128 : 64);
   if (!make_operand_map(&ma, A, args.M, args.K, kBM, bf16) ||
@@ -1115,10 +1246,14 @@ int launch_majors(const Operand& A, const Operand& B, GemmArgs args, int out_dty
 
 template <typename TIn, typename TOut>
 int launch_typed(const Operand& A, const Operand& B, const GemmArgs& args, int out_dtype,
-                 cudaStream_t s) {
-  if (!A.mn_major && !B.mn_major) return launch_majors<TIn, TOut, false, false>(A, B, args, out_dtype, s);
-  if (!A.mn_major && B.mn_major) return launch_majors<TIn, TOut, false, true>(A, B, args, out_dtype, s);
-  return launch_majors<TIn, TOut, true, true>(A, B, args, out_dtype, s);
+                 void* partials, cudaStream_t s) {
+  if (!A.mn_major && !B.mn_major) {
+    return launch_majors<TIn, TOut, false, false>(A, B, args, out_dtype, partials, s);
+  }
+  if (!A.mn_major && B.mn_major) {
+    return launch_majors<TIn, TOut, false, true>(A, B, args, out_dtype, partials, s);
+  }
+  return launch_majors<TIn, TOut, true, true>(A, B, args, out_dtype, partials, s);
 }
 
 // Check one operand's layout; `mn` is its M (A) or N (B) extent.
@@ -1160,7 +1295,9 @@ extern "C" int64_t mb_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int 
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   int per = 0;
   const int slices = k_slices_for(M, N, K, a_parts, b_parts, out_dtype, true, &per);
-  return slices > 1 ? int64_t(slices) * M * slices_pld(N) * int64_t(sizeof(float)) : 0;
+  if (slices > 1) return int64_t(slices) * M * slices_pld(N) * int64_t(sizeof(float));
+  TailPlan plan;
+  return tail_plan(M, N, K, &plan) ? tail_workspace_bytes(M, N, plan) : 0;
 }
 
 extern "C" int mb_gemm(int in_dtype, const void* A, int a_major, int64_t lda, int64_t a_part_stride,
@@ -1229,8 +1366,19 @@ extern "C" int mb_gemm(int in_dtype, const void* A, int a_major, int64_t lda, in
     // mb_gemm_tn, which takes no workspace): keep the ones accuracy needs
     args.k_slices = k_slices_for(M, N, K, a_parts, b_parts, out_dtype, false, &args.kb_per_slice);
   }
+  args.full_units = 0;
+  args.p_row0 = 0;
+  TailPlan plan;
+  if (args.k_slices == 1 && tail_plan(M, N, K, &plan) && workspace != nullptr &&
+      workspace_bytes >= tail_workspace_bytes(M, N, plan) && aligned_to(workspace, 16) &&
+      aligned_to(C, 16) && (ldc * out_elt) % 16 == 0) {
+    args.full_units = plan.full_units;
+    args.k_slices = plan.slices;
+    args.kb_per_slice = plan.kb_per_slice;
+    args.p_row0 = plan.p_row0;
+  }
   int rc;
-  if (args.k_slices > 1) {
+  if (args.k_slices > 1 && args.full_units == 0) {
     // fp32 partial sums per K slice into the workspace, then their ordered sum
     const int64_t need = int64_t(args.k_slices) * M * pld * int64_t(sizeof(float));
     MB_CHECK_ARG(workspace != nullptr && workspace_bytes >= need && aligned_to(workspace, 16),
@@ -1241,8 +1389,8 @@ extern "C" int mb_gemm(int in_dtype, const void* A, int a_major, int64_t lda, in
     part.ldc = pld;
     part.bias = nullptr;
     part.vec_ok = 1;
-    rc = in_dtype == MB_BF16 ? launch_typed<__nv_bfloat16, float>(a, b, part, MB_F32, s)
-                             : launch_typed<__half, float>(a, b, part, MB_F32, s);
+    rc = in_dtype == MB_BF16 ? launch_typed<__nv_bfloat16, float>(a, b, part, MB_F32, nullptr, s)
+                             : launch_typed<__half, float>(a, b, part, MB_F32, nullptr, s);
     if (rc != 0) return rc;
     const unsigned grid = static_cast<unsigned>(imin64(ceil_div(M * N, 256), 148 * 8));
     const float* ws = static_cast<const float*>(workspace);
@@ -1259,14 +1407,35 @@ extern "C" int mb_gemm(int in_dtype, const void* A, int a_major, int64_t lda, in
     MB_CHECK_LAUNCH("mb_gemm");
     return 0;
   }
+  void* partials = args.full_units > 0 ? workspace : nullptr;
   if (in_dtype == MB_BF16) {
-    rc = out_dtype == MB_F32 ? launch_typed<__nv_bfloat16, float>(a, b, args, out_dtype, s)
-                             : launch_typed<__nv_bfloat16, __nv_bfloat16>(a, b, args, out_dtype, s);
+    rc = out_dtype == MB_F32 ? launch_typed<__nv_bfloat16, float>(a, b, args, out_dtype, partials, s)
+                             : launch_typed<__nv_bfloat16, __nv_bfloat16>(a, b, args, out_dtype, partials, s);
   } else {
-    rc = out_dtype == MB_F32 ? launch_typed<__half, float>(a, b, args, out_dtype, s)
-                             : launch_typed<__half, __half>(a, b, args, out_dtype, s);
+    rc = out_dtype == MB_F32 ? launch_typed<__half, float>(a, b, args, out_dtype, partials, s)
+                             : launch_typed<__half, __half>(a, b, args, out_dtype, partials, s);
   }
   if (rc != 0) return rc;
+  if (args.full_units > 0) {
+    // the tail tiles: their slices' partial sums added in order, + bias
+    const int64_t rows = M - args.p_row0;
+    const unsigned grid = static_cast<unsigned>(imin64(ceil_div(rows * N, 256), 148 * 8));
+    const float* ws = static_cast<const float*>(workspace);
+    const int64_t n_tiles = (N + k2BN - 1) / k2BN;
+    if (out_dtype == MB_F32) {
+      tail_reduce_kernel<float><<<grid, 256, 0, s>>>(ws, args.k_slices, M, N, pld, args.p_row0,
+                                                     args.full_units, n_tiles, bias, bias_dtype,
+                                                     static_cast<float*>(C), ldc);
+    } else if (out_dtype == MB_BF16) {
+      tail_reduce_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+          ws, args.k_slices, M, N, pld, args.p_row0, args.full_units, n_tiles, bias, bias_dtype,
+          static_cast<__nv_bfloat16*>(C), ldc);
+    } else {
+      tail_reduce_kernel<__half><<<grid, 256, 0, s>>>(ws, args.k_slices, M, N, pld, args.p_row0,
+                                                      args.full_units, n_tiles, bias, bias_dtype,
+                                                      static_cast<__half*>(C), ldc);
+    }
+  }
   MB_CHECK_LAUNCH("mb_gemm");
   return 0;
 }

@@ -113,6 +113,35 @@ def test_fp32_weight_gradient_over_long_k_runs_in_slices():
            "dW over K = 51200")
 
 
+def test_long_k_tail_slicing_matches_fp32_products():
+    """K >= 8192 with more two-SM tiles than SM pairs: the whole waves of tiles
+    run unsliced and only the last wave's tiles are split into K slices whose
+    fp32 partial sums a second kernel adds (+ bias). Weight gradients
+    (M-major x, N-major G, 16-bit and fp32 output) and a forward with bias and
+    ragged M and N, against fp32 products of the same operands."""
+
+    lib = nat.lib()
+    assert lib.mb_gemm_workspace_bytes(4096, 4096, 8192, 1, 1, nat.MB_BF16) > 0
+    assert lib.mb_gemm_workspace_bytes(4096, 4096, 4096, 1, 1, nat.MB_BF16) == 0
+    gen = torch.Generator(device=DEV).manual_seed(21)
+    rows, F, N = 8192, 4096, 4096
+    x = _spikes((rows, F), gen, 0.1, torch.bfloat16)
+    g = _rand((rows, N), gen, torch.bfloat16, scale=0.01)
+    ref = x.float().t() @ g.float()
+    _check(projection.weight_grad(x, g, torch.bfloat16).float(), ref.bfloat16().float(), 1e-2,
+           "dW bf16, tail-sliced")
+    _check(projection.weight_grad(x, g, torch.float32), ref, 1e-4, "dW fp32 out, tail-sliced")
+    del x, g, ref
+    M, K, N2 = 4000, 8192, 4000
+    xf = _spikes((M, K), gen, 0.2, torch.bfloat16)
+    w = _rand((K, N2), gen, torch.bfloat16, scale=K ** -0.5)
+    b = _rand((N2,), gen, torch.bfloat16, scale=0.1)
+    cur = projection.project(xf, w, b)
+    _check(cur.float(), (xf.float() @ w.float() + b.float()).bfloat16().float(), 1e-2,
+           "forward with bias, tail-sliced, ragged")
+    assert nat.device_status(clear=True) == 0
+
+
 def test_split_parts_sum_exactly_and_flag_nonzero_parts():
     gen = torch.Generator(device=DEV).manual_seed(11)
     src = torch.randn((37, 45), generator=gen, device=DEV) * 3.0
