@@ -192,14 +192,27 @@ def max_over_ranks(value: float, world: int) -> float:
 # GPU arm
 # ---------------------------------------------------------------------------
 def scan_workload(name: str, rank: int):
+    """Two seeded input sets (x, grad_spikes) of the workload and its forward.
+    Steps alternate between the sets: each set is larger than L2, so no step
+    reads inputs the step before left in L2 (the forward -> backward reuse
+    inside a step is real, a step -> step reuse of the same inputs would not
+    be)."""
+
     import myelin_b200 as mb
 
-    gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
     shape = (T_STEPS, BATCH, NEURONS)
+    sets = []
+    for k in range(2):
+        gen = torch.Generator(device="cuda").manual_seed(1234 + rank + 1000 * k)
+        if name == "alif_bf16":
+            x = (torch.randn(shape, generator=gen, device="cuda") * 0.6 + 0.2).to(torch.bfloat16)
+            gs = torch.randn(shape, generator=gen, device="cuda").to(torch.bfloat16)
+        else:
+            x = torch.randn(shape, generator=gen, device="cuda") * 0.5 + 0.3
+            gs = torch.randn(shape, generator=gen, device="cuda")
+        sets.append((x, gs))
     if name == "alif_bf16":
         dtype = torch.bfloat16
-        x = (torch.randn(shape, generator=gen, device="cuda") * 0.6 + 0.2).to(dtype)
-        gs = torch.randn(shape, generator=gen, device="cuda").to(dtype)
         params = mb.ALIFParams(tau_mem=10.0, tau_adaptation=50.0, threshold=1.0, reset=0.0,
                                beta=1.8)
         zeros = torch.zeros((BATCH, NEURONS), dtype=dtype, device="cuda")
@@ -211,8 +224,6 @@ def scan_workload(name: str, rank: int):
             return spikes
     else:
         dtype = torch.float32
-        x = torch.randn(shape, generator=gen, device="cuda") * 0.5 + 0.3
-        gs = torch.randn(shape, generator=gen, device="cuda")
         params = mb.LIFParams(tau_mem=10.0, threshold=1.0, reset=0.0)
         zeros = torch.zeros((BATCH, NEURONS), dtype=dtype, device="cuda")
 
@@ -220,7 +231,7 @@ def scan_workload(name: str, rank: int):
             state, spikes = mb.surrogate_lif_forward(xin, mb.LIFState(zeros), params,
                                                      surrogate="atan", checkpoint_size="memory")
             return spikes
-    return x, gs, forward
+    return sets, forward
 
 
 def run_gpu(args) -> None:
@@ -236,8 +247,10 @@ def run_gpu(args) -> None:
         return run_izhikevich(args, world, rank, local)
     if name == "lif_packed":
         return run_lif_packed(args, world, rank, local)
-    x, gs, forward = scan_workload(name, rank)
-    x.requires_grad_(True)
+    sets, forward = scan_workload(name, rank)
+    for xs, _ in sets:
+        xs.requires_grad_(True)
+    x, gs = sets[0]
     stream = torch.cuda.current_stream()
     units = T_STEPS * BATCH * NEURONS  # neuron-steps per rank per step
 
@@ -249,9 +262,10 @@ def run_gpu(args) -> None:
     # warm up like the timed loop below: the previous step's spikes (and the
     # checkpoints they hold) stay alive while the next forward allocates, so
     # the allocator has cached every block before timing starts
-    for _ in range(args.warmup):
-        spikes = forward(x)
-        torch.autograd.grad(spikes, x, gs)
+    for k in range(args.warmup):
+        xs, g = sets[k % 2]
+        spikes = forward(xs)
+        torch.autograd.grad(spikes, xs, g)
     torch.cuda.synchronize()
 
     # eager: the public API called step by step, per-kernel events on the
@@ -266,10 +280,11 @@ def run_gpu(args) -> None:
     t_host = time.perf_counter()
     for k in range(args.steps):
         e0, e1, e2 = ev[k]
+        xs, g = sets[k % 2]
         e0.record(stream)
-        spikes = forward(x)
+        spikes = forward(xs)
         e1.record(stream)
-        torch.autograd.grad(spikes, x, gs)
+        torch.autograd.grad(spikes, xs, g)
         e2.record(stream)
     stop.record(stream)
     # host time to issue the steps: at or above the device time per step,
@@ -286,38 +301,43 @@ def run_gpu(args) -> None:
     # back to back without waiting on the host between launches
     # (a fresh leaf: autograd binds a leaf's gradient sink to the stream it
     # was first used on, and the eager loop above used the legacy stream)
-    xg = x.detach().requires_grad_(True)
+    # One graph per input set; the timed loop alternates them.
+    leaves = [(xs.detach().requires_grad_(True), g) for xs, g in sets]
     cap = torch.cuda.Stream()
     cap.wait_stream(stream)
     with torch.cuda.stream(cap):
         for _ in range(2):
-            torch.autograd.grad(forward(xg), xg, gs)
+            for xg, g in leaves:
+                torch.autograd.grad(forward(xg), xg, g)
     stream.wait_stream(cap)
     torch.cuda.synchronize()
-    step_graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(step_graph, stream=cap):
-        torch.autograd.grad(forward(xg), xg, gs)
-    for _ in range(args.warmup):
-        step_graph.replay()
+    step_graphs = []
+    for xg, g in leaves:
+        graph_k = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph_k, stream=cap):
+            torch.autograd.grad(forward(xg), xg, g)
+        step_graphs.append(graph_k)
+    for k in range(args.warmup):
+        step_graphs[k % 2].replay()
     torch.cuda.synchronize()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         barrier(world)
         torch.cuda.synchronize()
         start.record(stream)
-        for _ in range(args.steps):
-            step_graph.replay()
+        for k in range(args.steps):
+            step_graphs[k % 2].replay()
         stop.record(stream)
         torch.cuda.synchronize()
         barrier(world)
     total_ms = max_over_ranks(start.elapsed_time(stop), world)
     ms_per_step = total_ms / args.steps
     value = units * world / (ms_per_step / 1e3)
-    del step_graph
+    del step_graphs, leaves
     status = nat.device_status(clear=True)
     # per-kernel device times for the roofline: the step's two kernels, each
     # replayed from its own graph with events between them
-    graph = graph_replay_diagnostic(name, x, gs, stream, args.steps, world)
+    graph = graph_replay_diagnostic(name, sets, stream, args.steps, world)
     timing = graph.get("in_graph", graph)
     fwd_ms, bwd_ms = timing["fwd_launch_ms"], timing["bwd_launch_ms"]
     launch_times = ("CUDA events recorded as nodes of one graph holding the step's two kernels"
@@ -403,7 +423,9 @@ def run_gpu(args) -> None:
             "T": T_STEPS, "B_per_gpu": BATCH, "N": NEURONS, "global_batch": BATCH * world,
             "parallelism": f"dp{world} (batch-sharded, no data-path collective)",
             "l2": "inputs larger than L2 (x and grad_spikes are T*B*N*elt = "
-                  f"{units * elt / 1e6:.0f} MB each), no flush",
+                  f"{units * elt / 1e6:.0f} MB each), no flush; two input sets, "
+                  "steps alternate between them, so no step reads inputs the previous "
+                  "step left in L2",
             "cuda_graph": "the public-API step (forward + autograd backward) captured once "
                           "and replayed; the eager figure is under 'eager'",
         },
@@ -439,13 +461,13 @@ def run_gpu(args) -> None:
         print(json.dumps(result), flush=True)
 
 
-def graph_replay_diagnostic(name: str, x, gs, stream, steps: int, world: int) -> dict:
+def graph_replay_diagnostic(name: str, sets, stream, steps: int, world: int) -> dict:
     """The step's two kernels (the scan forward and backward the public API
     launches, called here through the same ops with the workload's
-    parameters) captured as two CUDA graphs and replayed, with events between
-    the replays: the kernels' device time without the host's per-launch work
-    (Python, autograd) in between. A gap between this and the eager step says
-    how much of the eager time is the host's."""
+    parameters) captured in CUDA graphs and replayed, alternating between the
+    two input sets like the timed step: the kernels' device time without the
+    host's per-launch work (Python, autograd) in between. A gap between this
+    and the eager step says how much of the eager time is the host's."""
 
     from myelin_b200 import _native as nat
     from myelin_b200 import compile_ops as cops
@@ -454,42 +476,49 @@ def graph_replay_diagnostic(name: str, x, gs, stream, steps: int, world: int) ->
     kw = dict(neuron=nat.MB_ALIF if alif else nat.MB_LIF, decay=0.9, threshold=1.0, reset=0.0,
               adapt_decay=(1.0 - 1.0 / 50.0) if alif else 0.0, beta=1.8 if alif else 0.0,
               reset_mode=nat.MB_RESET_SUBTRACT if alif else nat.MB_RESET_HARD)
-    B, N = x.shape[1], x.shape[2]
-    zeros = torch.zeros((B, N), dtype=x.dtype, device=x.device)
-    xd = x.detach()
+    x0 = sets[0][0]
+    B, N = x0.shape[1], x0.shape[2]
+    zeros = torch.zeros((B, N), dtype=x0.dtype, device=x0.device)
+    inputs = [(xs.detach(), g) for xs, g in sets]
 
-    def fwd():
-        out = cops.scan_forward(xd, zeros, zeros if alif else None, kw["neuron"], kw["decay"],
-                                kw["threshold"], kw["reset"], kw["adapt_decay"], kw["beta"],
-                                kw["reset_mode"], dense=True, checkpoints=True)
+    def fwd(k):
+        out = cops.scan_forward(inputs[k][0], zeros, zeros if alif else None, kw["neuron"],
+                                kw["decay"], kw["threshold"], kw["reset"], kw["adapt_decay"],
+                                kw["beta"], kw["reset_mode"], dense=True, checkpoints=True)
         return out[5], out[6]
 
-    def bwd(ckpt_v, ckpt_a):
-        return cops.scan_backward(xd, ckpt_v, ckpt_a, grad_spikes=gs, grad_vT=None,
-                                  grad_aT=None, surrogate=2, slope=10.0, need_v0=False,
-                                  need_a0=False, **kw)[0]
+    def bwd(k, ckpt_v, ckpt_a):
+        return cops.scan_backward(inputs[k][0], ckpt_v, ckpt_a, grad_spikes=inputs[k][1],
+                                  grad_vT=None, grad_aT=None, surrogate=2, slope=10.0,
+                                  need_v0=False, need_a0=False, **kw)[0]
 
     cap = torch.cuda.Stream()
     cap.wait_stream(stream)
     with torch.cuda.stream(cap):
         for _ in range(2):
-            bwd(*fwd())
+            for k in range(2):
+                bwd(k, *fwd(k))
     stream.wait_stream(cap)
     torch.cuda.synchronize()
-    g_fwd, g_bwd = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g_fwd, stream=cap):
-        ckpts = fwd()
-    with torch.cuda.graph(g_bwd, pool=g_fwd.pool(), stream=cap):
-        bwd(*ckpts)
+    graphs = []
+    for k in range(2):
+        g_fwd, g_bwd = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_fwd, stream=cap):
+            ckpts = fwd(k)
+        with torch.cuda.graph(g_bwd, pool=g_fwd.pool(), stream=cap):
+            bwd(k, *ckpts)
+        graphs.append((g_fwd, g_bwd))
     for _ in range(3):
-        g_fwd.replay()
-        g_bwd.replay()
+        for g_fwd, g_bwd in graphs:
+            g_fwd.replay()
+            g_bwd.replay()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
            torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
-    for e0, e1, e2 in ev:
+    for i, (e0, e1, e2) in enumerate(ev):
+        g_fwd, g_bwd = graphs[i % 2]
         e0.record(stream)
         g_fwd.replay()
         e1.record(stream)
@@ -499,33 +528,35 @@ def graph_replay_diagnostic(name: str, x, gs, stream, steps: int, world: int) ->
     total = max_over_ranks(ev[0][0].elapsed_time(ev[-1][2]), world) / steps
     fwd_ms = statistics.mean(a.elapsed_time(b) for a, b, _ in ev)
     bwd_ms = statistics.mean(b.elapsed_time(c) for _, b, c in ev)
-    del g_fwd, g_bwd
+    del graphs
 
-    # Both kernels in ONE graph with event-record nodes before, between and
-    # after them: each kernel's device time as it runs inside the step, with
-    # no graph launch (and its host round trip) between the two. Every rank
-    # takes the same collective steps whether or not this works here.
+    # Both sets' kernels in ONE graph with event-record nodes before, between
+    # and after them: each kernel's device time as it runs inside the
+    # alternating steps, with no graph launch (and its host round trip)
+    # between kernels. Every rank takes the same collective steps whether or
+    # not this works here.
     in_fwd = in_bwd = in_over = -1.0
     try:
-        evs = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(4)]
+        evs = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(6)]
         g_one = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g_one, stream=cap):
-            evs[0].record(cap)
-            ckpts = fwd()
-            evs[1].record(cap)
-            bwd(*ckpts)
-            evs[2].record(cap)
-            evs[3].record(cap)  # an empty interval: what one event node itself adds
+            for k in range(2):
+                evs[2 * k].record(cap)
+                ckpts = fwd(k)
+                evs[2 * k + 1].record(cap)
+                bwd(k, *ckpts)
+            evs[4].record(cap)
+            evs[5].record(cap)  # an empty interval: what one event node itself adds
         for _ in range(3):
             g_one.replay()
         torch.cuda.synchronize()
         f_list, b_list, o_list = [], [], []
-        for _ in range(steps):
+        for _ in range(max(1, steps // 2)):
             g_one.replay()
             torch.cuda.synchronize()
-            f_list.append(evs[0].elapsed_time(evs[1]))
-            b_list.append(evs[1].elapsed_time(evs[2]))
-            o_list.append(evs[2].elapsed_time(evs[3]))
+            f_list += [evs[0].elapsed_time(evs[1]), evs[2].elapsed_time(evs[3])]
+            b_list += [evs[1].elapsed_time(evs[2]), evs[3].elapsed_time(evs[4])]
+            o_list.append(evs[4].elapsed_time(evs[5]))
         del g_one
         in_fwd, in_bwd = statistics.mean(f_list), statistics.mean(b_list)
         in_over = statistics.mean(o_list)

@@ -341,7 +341,11 @@ __global__ void __launch_bounds__(kThreads, MINB) scan_bwd_fast_kernel(
   auto stage_g = [&](int s) { return stage_x(s) + kChunk * kTileN; };
   auto stage_c = [&](int s) { return reinterpret_cast<float*>(stage_g(s) + kChunk * kTileN); };
 
-  const int64_t e0 = int64_t(blockIdx.x) * kTileN;
+  // Tiles in reverse block order: the forward runs tiles in block order, so
+  // the backward's first CTAs take the tiles the forward finished last, whose
+  // last chunks (inputs and checkpoints, read first here) are still in L2
+  // (config 3, ALIF bf16: forward + backward 0.2415 -> 0.2303 ms).
+  const int64_t e0 = int64_t(gridDim.x - 1 - blockIdx.x) * kTileN;
   const int tile_n = static_cast<int>(imin64(kTileN, a.BN - e0));
   const int64_t K = (a.T + kChunk - 1) / kChunk;
   constexpr bool kSpikes = MODE == kBwdSpikes || MODE == kBwdAny;
