@@ -729,6 +729,12 @@ template <int DT>
 static void launch_pack_count(const void* spikes, int32_t* words, int64_t rows, int64_t n,
                               int64_t* counts64, int32_t* counts32, void* workspace,
                               cudaStream_t s) {
+  if (pack_count_fused_ok(DT, spikes, n) && pack_count_rows_ok(n, words, nullptr, 0)) {
+    // whole rows per block, words out as bulk copies (config 4 on one GPU:
+    // 0.230 -> 0.213 ms against the per-thread word stores below)
+    launch_pack_count_rows(spikes, words, nullptr, 0, rows, n, counts64, counts32, s);
+    return;
+  }
   if (pack_count_fused_ok(DT, spikes, n)) {
     launch_pack_count_u8(spikes, words, PeerSlots{}, 0, rows, n, counts64, counts32, s);
     return;

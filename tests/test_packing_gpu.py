@@ -137,11 +137,13 @@ def test_pack_with_counts_matches_oracle(oracle, dtype, shape, count_dtype):
     assert np.array_equal(counts.cpu().numpy().astype(np.int64), expected)
 
 
-def test_pack_with_counts_long_columns_flush():
-    """More rows than the 8-bit counters hold between flushes (255), all ones:
-    every column count equals the row count."""
+@pytest.mark.parametrize("rows,n", [(70000, 64), (160000, 4096)])
+def test_pack_with_counts_long_columns_flush(rows, n):
+    """More rows per block than the 8-bit counters hold between flushes (255),
+    all ones, on the per-word-column kernel (n = 64) and the whole-row kernel
+    (n = 4096: blocks of 272 rows): every column count equals the row
+    count."""
 
-    rows, n = 70000, 64
     spikes = torch.ones((rows, n), dtype=torch.bool, device=DEV)
     packed, counts = mb.pack_spikes_with_counts(spikes)
     assert bool(torch.all(counts == rows))
