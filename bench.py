@@ -1050,7 +1050,7 @@ def run_pack_count(args, world, rank, local) -> None:
         "roofline": {"bound": "hbm", "achieved": round(algo / (ms / 1e3) / 1e9, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(algo / (ms / 1e3) / 1e9 / peak, 4),
                      "peak_kind": peak_kind,
-                     "traffic": profile_traffic("pack_count_u8_config4") if world == 1 else None,
+                     "traffic": profile_traffic("pack_count_rows_config4") if world == 1 else None,
                      "note": "fused pack+count bytes over the whole step (collectives included)"},
         "spike_count_check": total,
         # one packing kernel per step (the totals are zeroed by a memset)
