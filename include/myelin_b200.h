@@ -235,7 +235,11 @@ enum mb_major { MB_KMAJOR = 0, MB_MNMAJOR = 1 };
  * accumulation of one MMA is not correctly rounded, so its error grows with
  * the MMAs summed into one accumulator), and to occupy the SMs when the
  * output has few tiles and K is long (the weight gradient of a small or
- * narrow layer, K = T*B).
+ * narrow layer, K = T*B). With K >= 8192 and more 256 x 256 tiles than SM
+ * pairs, only the tiles of the last, partial wave are sliced (their fp32
+ * partials cover just their rows of C); the others are written directly.
+ * Without the workspace these optional slices are skipped (same result up
+ * to summation order).
  * Used for the stream synapse's currents x[T*B, F] * W[F, N] (B = W N-major,
  * no transposed copy), input gradient G * W^T (both K-major) and weight
  * gradient x^T G (A = x M-major, B = G N-major; no transposes).
