@@ -81,6 +81,71 @@ __global__ void split_bf16_kernel(const TS* __restrict__ src, int64_t rows, int6
   }
 }
 
+// Vector form of split_bf16_kernel for an fp32 source with unit column
+// stride and 16-byte aligned rows, 4-aligned widths and a 4-aligned
+// destination pitch: thread = 4 consecutive columns (one 16-byte load, one
+// 8-byte store per part), rows on blockIdx.y, four rows' loads in flight.
+template <int PARTS>
+__device__ __forceinline__ uint32_t split_store4(const float4 v, __nv_bfloat16* out,
+                                                 int64_t part_stride) {
+  float rest[4] = {v.x, v.y, v.z, v.w};
+  uint32_t nz = 0;
+  bool finite[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) finite[e] = isfinite(rest[e]);
+#pragma unroll
+  for (int p = 0; p < PARTS; ++p) {
+    __nv_bfloat16 h[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      // inf / nan stay in the leading part, the rest are zero
+      h[e] = (p == 0 || finite[e]) ? __float2bfloat16_rn(rest[e]) : __float2bfloat16_rn(0.0f);
+      const float hf = __bfloat162float(h[e]);
+      nz |= (hf != 0.0f || (p == 0 && !finite[e])) ? (1u << p) : 0u;
+      rest[e] = finite[e] ? __fsub_rn(rest[e], hf) : 0.0f;  // exact: a bf16 rounding error
+    }
+    uint2 w;
+    w.x = uint32_t(__bfloat16_as_ushort(h[0])) | (uint32_t(__bfloat16_as_ushort(h[1])) << 16);
+    w.y = uint32_t(__bfloat16_as_ushort(h[2])) | (uint32_t(__bfloat16_as_ushort(h[3])) << 16);
+    *reinterpret_cast<uint2*>(out + p * part_stride) = w;
+  }
+  return nz;
+}
+
+template <int PARTS>
+__global__ void split_bf16_vec4_kernel(const float* __restrict__ src, int64_t rows, int64_t cols,
+                                       int64_t rs, __nv_bfloat16* __restrict__ dst,
+                                       int64_t dst_rows, int64_t dst_cols, int64_t ld,
+                                       int64_t part_stride, int32_t* nonzero) {
+  uint32_t nz = 0;
+  const int64_t c = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+  if (c < dst_cols) {
+    const bool in_cols = c < cols;  // cols % 4 == 0: a group is wholly in or out
+    const int64_t step = gridDim.y;
+    auto load = [&](int64_t r) {
+      return (in_cols && r < rows) ? __ldg(reinterpret_cast<const float4*>(src + r * rs + c))
+                                   : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    };
+    int64_t r = blockIdx.y;
+    for (; r + 3 * step < dst_rows; r += 4 * step) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = load(r + u * step);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) nz |= split_store4<PARTS>(v[u], dst + (r + u * step) * ld + c, part_stride);
+    }
+    for (; r < dst_rows; r += step) nz |= split_store4<PARTS>(load(r), dst + r * ld + c, part_stride);
+  }
+  if (nonzero != nullptr) {
+    nz = __reduce_or_sync(0xffffffffu, nz);
+    if ((threadIdx.x & 31) == 0) {
+      for (int p = 0; p < PARTS; ++p) {
+        if (nz & (1u << p)) atomicOr(nonzero + p, 1);
+      }
+    }
+  }
+}
+
 // Column sums, stage 1: block (cb, slice) sums rows [slice * rows_per_slice,
 // ...) of 256 consecutive columns, one column per thread, in row order.
 template <typename TS>
@@ -152,6 +217,28 @@ extern "C" int mb_split_bf16(int src_dtype, const void* src, int64_t rows, int64
   }
   MB_CHECK_ARG((src != nullptr || rows * cols == 0) && dst != nullptr,
                "mb_split_bf16: null pointer");
+  if (src_dtype == MB_F32 && src_col_stride == 1 && aligned_to(src, 16) && src_row_stride % 4 == 0 &&
+      cols % 4 == 0 && dst_cols % 4 == 0 && dst_ld % 4 == 0 && dst_part_stride % 4 == 0 &&
+      aligned_to(dst, 8)) {
+    // 4 columns per thread, about 8 blocks of 256 threads per SM
+    const int64_t col_blocks = ceil_div(dst_cols / 4, 256);
+    const dim3 grid(static_cast<unsigned>(col_blocks),
+                    static_cast<unsigned>(imin64(dst_rows, imin64(65535, ceil_div(148 * 8, col_blocks)))));
+    auto* out = static_cast<__nv_bfloat16*>(dst);
+    const auto* in = static_cast<const float*>(src);
+    if (parts == 1) {
+      split_bf16_vec4_kernel<1><<<grid, 256, 0, s>>>(in, rows, cols, src_row_stride, out, dst_rows,
+                                                     dst_cols, dst_ld, dst_part_stride, nonzero);
+    } else if (parts == 2) {
+      split_bf16_vec4_kernel<2><<<grid, 256, 0, s>>>(in, rows, cols, src_row_stride, out, dst_rows,
+                                                     dst_cols, dst_ld, dst_part_stride, nonzero);
+    } else {
+      split_bf16_vec4_kernel<3><<<grid, 256, 0, s>>>(in, rows, cols, src_row_stride, out, dst_rows,
+                                                     dst_cols, dst_ld, dst_part_stride, nonzero);
+    }
+    MB_CHECK_LAUNCH("mb_split_bf16");
+    return 0;
+  }
   // enough blocks for about 16 per SM: columns in blocks of 256, rows on y
   const int64_t col_blocks = imin64(ceil_div(dst_cols, 256), 148 * 16);
   const dim3 grid(static_cast<unsigned>(col_blocks),

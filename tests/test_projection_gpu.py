@@ -142,6 +142,44 @@ def test_long_k_tail_slicing_matches_fp32_products():
     assert nat.device_status(clear=True) == 0
 
 
+@pytest.mark.parametrize("rows,cols,ld", [(37, 45, 48), (64, 96, 96), (6400, 784, 784)])
+def test_split_parts_match_successive_bf16_roundings(rows, cols, ld):
+    """Each part is the bf16 rounding of what the parts before it left, for
+    the scalar kernel (45 columns) and the 4-column vector kernel (96, 784):
+    bit for bit against the same roundings in torch, zero padding outside
+    the source, inf/nan kept whole in the leading part."""
+
+    gen = torch.Generator(device=DEV).manual_seed(rows + cols)
+    src = torch.randn((rows, cols), generator=gen, device=DEV) * 3.0
+    src[0, 0] = float("inf")
+    src[1, 2] = float("nan")
+    src[2, 3] = 0.0
+    src[3, 1] = 1e-30
+    dst_rows = rows + 3
+    parts = torch.full((3, dst_rows, ld), 7.0, dtype=torch.bfloat16, device=DEV)
+    nz = torch.empty(3, dtype=torch.int32, device=DEV)
+    nat.split_bf16(src, rows, cols, cols, 1, 3, parts, dst_rows, ld, ld, dst_rows * ld, nz)
+    torch.cuda.synchronize()
+    finite = torch.isfinite(src)
+    rest = torch.where(finite, src, torch.zeros_like(src))
+    want = []
+    for p in range(3):
+        h = rest.bfloat16()
+        want.append(h)
+        rest = rest - h.float()
+    for p in range(3):
+        got = parts[p, :rows, :cols]
+        assert torch.equal(got.view(torch.int16)[finite], want[p].view(torch.int16)[finite]), p
+        if p == 0:
+            lead = got.float()
+            assert torch.isinf(lead[0, 0]) and lead[0, 0] > 0 and torch.isnan(lead[1, 2])
+        else:
+            assert torch.count_nonzero(got.float()[~finite]) == 0
+        assert torch.count_nonzero(parts[p, rows:, :]) == 0
+        assert torch.count_nonzero(parts[p, :, cols:]) == 0
+    assert nz.tolist() == [1, 1, 1]
+
+
 def test_split_parts_sum_exactly_and_flag_nonzero_parts():
     gen = torch.Generator(device=DEV).manual_seed(11)
     src = torch.randn((37, 45), generator=gen, device=DEV) * 3.0
