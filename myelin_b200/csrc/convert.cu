@@ -170,6 +170,55 @@ __global__ void column_sums_partial_kernel(const TS* __restrict__ src, int64_t r
   partial[int64_t(blockIdx.y) * cols + c] = acc;
 }
 
+// Vector form of stage 1 (16-byte rows, widths a multiple of the vector):
+// thread = 16 bytes of consecutive columns (4 fp32 or 8 16-bit values),
+// eight rows' loads in flight, each column summed in row order as above.
+template <typename TS>
+__device__ __forceinline__ void add_row16(float* acc, const uint4 v) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  if constexpr (std::is_same<TS, float>::value) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[e] += __uint_as_float(w[e]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if constexpr (std::is_same<TS, __nv_bfloat16>::value) {
+        acc[2 * e] += __uint_as_float(w[e] << 16);
+        acc[2 * e + 1] += __uint_as_float(w[e] & 0xffff0000u);
+      } else {
+        acc[2 * e] += __half2float(__ushort_as_half(static_cast<uint16_t>(w[e] & 0xffffu)));
+        acc[2 * e + 1] += __half2float(__ushort_as_half(static_cast<uint16_t>(w[e] >> 16)));
+      }
+    }
+  }
+}
+
+template <typename TS>
+__global__ void column_sums_partial_vec_kernel(const TS* __restrict__ src, int64_t rows,
+                                               int64_t cols, int64_t ld, int64_t rows_per_slice,
+                                               float* __restrict__ partial) {
+  constexpr int kVec = 16 / int(sizeof(TS));
+  const int64_t c = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * kVec;
+  const int64_t r0 = int64_t(blockIdx.y) * rows_per_slice;
+  const int64_t r1 = imin64(rows, r0 + rows_per_slice);
+  if (c >= cols) return;
+  float acc[kVec];
+#pragma unroll
+  for (int e = 0; e < kVec; ++e) acc[e] = 0.0f;
+  int64_t r = r0;
+  for (; r + 8 <= r1; r += 8) {
+    uint4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = __ldg(reinterpret_cast<const uint4*>(src + (r + j) * ld + c));
+#pragma unroll
+    for (int j = 0; j < 8; ++j) add_row16<TS>(acc, v[j]);
+  }
+  for (; r < r1; ++r) add_row16<TS>(acc, __ldg(reinterpret_cast<const uint4*>(src + r * ld + c)));
+  float* out = partial + int64_t(blockIdx.y) * cols + c;
+#pragma unroll
+  for (int e = 0; e < kVec; ++e) out[e] = acc[e];
+}
+
 // Stage 2: sum the slices of each column in slice order, write out.
 template <typename TO>
 __global__ void column_sums_final_kernel(const float* __restrict__ partial, int64_t slices,
@@ -177,13 +226,23 @@ __global__ void column_sums_final_kernel(const float* __restrict__ partial, int6
   const int64_t c = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (c >= cols) return;
   float acc = 0.0f;
-  for (int64_t s = 0; s < slices; ++s) acc += partial[s * cols + c];
+  int64_t s = 0;
+  for (; s + 32 <= slices; s += 32) {  // 32 loads in flight, summed in slice order
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = partial[(s + j) * cols + c];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) acc += v[j];
+  }
+  for (; s < slices; ++s) acc += partial[s * cols + c];
   out[c] = Elem<TO>::from_f(acc);
 }
 
 int64_t column_slices(int64_t rows, int64_t cols) {
-  const int64_t col_blocks = ceil_div(cols, 256);
-  int64_t slices = ceil_div(148 * 8, col_blocks);  // about 8 blocks per SM
+  // about 8 blocks per SM when a thread reads 4 columns (fp32 vector loads;
+  // 16-bit ones read 8, so half as many blocks with twice the bytes each)
+  const int64_t col_blocks = ceil_div(cols, 256 * 4);
+  int64_t slices = ceil_div(148 * 8, col_blocks);
   const int64_t max_by_rows = ceil_div(rows, 128);  // at least 128 rows per slice
   if (slices > max_by_rows) slices = max_by_rows;
   return slices < 1 ? 1 : slices;
@@ -296,7 +355,26 @@ extern "C" int mb_column_sums(int dtype, const void* src, int64_t rows, int64_t 
   float* partial = static_cast<float*>(workspace);
   const dim3 grid1(static_cast<unsigned>(ceil_div(cols, 256)), static_cast<unsigned>(slices));
   const int64_t per = ceil_div(rows, slices);
-  switch (dtype) {
+  const int64_t vec = dtype == MB_F32 ? 4 : 8;  // elements per 16-byte load
+  // wide rows (config 5: 51200 x 4096 bf16 103 -> 79 us); narrower ones keep a
+  // thread per column, whose many warps hide the latency better
+  if (cols >= 2048 && cols % vec == 0 && ld % vec == 0 && aligned_to(src, 16) &&
+      aligned_to(workspace, 16)) {
+    // narrower blocks when the slices alone leave the SMs short of blocks
+    unsigned bs = 256;
+    while (bs > 32 && ceil_div(cols / vec, bs) * slices < 148 * 4) bs /= 2;
+    const dim3 gridv(static_cast<unsigned>(ceil_div(cols / vec, bs)), static_cast<unsigned>(slices));
+    if (dtype == MB_F32) {
+      column_sums_partial_vec_kernel<float><<<gridv, bs, 0, s>>>(
+          static_cast<const float*>(src), rows, cols, ld, per, partial);
+    } else if (dtype == MB_BF16) {
+      column_sums_partial_vec_kernel<__nv_bfloat16><<<gridv, bs, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(src), rows, cols, ld, per, partial);
+    } else {
+      column_sums_partial_vec_kernel<__half><<<gridv, bs, 0, s>>>(
+          static_cast<const __half*>(src), rows, cols, ld, per, partial);
+    }
+  } else switch (dtype) {
     case MB_F32:
       column_sums_partial_kernel<float><<<grid1, 256, 0, s>>>(static_cast<const float*>(src),
                                                               rows, cols, ld, per, partial);
