@@ -177,6 +177,23 @@ int mb_scan_backward(int neuron, int dtype, const void* x, const float* ckpt_v,
                      int reset_mode, int surrogate, float slope, void* stream);
 
 /*
+ * mb_scan_backward plus grad_sum (fp32 [B*N], 8-byte aligned, nullable): for
+ * every neuron the sum over t of grad_x as stored (in the I/O type), from
+ * the last step to the first, in fp32. The LIF backward kernel forms it as it
+ * writes grad_x; other kinds and layouts sum grad_x over t afterwards. The
+ * bias gradient of a stream-synapse layer is the column sum of grad_sum
+ * viewed as [B, N] (mb_column_sums), instead of a pass over [T*B, N].
+ * Replaces: the bias-gradient reduction of src/myelin/triton/lif.py:1232-1258
+ *   (float atomics there; fixed order here).
+ */
+int mb_scan_backward_sum(int neuron, int dtype, const void* x, const float* ckpt_v,
+                         const float* ckpt_a, const void* grad_spikes, const void* grad_rates,
+                         const void* grad_vT, const void* grad_aT, void* grad_x, void* grad_v0,
+                         void* grad_a0, float* grad_sum, int64_t T, int64_t B, int64_t N,
+                         float decay, float threshold, float reset, float adapt_decay,
+                         float beta, int reset_mode, int surrogate, float slope, void* stream);
+
+/*
  * Fused-time Izhikevich forward over x[T,B,N] (dtype MB_F32/BF16/F16):
  *   dv  = ((c2 * v) * v + c1 * v) + bias - u + x_t     (one rounding per op)
  *   p_v = v + dt * dv;   p_u = u + dt * (a * (b * v - u))

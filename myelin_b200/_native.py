@@ -63,6 +63,11 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_int, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
          _i64, _i64, _i64, _f, _f, _f, _f, _f, _int, _int, _f, _vp],
     ),
+    "mb_scan_backward_sum": (
+        _int,
+        [_int, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+         _i64, _i64, _i64, _f, _f, _f, _f, _f, _int, _int, _f, _vp],
+    ),
     "mb_gemm_tn": (
         _int, [_int, _vp, _i64, _vp, _i64, _vp, _int, _int, _vp, _i64, _i64, _i64, _i64, _vp]
     ),
@@ -234,16 +239,29 @@ def scan_backward(
     reset_mode: int,
     surrogate: int,
     slope: float,
+    grad_sum: torch.Tensor | None = None,
 ) -> None:
+    """Reverse scan; ``grad_sum`` (fp32 [B*N], optional) receives the sum over
+    t of grad_x, last step first (``mb_scan_backward_sum``)."""
+
     T, B, N = x.shape
     with torch.cuda.device(x.device):
-        status = lib().mb_scan_backward(
-            neuron, dtype_code(x.dtype), ptr(x), ptr(ckpt_v), ptr(ckpt_a),
-            ptr(grad_spikes), ptr(grad_rates), ptr(grad_vT), ptr(grad_aT),
-            ptr(grad_x), ptr(grad_v0), ptr(grad_a0),
-            T, B, N, decay, threshold, reset, adapt_decay, beta, reset_mode,
-            surrogate, slope, stream_handle(x.device),
-        )
+        if grad_sum is None:
+            status = lib().mb_scan_backward(
+                neuron, dtype_code(x.dtype), ptr(x), ptr(ckpt_v), ptr(ckpt_a),
+                ptr(grad_spikes), ptr(grad_rates), ptr(grad_vT), ptr(grad_aT),
+                ptr(grad_x), ptr(grad_v0), ptr(grad_a0),
+                T, B, N, decay, threshold, reset, adapt_decay, beta, reset_mode,
+                surrogate, slope, stream_handle(x.device),
+            )
+        else:
+            status = lib().mb_scan_backward_sum(
+                neuron, dtype_code(x.dtype), ptr(x), ptr(ckpt_v), ptr(ckpt_a),
+                ptr(grad_spikes), ptr(grad_rates), ptr(grad_vT), ptr(grad_aT),
+                ptr(grad_x), ptr(grad_v0), ptr(grad_a0), ptr(grad_sum),
+                T, B, N, decay, threshold, reset, adapt_decay, beta, reset_mode,
+                surrogate, slope, stream_handle(x.device),
+            )
     check(status, "mb_scan_backward")
 
 

@@ -172,18 +172,21 @@ class LinearScanFunction(torch.autograd.Function):
         need_x, need_w, need_b = ctx.needs_input_grad[:3]
         T, B, F = inputs.shape
         N = weight.shape[1]
-        grad_currents, _, _ = cops.scan_backward(
+        need_bias = need_b and ctx.has_bias
+        # with a bias, the reverse scan also sums dL/dcurrents over t per neuron
+        # as it stores it; db is then the sum of those over the batch rows
+        outs = cops.scan_backward(
             currents, ckpt_v, None, grad_spikes=None if rate_output else g_out,
             grad_rates=g_out if rate_output else None, grad_vT=g_vT, neuron=nat.MB_LIF,
             decay=decay, threshold=threshold, reset=reset, adapt_decay=0.0, beta=0.0,
             reset_mode=nat.MB_RESET_HARD, surrogate=surrogate, slope=slope, need_v0=False,
-            need_a0=False,
+            need_a0=False, need_sum=need_bias,
         )
-        g2 = grad_currents.view(T * B, N)
+        g2 = outs[0].view(T * B, N)
         grad_inputs = _input_grad(g2, weight).view(T, B, F) if need_x else None
-        grad_weight, grad_bias = _weight_bias_grads(
-            inputs.reshape(T * B, F), g2, weight, ctx.bias_like, need_w,
-            need_b and ctx.has_bias)
+        grad_weight, _ = _weight_bias_grads(inputs.reshape(T * B, F), g2, weight, None, need_w,
+                                            False)
+        grad_bias = cops.bias_grad(outs[3].view(B, N), ctx.bias_like) if need_bias else None
         return (grad_inputs, grad_weight, grad_bias, *tail)
 
 
@@ -255,11 +258,15 @@ class TwoLayerPackedHiddenRateFunction(torch.autograd.Function):
                                       0.0, nat.MB_RESET_HARD, packed=True)[3]
         hidden = cops.unpack(words, T * B, H, inputs.dtype)  # [T*B, H]
         cur2 = _project(hidden, w2, b2).view(T, B, O)
-        g_cur2, _, _ = cops.scan_backward(cur2, ckpt2, None, grad_rates=g_rates, **scan_kw)
+        # the bias gradients as in LinearScanFunction: sums over t formed by the
+        # reverse scan, then over the batch rows (the same bits as the dense path)
+        sum2 = need_b2 and b2 is not None
+        outs2 = cops.scan_backward(cur2, ckpt2, None, grad_rates=g_rates, need_sum=sum2,
+                                   **scan_kw)
         del cur2
-        g2 = g_cur2.view(T * B, O)
-        grad_w2, grad_b2 = _weight_bias_grads(hidden, g2, w2, b2, need_w2,
-                                              need_b2 and b2 is not None)
+        g2 = outs2[0].view(T * B, O)
+        grad_w2, _ = _weight_bias_grads(hidden, g2, w2, None, need_w2, False)
+        grad_b2 = cops.bias_grad(outs2[3].view(B, O), b2) if sum2 else None
         del hidden
 
         grad_x = grad_w1 = grad_b1 = None
@@ -267,10 +274,12 @@ class TwoLayerPackedHiddenRateFunction(torch.autograd.Function):
             g_hidden = _input_grad(g2, w2).view(T, B, H)
             if cur1 is None:
                 cur1 = _project(x2, w1, b1).view(T, B, H)
-            g_cur1, _, _ = cops.scan_backward(cur1, ckpt1, None, grad_spikes=g_hidden, **scan_kw)
+            sum1 = need_b1 and b1 is not None
+            outs1 = cops.scan_backward(cur1, ckpt1, None, grad_spikes=g_hidden, need_sum=sum1,
+                                       **scan_kw)
             del cur1, g_hidden
-            g1 = g_cur1.view(T * B, H)
+            g1 = outs1[0].view(T * B, H)
             grad_x = _input_grad(g1, w1).view(T, B, F) if need_x else None
-            grad_w1, grad_b1 = _weight_bias_grads(x2, g1, w1, b1, need_w1,
-                                                  need_b1 and b1 is not None)
+            grad_w1, _ = _weight_bias_grads(x2, g1, w1, None, need_w1, False)
+            grad_b1 = cops.bias_grad(outs1[3].view(B, H), b1) if sum1 else None
         return (grad_x, grad_w1, grad_b1, grad_w2, grad_b2, *tail)

@@ -118,7 +118,7 @@ def scan_forward(x, v0, a0, neuron, decay, threshold, reset, adapt_decay, beta, 
 # ---------------------------------------------------------------------------
 def _scan_backward_eager(x, ckpt_v, ckpt_a, grad_spikes, grad_rates, grad_vT, grad_aT, neuron,
                          decay, threshold, reset, adapt_decay, beta, reset_mode, surrogate,
-                         slope, need_v0, need_a0, reject_spike_grad):
+                         slope, need_v0, need_a0, reject_spike_grad, need_sum=False):
     """Allocates only the requested gradients; the others are None."""
 
     if reject_spike_grad and grad_spikes is not None:
@@ -134,6 +134,7 @@ def _scan_backward_eager(x, ckpt_v, ckpt_a, grad_spikes, grad_rates, grad_vT, gr
     grad_x = torch.empty_like(x)
     grad_v0 = torch.empty((B, N), dtype=x.dtype, device=x.device) if need_v0 else None
     grad_a0 = torch.empty((B, N), dtype=x.dtype, device=x.device) if alif and need_a0 else None
+    grad_sum = torch.empty((B * N,), dtype=torch.float32, device=x.device) if need_sum else None
     nat.scan_backward(
         neuron=neuron, x=x, ckpt_v=ckpt_v, ckpt_a=ckpt_a if alif else None,
         grad_spikes=None if grad_spikes is None else grad_spikes.contiguous(),
@@ -142,9 +143,9 @@ def _scan_backward_eager(x, ckpt_v, ckpt_a, grad_spikes, grad_rates, grad_vT, gr
         grad_aT=None if (grad_aT is None or not alif) else grad_aT.contiguous(),
         grad_x=grad_x, grad_v0=grad_v0, grad_a0=grad_a0, decay=decay, threshold=threshold,
         reset=reset, adapt_decay=adapt_decay, beta=beta, reset_mode=reset_mode,
-        surrogate=surrogate, slope=slope,
+        surrogate=surrogate, slope=slope, grad_sum=grad_sum,
     )
-    return grad_x, grad_v0, grad_a0
+    return grad_x, grad_v0, grad_a0, grad_sum
 
 
 def _scan_backward_impl(
@@ -153,11 +154,13 @@ def _scan_backward_impl(
     grad_vT: torch.Tensor | None, grad_aT: torch.Tensor | None, neuron: int, decay: float,
     threshold: float, reset: float, adapt_decay: float, beta: float, reset_mode: int,
     surrogate: int, slope: float, need_v0: bool, need_a0: bool, reject_spike_grad: bool,
-) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    need_sum: bool = False,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
     outs = _scan_backward_eager(x, ckpt_v, ckpt_a, grad_spikes, grad_rates, grad_vT, grad_aT,
                                 neuron, decay, threshold, reset, adapt_decay, beta, reset_mode,
-                                surrogate, slope, need_v0, need_a0, reject_spike_grad)
-    return tuple(x.new_empty(0) if t is None else t for t in outs)  # type: ignore[return-value]
+                                surrogate, slope, need_v0, need_a0, reject_spike_grad, need_sum)
+    empty = (x.new_empty(0), x.new_empty(0), x.new_empty(0), x.new_empty(0, dtype=torch.float32))
+    return tuple(e if t is None else t for t, e in zip(outs, empty))  # type: ignore[return-value]
 
 
 scan_backward_op = torch.library.custom_op(f"{_NS}::scan_backward", _scan_backward_impl,
@@ -167,29 +170,35 @@ scan_backward_op = torch.library.custom_op(f"{_NS}::scan_backward", _scan_backwa
 @scan_backward_op.register_fake
 def _scan_backward_fake(x, ckpt_v, ckpt_a, grad_spikes, grad_rates, grad_vT, grad_aT, neuron,
                         decay, threshold, reset, adapt_decay, beta, reset_mode, surrogate, slope,
-                        need_v0, need_a0, reject_spike_grad):
+                        need_v0, need_a0, reject_spike_grad, need_sum=False):
     B, N = x.shape[1], x.shape[2]
     alif = neuron == nat.MB_ALIF
     return (torch.empty_like(x), x.new_empty((B, N) if need_v0 else (0,)),
-            x.new_empty((B, N) if alif and need_a0 else (0,)))
+            x.new_empty((B, N) if alif and need_a0 else (0,)),
+            x.new_empty((B * N,) if need_sum else (0,), dtype=torch.float32))
 
 
 def scan_backward(x, ckpt_v, ckpt_a, *, grad_spikes=None, grad_rates=None, grad_vT=None,
                   grad_aT=None, neuron, decay, threshold, reset, adapt_decay, beta, reset_mode,
-                  surrogate, slope, need_v0=True, need_a0=True, reject_spike_grad=False):
+                  surrogate, slope, need_v0=True, need_a0=True, reject_spike_grad=False,
+                  need_sum=False):
     """Reverse-time surrogate backward (``mb_scan_backward``).
 
     Returns ``(grad_x, grad_v0, grad_a0)``; gradients that were not requested
-    are None.
+    are None. With ``need_sum`` a fourth value: the fp32 sum over t of grad_x
+    per neuron, [B*N] (``mb_scan_backward_sum``; formed inside the LIF
+    backward kernel as it stores grad_x).
     """
 
     args = (x, ckpt_v, ckpt_a, grad_spikes, grad_rates, grad_vT, grad_aT, int(neuron),
             float(decay), float(threshold), float(reset), float(adapt_decay), float(beta),
             int(reset_mode), int(surrogate), float(slope), bool(need_v0), bool(need_a0),
-            bool(reject_spike_grad))
+            bool(reject_spike_grad), bool(need_sum))
     if _tracing():
-        return tuple(_none0(t) for t in scan_backward_op(*args))
-    return _scan_backward_eager(*args)
+        outs = tuple(_none0(t) for t in scan_backward_op(*args))
+    else:
+        outs = _scan_backward_eager(*args)
+    return outs if need_sum else outs[:3]
 
 
 # ---------------------------------------------------------------------------
@@ -309,6 +318,29 @@ def linear_weight_grad(x2: torch.Tensor, g2: torch.Tensor, weight_like: torch.Te
     else:
         gw, gb = _linear_weight_grad_impl(x2, g2, weight_like, bias_like)
     return gw, (gb if bias_like is not None else None)
+
+
+def _bias_grad_impl(rows: torch.Tensor, bias_like: torch.Tensor) -> torch.Tensor:
+    from myelin_b200 import projection
+
+    return projection.bias_grad(rows, bias_like.dtype)
+
+
+bias_grad_op = torch.library.custom_op(f"{_NS}::bias_grad", _bias_grad_impl, mutates_args=())
+
+
+@bias_grad_op.register_fake
+def _bias_grad_fake(rows, bias_like):
+    return bias_like.new_empty((rows.shape[1],))
+
+
+def bias_grad(rows: torch.Tensor, bias_like: torch.Tensor) -> torch.Tensor:
+    """Column sums of ``rows`` [R, N] in a fixed order, in the bias's dtype
+    (``mb_column_sums``): the bias gradient from per-neuron sums over t."""
+
+    if _tracing():
+        return bias_grad_op(rows, bias_like)
+    return _bias_grad_impl(rows, bias_like)
 
 
 # ---------------------------------------------------------------------------
@@ -457,5 +489,5 @@ def izhikevich_forward(x: torch.Tensor, v0: torch.Tensor, u0: torch.Tensor,
 
 
 OPS = (scan_forward_op, scan_backward_op, gemm_tn_op, linear_project_op, linear_input_grad_op,
-       linear_weight_grad_op, pack_op, unpack_op, count_rows_op, count_columns_op, pack_count_op,
-       izhikevich_op)
+       linear_weight_grad_op, bias_grad_op, pack_op, unpack_op, count_rows_op, count_columns_op,
+       pack_count_op, izhikevich_op)

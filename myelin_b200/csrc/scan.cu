@@ -611,13 +611,28 @@ extern "C" int mb_scan_forward_packed_scatter(int neuron, int dtype, const void*
   return 0;
 }
 
-extern "C" int mb_scan_backward(int neuron, int dtype, const void* x, const float* ckpt_v,
-                                const float* ckpt_a, const void* grad_spikes,
-                                const void* grad_rates, const void* grad_vT, const void* grad_aT,
-                                void* grad_x, void* grad_v0, void* grad_a0, int64_t T, int64_t B,
-                                int64_t N, float decay, float threshold, float reset,
-                                float adapt_decay, float beta, int reset_mode, int surrogate,
-                                float slope, void* stream) {
+namespace mb {
+namespace {
+
+// Sum over t (last step first) of grad_x[t, i] as stored: the path for the
+// neuron kinds and layouts whose backward kernel does not form it itself.
+template <typename T>
+__global__ void sum_over_t_kernel(const T* __restrict__ grad_x, int64_t steps, int64_t BN,
+                                  float* __restrict__ out) {
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < BN;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    float acc = 0.0f;
+    for (int64_t t = steps - 1; t >= 0; --t) acc += Elem<T>::to_f(grad_x[t * BN + i]);
+    out[i] = acc;
+  }
+}
+
+int scan_backward_impl(int neuron, int dtype, const void* x, const float* ckpt_v,
+                       const float* ckpt_a, const void* grad_spikes, const void* grad_rates,
+                       const void* grad_vT, const void* grad_aT, void* grad_x, void* grad_v0,
+                       void* grad_a0, float* grad_sum, int64_t T, int64_t B, int64_t N,
+                       float decay, float threshold, float reset, float adapt_decay, float beta,
+                       int reset_mode, int surrogate, float slope, void* stream) {
   clear_error();
   if (check_common("mb_scan_backward", neuron, dtype, T, B, N, reset_mode)) return 1;
   MB_CHECK_ARG(surrogate >= MB_SURR_SIGMOID && surrogate <= MB_SURR_NONE,
@@ -627,26 +642,76 @@ extern "C" int mb_scan_backward(int neuron, int dtype, const void* x, const floa
                "mb_scan_backward: x, ckpt_v and grad_x are required");
   MB_CHECK_ARG(neuron == MB_LIF || T == 0 || ckpt_a != nullptr,
                "mb_scan_backward: ALIF requires ckpt_a");
+  MB_CHECK_ARG(aligned_to(grad_sum, 8), "mb_scan_backward: grad_sum must be 8-byte aligned");
+  cudaStream_t s = as_stream(stream);
+  if (T == 0 && grad_sum != nullptr) cudaMemsetAsync(grad_sum, 0, size_t(B * N) * sizeof(float), s);
   ScanBwdArgs a{};
   a.x = x; a.ckpt_v = ckpt_v; a.ckpt_a = ckpt_a;
   a.grad_spikes = grad_spikes; a.grad_rates = grad_rates;
   a.grad_vT = grad_vT; a.grad_aT = grad_aT;
   a.grad_x = grad_x; a.grad_v0 = grad_v0; a.grad_a0 = grad_a0;
+  // the fast LIF backward adds up grad_x as it stores it
+  a.grad_sum = neuron == MB_LIF ? grad_sum : nullptr;
   a.T = T; a.B = B; a.N = N; a.BN = B * N;
   a.decay = decay; a.threshold = threshold; a.reset = reset;
   a.adapt_decay = adapt_decay; a.beta = beta; a.slope = slope;
-  cudaStream_t s = as_stream(stream);
-  if (launch_scan_bwd_fast(dtype, neuron, reset_mode, surrogate, a, s)) {
-    MB_CHECK_LAUNCH("mb_scan_backward");
-    return 0;
+  const bool fast = launch_scan_bwd_fast(dtype, neuron, reset_mode, surrogate, a, s);
+  if (!fast) {
+    switch (dtype) {
+      case MB_F32: dispatch_bwd<float>(neuron, reset_mode, surrogate, a, s); break;
+      case MB_BF16: dispatch_bwd<__nv_bfloat16>(neuron, reset_mode, surrogate, a, s); break;
+      default: dispatch_bwd<__half>(neuron, reset_mode, surrogate, a, s); break;
+    }
   }
-  switch (dtype) {
-    case MB_F32: dispatch_bwd<float>(neuron, reset_mode, surrogate, a, s); break;
-    case MB_BF16: dispatch_bwd<__nv_bfloat16>(neuron, reset_mode, surrogate, a, s); break;
-    default: dispatch_bwd<__half>(neuron, reset_mode, surrogate, a, s); break;
+  if (grad_sum != nullptr && T > 0 && !(fast && a.grad_sum != nullptr)) {
+    const int64_t BN = B * N;
+    const unsigned grid = static_cast<unsigned>(imin64(ceil_div(BN, 256), 148 * 16));
+    switch (dtype) {
+      case MB_F32:
+        sum_over_t_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(grad_x), T, BN, grad_sum);
+        break;
+      case MB_BF16:
+        sum_over_t_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+            static_cast<const __nv_bfloat16*>(grad_x), T, BN, grad_sum);
+        break;
+      default:
+        sum_over_t_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(grad_x), T, BN,
+                                                       grad_sum);
+        break;
+    }
   }
   MB_CHECK_LAUNCH("mb_scan_backward");
   return 0;
+}
+
+}  // namespace
+}  // namespace mb
+
+extern "C" int mb_scan_backward(int neuron, int dtype, const void* x, const float* ckpt_v,
+                                const float* ckpt_a, const void* grad_spikes,
+                                const void* grad_rates, const void* grad_vT, const void* grad_aT,
+                                void* grad_x, void* grad_v0, void* grad_a0, int64_t T, int64_t B,
+                                int64_t N, float decay, float threshold, float reset,
+                                float adapt_decay, float beta, int reset_mode, int surrogate,
+                                float slope, void* stream) {
+  return scan_backward_impl(neuron, dtype, x, ckpt_v, ckpt_a, grad_spikes, grad_rates, grad_vT,
+                            grad_aT, grad_x, grad_v0, grad_a0, nullptr, T, B, N, decay,
+                            threshold, reset, adapt_decay, beta, reset_mode, surrogate, slope,
+                            stream);
+}
+
+extern "C" int mb_scan_backward_sum(int neuron, int dtype, const void* x, const float* ckpt_v,
+                                    const float* ckpt_a, const void* grad_spikes,
+                                    const void* grad_rates, const void* grad_vT,
+                                    const void* grad_aT, void* grad_x, void* grad_v0,
+                                    void* grad_a0, float* grad_sum, int64_t T, int64_t B,
+                                    int64_t N, float decay, float threshold, float reset,
+                                    float adapt_decay, float beta, int reset_mode, int surrogate,
+                                    float slope, void* stream) {
+  return scan_backward_impl(neuron, dtype, x, ckpt_v, ckpt_a, grad_spikes, grad_rates, grad_vT,
+                            grad_aT, grad_x, grad_v0, grad_a0, grad_sum, T, B, N, decay,
+                            threshold, reset, adapt_decay, beta, reset_mode, surrogate, slope,
+                            stream);
 }
 
 namespace mb {

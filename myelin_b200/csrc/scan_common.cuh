@@ -66,6 +66,9 @@ struct ScanBwdArgs {
   void* grad_x;
   void* grad_v0;
   void* grad_a0;
+  // optional: sum over t of grad_x (as stored, in the I/O type), fp32 [B*N],
+  // summed from the last step to the first
+  float* grad_sum;
   int64_t T, B, N, BN;
   int64_t groups_per_row;  // ceil(N / 32)
   float decay, threshold, reset, adapt_decay, beta, slope;

@@ -19,6 +19,7 @@
 #include <climits>
 #include <cstring>
 #include <initializer_list>
+#include <type_traits>
 
 #include "async_copy.cuh"
 #include "common.cuh"
@@ -436,6 +437,12 @@ __global__ void __launch_bounds__(kThreads, MINB) scan_bwd_fast_kernel(
     return gp;
   };
 
+  // Per-neuron sum over t of grad_x (LIF only: the bias gradient of a
+  // stream-synapse layer, db = sum over t and batch rows), from the last
+  // step to the first, of the values as stored.
+  const bool do_sum = KIND == MB_LIF && a.grad_sum != nullptr;
+  F2 gsum = f2(0.0f);
+
   // grad_x overwrites the x values of the stage (x is dead once the chunk is
   // replayed; each thread its own pair) and the finished stage goes out with
   // one bulk tensor store.
@@ -461,7 +468,8 @@ __global__ void __launch_bounds__(kThreads, MINB) scan_bwd_fast_kernel(
         PV[j] = (RESET == MB_RESET_SUBTRACT) ? st.diff : st.p;
         TH[j] = st.nth;
       };
-      auto reverse = [&](int j) {
+      // tag: also add the stored grad_x to the per-neuron sum over t
+      auto reverse = [&](int j, auto tag) {
         F2 g = gr;
         if (MODE == kBwdSpikes) {
           g = f2(P::to_f2(grow[j * (kTileN / 2)]));
@@ -469,22 +477,35 @@ __global__ void __launch_bounds__(kThreads, MINB) scan_bwd_fast_kernel(
           g = add2(g, f2(P::to_f2(grow[j * (kTileN / 2)])));
         }
         const float2 gp = split(adjoint(PV[j], TH[j], g));
-        xrow[j * (kTileN / 2)] = P::from_f2(gp.x, gp.y);
+        const V stored = P::from_f2(gp.x, gp.y);
+        xrow[j * (kTileN / 2)] = stored;
+        if constexpr (decltype(tag)::value) gsum = add2(gsum, f2(P::to_f2(stored)));
+      };
+      auto reverse_chunk = [&](auto tag) {
+        if (len == kChunk) {
+#pragma unroll
+          for (int j = kChunk - 1; j >= 0; --j) reverse(j, tag);
+        } else {
+#pragma unroll
+          for (int j = kChunk - 1; j >= 0; --j) {
+            if (j < len) reverse(j, tag);
+          }
+        }
       };
       if (len == kChunk) {
 #pragma unroll
         for (int j = 0; j < kChunk; ++j) replay(j);
-#pragma unroll
-        for (int j = kChunk - 1; j >= 0; --j) reverse(j);
       } else {
 #pragma unroll
         for (int j = 0; j < kChunk; ++j) {
           if (j < len) replay(j);
         }
-#pragma unroll
-        for (int j = kChunk - 1; j >= 0; --j) {
-          if (j < len) reverse(j);
-        }
+      }
+      if constexpr (KIND == MB_LIF) {
+        if (do_sum) reverse_chunk(std::true_type{});
+        else reverse_chunk(std::false_type{});
+      } else {
+        reverse_chunk(std::false_type{});
       }
     }
     // the warp done last with the chunk writes grad_x (it overwrote x in the
@@ -498,6 +519,7 @@ __global__ void __launch_bounds__(kThreads, MINB) scan_bwd_fast_kernel(
   }
   bulk_wait_all();
   if (!valid) return;
+  if (do_sum) reinterpret_cast<float2*>(a.grad_sum)[e >> 1] = split(gsum);
   if (a.grad_v0) reinterpret_cast<V*>(a.grad_v0)[e >> 1] = P::from_f2(split(gm).x, split(gm).y);
   if (KIND == MB_ALIF && a.grad_a0) {
     reinterpret_cast<V*>(a.grad_a0)[e >> 1] = P::from_f2(split(ga).x, split(ga).y);

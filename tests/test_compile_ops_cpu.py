@@ -20,7 +20,7 @@ from myelin_b200 import _native as nat
 from myelin_b200 import compile_ops as cops
 
 OP_NAMES = ("scan_forward", "scan_backward", "gemm_tn", "linear_project", "linear_input_grad",
-            "linear_weight_grad", "pack_spikes", "unpack_spikes",
+            "linear_weight_grad", "bias_grad", "pack_spikes", "unpack_spikes",
             "count_rows", "count_columns", "pack_count_spikes", "izhikevich_forward")
 
 

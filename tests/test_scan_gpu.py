@@ -373,3 +373,41 @@ def test_north_star_alif_bf16_full_size(oracle):
     ref = oracle.scan_backward(xf, z, z, grad_spikes=gs.float().numpy(), surrogate="atan",
                                slope=10.0, **okw)
     assert_close_scaled(host(xd.grad), ref["grad_x"], rtol=2e-2, what="grad_x")
+
+
+@pytest.mark.parametrize("shape,dtype,neuron", [
+    ((40, 3, 64), torch.float32, nat.MB_LIF),     # fast LIF kernel, fp32 I/O
+    ((33, 4, 96), torch.bfloat16, nat.MB_LIF),    # fast LIF kernel, bf16 I/O, partial chunk
+    ((21, 3, 5), torch.float32, nat.MB_LIF),      # rows not 16-byte aligned: general kernel
+    ((40, 3, 64), torch.bfloat16, nat.MB_ALIF),   # ALIF: summed after the kernel
+])
+def test_backward_sum_over_t_of_stored_gradient(shape, dtype, neuron):
+    """``mb_scan_backward_sum``: per neuron, the fp32 sum over t of grad_x as
+    stored, from the last step to the first: bit for bit against the same
+    additions on the host, with grad_x itself unchanged."""
+
+    from myelin_b200 import compile_ops as cops
+
+    T, B, N = shape
+    g = torch.Generator(device=DEV).manual_seed(T + B + N + neuron)
+    x = (torch.randn(shape, generator=g, device=DEV) * 0.6 + 0.3).to(dtype)
+    gs = torch.randn(shape, generator=g, device=DEV).to(dtype)
+    z = torch.zeros((B, N), dtype=dtype, device=DEV)
+    alif = neuron == nat.MB_ALIF
+    kw = dict(neuron=neuron, decay=0.9, threshold=1.0, reset=0.0,
+              adapt_decay=0.98 if alif else 0.0, beta=1.8 if alif else 0.0,
+              reset_mode=nat.MB_RESET_HARD)
+    fwd = cops.scan_forward(x, z, z if alif else None, kw["neuron"], kw["decay"], kw["threshold"],
+                            kw["reset"], kw["adapt_decay"], kw["beta"], kw["reset_mode"],
+                            dense=True, checkpoints=True)
+    args = dict(grad_spikes=gs, surrogate=1, slope=25.0, need_v0=False,  # fast_sigmoid
+                need_a0=False, **kw)
+    plain = cops.scan_backward(x, fwd[5], fwd[6], **args)
+    gx, _, _, gsum = cops.scan_backward(x, fwd[5], fwd[6], need_sum=True, **args)
+    torch.cuda.synchronize()
+    assert torch.equal(gx, plain[0])
+    want = torch.zeros((B * N,), dtype=torch.float32)
+    host = gx.float().cpu().reshape(T, B * N)
+    for t in range(T - 1, -1, -1):
+        want = want + host[t]
+    assert torch.equal(gsum.cpu(), want)
