@@ -79,3 +79,29 @@ def test_empty_problem_is_a_no_op():
 def test_library_is_a_plain_shared_object():
     handle = ctypes.CDLL(str(nat.LIB_PATH))
     assert handle.mb_version.restype is not None or True
+
+
+def test_gemm_work_plan_sizes():
+    """Host-side K-slice plans of mb_gemm, through the workspace each needs
+    (with no GPU visible the library plans for the B200's 148 SMs, 74 SM pairs).
+
+    - K < 8192 with many tiles: no slicing, no workspace;
+    - config-5 weight gradient (4096 x 4096 outputs, K = T*B = 51200, bf16):
+      256 pair tiles = 3 whole waves of 74 + 34 tail tiles, sliced in 2; the
+      fp32 partials cover only the tail tiles' rows, 3328 .. 4095;
+    - fp32 output from 3-part split operands (config-2 layer-1 weight
+      gradient, 784 x 1024, K = 6400): accuracy slices of at most 2048 of K,
+      4 of them over the whole output;
+    - a 10-wide output with long K: sliced until the units fill the SMs."""
+
+    lib = nat.lib()
+    ws = lib.mb_gemm_workspace_bytes
+    assert ws(51200, 4096, 4096, 1, 1, nat.MB_BF16) == 0
+    tail = 2 * (4096 - 13 * 256) * 4096 * 4
+    assert ws(4096, 4096, 51200, 1, 1, nat.MB_BF16) == tail
+    assert ws(4096, 4096, 8192, 1, 1, nat.MB_BF16) == tail
+    assert ws(4096, 4096, 51200, 1, 1, nat.MB_F32) == tail
+    assert ws(784, 1024, 6400, 3, 3, nat.MB_F32) == 4 * 784 * 1024 * 4
+    narrow = ws(4096, 10, 51200, 1, 1, nat.MB_BF16)
+    assert narrow > 0 and narrow % (4096 * 12 * 4) == 0  # slices x M x pitch(10 -> 12) x fp32
+    assert ws(0, 10, 10, 1, 1, nat.MB_BF16) == 0
